@@ -1,0 +1,171 @@
+// Family E: multi-output fused elementwise loops.
+//
+// Replaces the "element.loop" kernel that lib/Lowering/CUDA.cpp:274-385 emits
+// for a batch of same-shape outputs: every output of the step is computed per
+// linear element index with all intermediates in registers (ScalarEmitter's
+// memo, ScalarEmitter.h:599-604, 825) and each public output gets its own store
+// (lib/Lowering/Host.cpp:862-866).  Differences, all B200-motivated:
+//   * 16-byte vector loads/stores (the reference issues scalar 4-byte
+//     accesses, CUDA.cpp:288-290, 371-373) and U independent units per thread
+//     in flight;
+//   * a persistent grid of (SMs x resident blocks) instead of
+//     min(65535, ceil(count/128)) blocks (CUDA.cpp:256-259);
+//   * the op program is a compile-time constant for the specialised plans, so
+//     the interpreter folds to straight-line code; other programs run the same
+//     interpreter on a runtime program held in the kernel's parameter space.
+#include <cuda_runtime.h>
+
+#include "ask_numerics.cuh"
+#include "kernels.h"
+#include "programs.h"
+#include "vec_io.cuh"
+
+namespace askb {
+
+namespace {
+
+// ---- specialised (compile-time program) path -----------------------------------
+template <class P, int K, int V>
+__device__ __forceinline__ void spec_load(const EwArgs& a, uint64_t base, bool vec, uint64_t (&x)[P::kIn][V]) {
+  if constexpr (K < P::kIn) {
+    load_port<P::in_type(K), P::in_map(K), V>(a.in[K], base, a.count, a.inner, vec, x[K]);
+    spec_load<P, K + 1, V>(a, base, vec, x);
+  }
+}
+
+template <class P, int I, int V>
+__device__ __forceinline__ void spec_exec(uint64_t (&r)[P::kInsn][V], const uint64_t (&x)[P::kIn][V]) {
+  if constexpr (I < P::kInsn) {
+    constexpr Insn ins = P::insn(I);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if constexpr (ins.op == OP_INPUT) r[I][v] = x[ins.a][v];
+      else r[I][v] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][v], r[ins.b][v], r[ins.c][v]);
+    }
+    spec_exec<P, I + 1, V>(r, x);
+  }
+}
+
+template <class P, int K, int V>
+__device__ __forceinline__ void spec_store(const EwArgs& a, uint64_t base, bool vec, const uint64_t (&r)[P::kInsn][V]) {
+  if constexpr (K < P::kOut) {
+    store_port<P::out_type(K), V>(a.out[K], base, a.count, vec, r[P::out_reg(K)]);
+    spec_store<P, K + 1, V>(a, base, vec, r);
+  }
+}
+
+template <class P, int V, int U>
+__global__ void __launch_bounds__(kEwThreads) ew_spec_kernel(const __grid_constant__ EwArgs args, int aligned) {
+  const uint64_t n = args.count;
+  const uint64_t units = (n + V - 1) / V;
+  const uint64_t nthreads = uint64_t(gridDim.x) * kEwThreads;
+  for (uint64_t u = uint64_t(blockIdx.x) * kEwThreads + threadIdx.x; u < units; u += nthreads * U) {
+    uint64_t x[U][P::kIn][V];
+#pragma unroll
+    for (int q = 0; q < U; ++q) {
+      const uint64_t uq = u + q * nthreads;
+      if (uq < units) spec_load<P, 0, V>(args, uq * V, aligned && (uq * V + V <= n), x[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < U; ++q) {
+      const uint64_t uq = u + q * nthreads;
+      if (uq < units) {
+        uint64_t r[P::kInsn][V];
+        spec_exec<P, 0, V>(r, x[q]);
+        spec_store<P, 0, V>(args, uq * V, aligned && (uq * V + V <= n), r);
+      }
+    }
+  }
+}
+
+// ---- runtime-program path -------------------------------------------------------
+template <int V>
+__global__ void __launch_bounds__(kEwThreads)
+    ew_generic_kernel(const __grid_constant__ Program prog, const __grid_constant__ EwArgs args, int aligned) {
+  const uint64_t n = args.count;
+  const uint64_t units = (n + V - 1) / V;
+  const uint64_t nthreads = uint64_t(gridDim.x) * kEwThreads;
+  uint64_t r[kMaxRegs][V];
+  for (uint64_t u = uint64_t(blockIdx.x) * kEwThreads + threadIdx.x; u < units; u += nthreads) {
+    const uint64_t base = u * V;
+    const bool vec = aligned && (base + V <= n);
+    for (int i = 0; i < prog.n_insn; ++i) {
+      const Insn& ins = prog.insn[i];
+      if (ins.op == OP_INPUT) {
+        uint64_t w[V];
+        rt_load<V>(prog.in_type[ins.a], prog.in_map[ins.a], args.in[ins.a], base, n, args.inner, vec, w);
+#pragma unroll
+        for (int v = 0; v < V; ++v) r[ins.dst][v] = w[v];
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          r[ins.dst][v] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][v], r[ins.b][v], r[ins.c][v]);
+      }
+    }
+    for (int k = 0; k < prog.n_out; ++k) {
+      uint64_t w[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) w[v] = r[prog.out_reg[k]][v];
+      rt_store<V>(prog.out_type[k], args.out[k], base, n, vec, w);
+    }
+  }
+}
+
+template <class P>
+struct EwSpecKernels {
+  static constexpr int kV = 4, kU = 2;
+  static void* vec() { return reinterpret_cast<void*>(&ew_spec_kernel<P, kV, kU>); }
+};
+
+void* ew_kernel_ptr(int spec) {
+  switch (spec) {
+    case EW_CFG1: return EwSpecKernels<ProgCfg1>::vec();
+    case EW_CFG5B: return EwSpecKernels<ProgCfg5b>::vec();
+    case EW_SOFTMAX_NORM_F16: return EwSpecKernels<ProgSoftmaxNorm<kF16>>::vec();
+    case EW_SOFTMAX_NORM_BF16: return EwSpecKernels<ProgSoftmaxNorm<kBF16>>::vec();
+    default: return reinterpret_cast<void*>(&ew_generic_kernel<4>);
+  }
+}
+
+}  // namespace
+
+bool ew_spec_program(int spec, Program* out) {
+  switch (spec) {
+    case EW_CFG1: *out = program_of<ProgCfg1>(); return true;
+    case EW_CFG5B: *out = program_of<ProgCfg5b>(); return true;
+    case EW_SOFTMAX_NORM_F16: *out = program_of<ProgSoftmaxNorm<kF16>>(); return true;
+    case EW_SOFTMAX_NORM_BF16: *out = program_of<ProgSoftmaxNorm<kBF16>>(); return true;
+    default: return false;
+  }
+}
+
+int ew_num_specs() { return EW_NUM_SPECS; }
+
+cudaError_t ew_occupancy(int spec, int* blocks_per_sm) {
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, ew_kernel_ptr(spec), kEwThreads, 0);
+}
+
+cudaError_t ew_launch(int spec, const Program& prog, const EwArgs& args, int aligned, int grid, cudaStream_t stream) {
+  if (args.count == 0) return cudaSuccess;
+  const dim3 g(grid), b(kEwThreads);
+  switch (spec) {
+    case EW_CFG1:
+      ew_spec_kernel<ProgCfg1, 4, 2><<<g, b, 0, stream>>>(args, aligned);
+      break;
+    case EW_CFG5B:
+      ew_spec_kernel<ProgCfg5b, 4, 2><<<g, b, 0, stream>>>(args, aligned);
+      break;
+    case EW_SOFTMAX_NORM_F16:
+      ew_spec_kernel<ProgSoftmaxNorm<kF16>, 4, 2><<<g, b, 0, stream>>>(args, aligned);
+      break;
+    case EW_SOFTMAX_NORM_BF16:
+      ew_spec_kernel<ProgSoftmaxNorm<kBF16>, 4, 2><<<g, b, 0, stream>>>(args, aligned);
+      break;
+    default:
+      ew_generic_kernel<4><<<g, b, 0, stream>>>(prog, args, aligned);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace askb

@@ -1,0 +1,103 @@
+// Internal launch interface between the C-ABI plan layer (plan.cpp) and the
+// kernel families.  Nothing here crosses the library boundary.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "ask_types.h"
+
+namespace askb {
+
+// ---- family E: fused elementwise -------------------------------------------
+constexpr int kEwThreads = 256;
+
+enum EwSpec : int {
+  EW_GENERIC = 0,
+  EW_CFG1,
+  EW_CFG5B,
+  EW_SOFTMAX_NORM_F16,
+  EW_SOFTMAX_NORM_BF16,
+  EW_NUM_SPECS
+};
+
+struct EwArgs {
+  const void* in[kMaxIn];
+  void* out[kMaxOut];
+  uint64_t count;
+  uint64_t inner;  // IM_OUTER / IM_INNER divisor
+};
+
+bool ew_spec_program(int spec, Program* out);
+cudaError_t ew_occupancy(int spec, int* blocks_per_sm);
+cudaError_t ew_launch(int spec, const Program& prog, const EwArgs& args, int aligned, int grid, cudaStream_t stream);
+
+// ---- family R/T: map-reduce over [outer, extent, inner] ------------------------
+constexpr int kRedThreads = 256;
+
+enum RedSpec : int {
+  RED_GENERIC = 0,
+  RED_ROWSTATS_F32,      // cfg2: sum, max, min, argmax of f32 rows
+  RED_GLOBAL_F32,        // cfg5a: sum, min, argmin of f32
+  RED_SOFTMAX_MAX_F16,   // cfg3 step 0: max of cast(x, f32)
+  RED_SOFTMAX_MAX_BF16,
+  RED_SOFTMAX_SUM_F16,   // cfg3 step 1: sum of exp(cast(x) - m)
+  RED_SOFTMAX_SUM_BF16,
+  RED_NUM_SPECS
+};
+
+struct RedArgs {
+  const void* in[kMaxIn];
+  void* out[kMaxReductions];
+  uint64_t outer, extent, inner;
+  uint64_t index_base;   // added to arg-reduction indices (global offset of a shard)
+  uint8_t n_red;
+  uint8_t red_op[kMaxReductions];
+  uint8_t red_src[kMaxReductions];   // which program output feeds each reduction
+  uint8_t red_type[kMaxReductions];  // type of the reduced value (program output type)
+};
+
+// One partial accumulator as stored in scratch: value word + arg index.
+struct RedPartial {
+  uint64_t v;
+  int64_t idx;
+};
+
+// Strategy chosen by the plan layer.
+enum RedStrategy : int {
+  RS_WARP_ROW = 0,   // inner == 1: one warp per output row, lanes stride the extent
+  RS_COLUMN = 1,     // inner > 1: one thread per output column, loop over extent
+  RS_SPLIT = 2,      // few outputs, huge extent: CTAs split the extent, partials in scratch
+};
+
+// Program and reduction list (all reductions fold program result 0) of a specialisation.
+bool red_spec_program(int spec, Program* out, int* n_red, uint8_t* ops);
+cudaError_t red_occupancy(int spec, int strategy, int* blocks_per_sm);
+// RS_SPLIT writes grid * n_red partials to `scratch` and then combines them
+// (second kernel) into the outputs, or, when `partials_out` is non-null, into
+// one per-launch record per reduction (sharded plans combine those across ranks).
+cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArgs& args, int aligned, int grid,
+                       void* scratch, RedPartial* partials_out, cudaStream_t stream);
+// Combine `n` records per reduction laid out [n][n_red] into the outputs.
+cudaError_t red_combine_records(const RedArgs& args, const RedPartial* records, int n, cudaStream_t stream);
+size_t red_split_scratch_bytes(int grid, int n_red);
+
+// ---- family G / X: gather and scatter_add over [outer, D, inner] ------------------
+struct IndexArgs {
+  const void* table;     // gather: params; scatter: updates
+  const void* index;
+  void* out;
+  const void* base;      // scatter: base tensor for the fused pre-copy (may equal out)
+  uint64_t outer, dim, inner, n;  // params/base [outer, dim, inner]; index [n]
+  int elem_type, index_type;
+};
+cudaError_t gather_launch(const IndexArgs& a, int aligned, int grid, cudaStream_t stream);
+cudaError_t scatter_add_launch(const IndexArgs& a, int aligned, int grid, cudaStream_t stream);
+
+// ---- input synthesis (Philox4x32-10) -------------------------------------------------
+enum GenKind : int { GEN_UNIFORM_F32 = 0, GEN_NORMAL_F32, GEN_NORMAL_F16, GEN_NORMAL_BF16, GEN_I32, GEN_ZIPF_I64, GEN_ZIPF_I32 };
+cudaError_t gen_launch(int kind, uint64_t seed, uint32_t stream_id, uint64_t offset, uint64_t count, double p0,
+                       double p1, const double* zipf_cdf, uint64_t zipf_n, void* dst, cudaStream_t stream);
+
+}  // namespace askb

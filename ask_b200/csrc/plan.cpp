@@ -1,0 +1,938 @@
+// C-ABI plan layer: recipe parsing and validation, kernel selection, launch.
+//
+// A recipe is the JSON form of one owned ASK execution-plan step.  It plays the
+// role of the step source that ask::lowerToCUDALLVM consumes
+// (lib/Lowering/CUDA.cpp:152-419): ports in the pointer-ABI order (inputs,
+// then outputs, CUDA.cpp:177-208), static sizes, and the step's computation as
+// an SSA op program using ASK's op names (include/ask/IR/ASKOps.h:70-145).
+// Validation follows the reference's rules where they apply:
+//   * at most 64 ports (CUDA.cpp:105-106);
+//   * add/mul need identical operand and result types (CUDA.cpp:139-142);
+//   * float-only ops (div, exp, log, ...), integer/bool-only bitwise ops and
+//     i32/i64-only shifts as stated in docs/en/ir.md:77;
+//   * reduce_any/all take bool, argmax/argmin need a non-empty axis
+//     (lib/IR/ASKOps.cpp:297-334, docs/en/ir.md:69);
+//   * gather/scatter_add index types are i32 or i64 (lib/IR/ASKOps.cpp:460-496).
+#include "../../include/ask_b200.h"
+
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "json.h"
+#include "kernels.h"
+
+using namespace askb;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Failure {
+  int code;
+  std::string message;
+};
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw Failure{code, msg}; }
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(ASK_B200_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <class F>
+int guarded(F&& body) {
+  try {
+    body();
+    g_last_error.clear();
+    return ASK_B200_OK;
+  } catch (const Failure& f) {
+    g_last_error = f.message;
+    return f.code;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return ASK_B200_E_INVALID;
+  } catch (...) {
+    g_last_error = "unknown error";
+    return ASK_B200_E_INVALID;
+  }
+}
+
+// ---- names ----------------------------------------------------------------------
+const char* const kTypeNames[kNumDTypes] = {"bool", "i32", "i64", "f32", "f16", "bf16"};
+
+int parse_dtype(const std::string& s) {
+  for (int t = 0; t < kNumDTypes; ++t)
+    if (s == kTypeNames[t]) return t;
+  if (s == "i1") return kBool;
+  fail(ASK_B200_E_INVALID, "unknown element type '" + s + "'");
+}
+
+struct OpName {
+  const char* name;
+  int op;
+  int arity;
+};
+const OpName kOpNames[] = {
+    {"add", OP_ADD, 2},          {"mul", OP_MUL, 2},          {"div", OP_DIV, 2},
+    {"floordiv", OP_FLOORDIV, 2}, {"mod", OP_MOD, 2},          {"pow", OP_POW, 2},
+    {"maximum", OP_MAXIMUM, 2},  {"minimum", OP_MINIMUM, 2},  {"bitwise_and", OP_AND, 2},
+    {"bitwise_or", OP_OR, 2},    {"bitwise_xor", OP_XOR, 2},  {"shift_left", OP_SHL, 2},
+    {"shift_right", OP_SHR, 2},  {"bitwise_not", OP_NOT, 1},  {"abs", OP_ABS, 1},
+    {"exp", OP_EXP, 1},          {"log", OP_LOG, 1},          {"sqrt", OP_SQRT, 1},
+    {"sin", OP_SIN, 1},          {"cos", OP_COS, 1},          {"tanh", OP_TANH, 1},
+    {"erf", OP_ERF, 1},          {"floor", OP_FLOOR, 1},      {"ceil", OP_CEIL, 1},
+    {"round", OP_ROUND, 1},
+};
+
+std::string strip_prefix(const std::string& s) { return s.rfind("ask.", 0) == 0 ? s.substr(4) : s; }
+
+int parse_map(const std::string& s) {
+  if (s == "full") return IM_FULL;
+  if (s == "scalar") return IM_SCALAR;
+  if (s == "outer") return IM_OUTER;
+  if (s == "inner") return IM_INNER;
+  fail(ASK_B200_E_INVALID, "unknown index map '" + s + "'");
+}
+const char* map_name(int m) {
+  return m == IM_FULL ? "full" : m == IM_SCALAR ? "scalar" : m == IM_OUTER ? "outer" : "inner";
+}
+
+// ---- constants ---------------------------------------------------------------------
+// double -> binary16 / bfloat16 bits with a single round-to-nearest-even step
+// (constants are rounded directly to the target width, docs/en/ir.md:108).
+uint32_t double_to_small_float(double x, int exp_bits, int man_bits) {
+  const uint32_t sign = std::signbit(x) ? (1u << (exp_bits + man_bits)) : 0u;
+  const uint32_t exp_all = (1u << exp_bits) - 1u;
+  if (std::isnan(x)) return sign | (exp_all << man_bits) | (1u << (man_bits - 1));
+  const double a = std::fabs(x);
+  if (std::isinf(a)) return sign | (exp_all << man_bits);
+  if (a == 0.0) return sign;
+  const int bias = (1 << (exp_bits - 1)) - 1;
+  const int emin = 1 - bias;
+  int e2;
+  std::frexp(a, &e2);
+  int e = e2 - 1;  // a in [2^e, 2^(e+1))
+  if (e < emin) {
+    const double q = std::nearbyint(std::ldexp(a, man_bits - emin));  // subnormal quantum 2^(emin-man)
+    return sign | uint32_t(q);  // q == 2^man rolls into the smallest normal
+  }
+  double q = std::nearbyint(std::ldexp(a, man_bits - e));
+  if (q == std::ldexp(1.0, man_bits + 1)) { q /= 2.0; ++e; }
+  if (e > bias) return sign | (exp_all << man_bits);
+  return sign | (uint32_t(e + bias) << man_bits) | (uint32_t(q) - (1u << man_bits));
+}
+
+float bits_to_float(uint32_t b) { float f; std::memcpy(&f, &b, 4); return f; }
+uint32_t float_to_bits(float f) { uint32_t b; std::memcpy(&b, &f, 4); return b; }
+
+// f16 bits -> f32 value (exact).
+float half_bits_to_float(uint32_t h) {
+  const uint32_t s = (h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+  if (e == 0x1f) return bits_to_float(s | 0x7f800000u | (m << 13));
+  if (e == 0) return (s ? -1.0f : 1.0f) * std::ldexp(float(m), -24);
+  return bits_to_float(s | ((e + 112u) << 23) | (m << 13));
+}
+
+uint64_t constant_word(const json::Value& v, int t) {
+  if (t == kBool) {
+    if (v.kind == json::Value::Bool) return v.b ? 1u : 0u;
+    if (v.kind == json::Value::Number) return v.num != 0.0 ? 1u : 0u;
+    fail(ASK_B200_E_INVALID, "bool constant must be true/false");
+  }
+  if (t == kI32 || t == kI64) {
+    const int64_t x = v.as_int("integer constant");
+    if (t == kI32 && (x < INT32_MIN || x > INT32_MAX)) fail(ASK_B200_E_INVALID, "i32 constant out of range");
+    return t == kI32 ? uint64_t(uint32_t(int32_t(x))) : uint64_t(x);
+  }
+  double d;
+  if (v.kind == json::Value::Number) {
+    d = v.num;
+  } else if (v.kind == json::Value::String) {
+    const std::string& s = v.str;
+    if (s.rfind("bits:", 0) == 0) {
+      const uint64_t bits = std::stoull(s.substr(5), nullptr, 0);
+      if (t == kF32) return bits & 0xffffffffu;
+      if (t == kF16) return float_to_bits(half_bits_to_float(uint32_t(bits & 0xffffu)));
+      return uint64_t(uint32_t(bits & 0xffffu) << 16);
+    }
+    if (s == "nan") d = std::nan("");
+    else if (s == "inf") d = INFINITY;
+    else if (s == "-inf") d = -INFINITY;
+    else d = std::stod(s);
+  } else {
+    fail(ASK_B200_E_INVALID, "float constant must be a number or string");
+  }
+  if (t == kF32) return float_to_bits(float(d));
+  if (t == kF16) return float_to_bits(half_bits_to_float(double_to_small_float(d, 5, 10)));
+  return uint64_t(double_to_small_float(d, 8, 7) << 16);
+}
+
+// ---- programs ------------------------------------------------------------------------
+struct Ports {
+  std::vector<int> type, map;
+};
+
+// Parse an SSA program.  Result: canonical SSA Program (dst == index), and the
+// type of every value.
+Program parse_program(const json::Value& prog_json, const json::Value& results_json, const Ports& in,
+                      bool allow_inner_map) {
+  const auto& insns = prog_json.as_array("program");
+  if (insns.empty() || insns.size() > size_t(kMaxInsn))
+    fail(ASK_B200_E_UNSUPPORTED, "program must have 1.." + std::to_string(kMaxInsn) + " instructions");
+  if (in.type.size() > size_t(kMaxIn)) fail(ASK_B200_E_UNSUPPORTED, "too many inputs for one fused step");
+  Program p{};
+  p.n_in = uint8_t(in.type.size());
+  for (size_t k = 0; k < in.type.size(); ++k) {
+    p.in_type[k] = uint8_t(in.type[k]);
+    if (in.map[k] == IM_INNER && !allow_inner_map) fail(ASK_B200_E_INVALID, "index map 'inner' is not valid here");
+    p.in_map[k] = uint8_t(in.map[k]);
+  }
+  std::vector<int> vt;
+  auto operand = [&](const json::Value& v, size_t i) -> uint8_t {
+    const int64_t a = v.as_int("operand");
+    if (a < 0 || size_t(a) >= i) fail(ASK_B200_E_INVALID, "operand must name an earlier instruction");
+    return uint8_t(a);
+  };
+  auto need = [&](bool ok, const std::string& what) {
+    if (!ok) fail(ASK_B200_E_INVALID, what);
+  };
+  for (size_t i = 0; i < insns.size(); ++i) {
+    const auto& ins = insns[i].as_array("instruction");
+    need(!ins.empty(), "empty instruction");
+    const std::string name = strip_prefix(ins[0].as_str("opcode"));
+    Insn x{};
+    x.dst = uint8_t(i);
+    int type = -1;
+    if (name == "input") {
+      need(ins.size() == 2, "input takes a port index");
+      const int64_t k = ins[1].as_int("input port");
+      need(k >= 0 && size_t(k) < in.type.size(), "input port out of range");
+      x.op = OP_INPUT; x.a = uint8_t(k); type = in.type[size_t(k)];
+    } else if (name == "const" || name == "constant") {
+      need(ins.size() == 3, "const takes a type and a value");
+      type = parse_dtype(ins[1].as_str("const type"));
+      x.op = OP_CONST; x.imm = constant_word(ins[2], type); x.src_type = uint8_t(type);
+    } else if (name == "cast") {
+      need(ins.size() == 3, "cast takes an operand and a type");
+      x.op = OP_CAST; x.a = operand(ins[1], i); type = parse_dtype(ins[2].as_str("cast type"));
+      x.src_type = uint8_t(vt[x.a]);
+    } else if (name == "compare") {
+      need(ins.size() == 4, "compare takes a predicate and two operands");
+      const std::string pred = ins[1].as_str("predicate");
+      const char* preds[] = {"eq", "ne", "lt", "le", "gt", "ge"};
+      int pi = -1;
+      for (int q = 0; q < 6; ++q) if (pred == preds[q]) pi = q;
+      need(pi >= 0, "unknown compare predicate '" + pred + "'");
+      x.op = OP_CMP; x.aux = uint8_t(pi); x.a = operand(ins[2], i); x.b = operand(ins[3], i);
+      need(vt[x.a] == vt[x.b], "compare operands must have identical types");
+      x.src_type = uint8_t(vt[x.a]); type = kBool;
+    } else if (name == "select") {
+      need(ins.size() == 4, "select takes a condition and two operands");
+      x.op = OP_SELECT; x.a = operand(ins[1], i); x.b = operand(ins[2], i); x.c = operand(ins[3], i);
+      need(vt[x.a] == kBool, "select condition must be bool");
+      need(vt[x.b] == vt[x.c], "select branches must have identical types");
+      x.src_type = kBool; type = vt[x.b];
+    } else {
+      const OpName* found = nullptr;
+      for (const auto& o : kOpNames) if (name == o.name) found = &o;
+      if (!found) fail(ASK_B200_E_UNSUPPORTED, "op '" + name + "' is not an elementwise op of this library");
+      need(int(ins.size()) == found->arity + 1, "op '" + name + "' takes " + std::to_string(found->arity) + " operand(s)");
+      x.op = uint8_t(found->op);
+      x.a = operand(ins[1], i);
+      if (found->arity == 2) {
+        x.b = operand(ins[2], i);
+        need(vt[x.a] == vt[x.b], "operands of '" + name + "' must have identical types");
+      }
+      type = vt[x.a];
+      x.src_type = uint8_t(type);
+      const bool fl = dtype_is_float(type), in_ = dtype_is_int(type), bo = type == kBool;
+      switch (found->op) {
+        case OP_ADD: case OP_MUL: case OP_FLOORDIV: case OP_MOD: case OP_POW: case OP_ABS:
+          need(fl || in_, "'" + name + "' needs a numeric type"); break;
+        case OP_DIV: case OP_EXP: case OP_LOG: case OP_SQRT: case OP_SIN: case OP_COS: case OP_TANH:
+        case OP_ERF: case OP_FLOOR: case OP_CEIL: case OP_ROUND:
+          need(fl, "'" + name + "' needs f32, f16 or bf16"); break;
+        case OP_AND: case OP_OR: case OP_XOR: case OP_NOT:
+          need(in_ || bo, "'" + name + "' needs bool, i32 or i64"); break;
+        case OP_SHL: case OP_SHR:
+          need(in_, "'" + name + "' needs i32 or i64"); break;
+        default: break;  // maximum/minimum accept all six types
+      }
+    }
+    x.type = uint8_t(type);
+    p.insn[i] = x;
+    vt.push_back(type);
+  }
+  p.n_insn = uint8_t(insns.size());
+  p.n_regs = p.n_insn;
+  const auto& res = results_json.as_array("results");
+  if (res.empty() || res.size() > size_t(kMaxOut)) fail(ASK_B200_E_UNSUPPORTED, "1.." + std::to_string(kMaxOut) + " results");
+  p.n_out = uint8_t(res.size());
+  for (size_t k = 0; k < res.size(); ++k) {
+    const int64_t r = res[k].as_int("result");
+    if (r < 0 || size_t(r) >= insns.size()) fail(ASK_B200_E_INVALID, "result names no instruction");
+    p.out_reg[k] = uint8_t(r);
+    p.out_type[k] = uint8_t(vt[size_t(r)]);
+  }
+  return p;
+}
+
+bool same_program(const Program& a, const Program& b) {
+  if (a.n_insn != b.n_insn || a.n_in != b.n_in || a.n_out != b.n_out) return false;
+  for (int k = 0; k < a.n_in; ++k)
+    if (a.in_type[k] != b.in_type[k] || a.in_map[k] != b.in_map[k]) return false;
+  for (int k = 0; k < a.n_out; ++k)
+    if (a.out_type[k] != b.out_type[k] || a.out_reg[k] != b.out_reg[k]) return false;
+  for (int i = 0; i < a.n_insn; ++i) {
+    const Insn &x = a.insn[i], &y = b.insn[i];
+    if (x.op != y.op || x.type != y.type || x.dst != y.dst || x.a != y.a || x.b != y.b || x.c != y.c ||
+        x.aux != y.aux || x.src_type != y.src_type || x.imm != y.imm)
+      return false;
+  }
+  return true;
+}
+
+// Linear-scan register assignment for the runtime interpreter: a value's
+// register is freed after its last use (results live to the end).
+int operand_count(int op) {
+  if (op == OP_INPUT || op == OP_CONST) return 0;
+  if (op == OP_SELECT) return 3;
+  if (op == OP_CMP || (op >= OP_ADD && op <= OP_SHR)) return 2;
+  return 1;  // cast and the unary ops
+}
+
+void assign_registers(Program& p) {
+  const int n = p.n_insn;
+  std::vector<int> last(n, -1);
+  auto use = [&](int v, int at) { if (at > last[v]) last[v] = at; };
+  for (int i = 0; i < n; ++i) {
+    const Insn& x = p.insn[i];
+    const int k = operand_count(x.op);
+    if (k >= 1) use(x.a, i);
+    if (k >= 2) use(x.b, i);
+    if (k >= 3) use(x.c, i);
+  }
+  for (int k = 0; k < p.n_out; ++k) last[p.out_reg[k]] = n;
+  std::vector<int> reg(n, -1);
+  std::vector<int> free_list;
+  int next = 0;
+  for (int i = 0; i < n; ++i) {
+    Insn& x = p.insn[i];
+    const int a = x.a, b = x.b, c = x.c;
+    // operands are read before the destination is written, so registers whose
+    // last use is this instruction may be reused for its result
+    for (int v = 0; v < i; ++v)
+      if (last[v] == i && reg[v] >= 0) { free_list.push_back(reg[v]); last[v] = -2; }
+    int r;
+    if (!free_list.empty()) { r = free_list.back(); free_list.pop_back(); }
+    else r = next++;
+    reg[i] = r;
+    x.dst = uint8_t(r);
+    if (x.op != OP_INPUT && x.op != OP_CONST) {
+      x.a = uint8_t(reg[a] < 0 ? 0 : reg[a]);
+      x.b = uint8_t(reg[b] < 0 ? 0 : reg[b]);
+      x.c = uint8_t(reg[c] < 0 ? 0 : reg[c]);
+    }
+    if (last[i] == -1) { free_list.push_back(r); last[i] = -2; }  // dead value
+  }
+  for (int k = 0; k < p.n_out; ++k) p.out_reg[k] = uint8_t(reg[p.out_reg[k]]);
+  p.n_regs = uint8_t(next);
+}
+
+// ---- plan -------------------------------------------------------------------------
+enum Family { FAM_ELEMENTWISE = 0, FAM_REDUCE, FAM_GATHER, FAM_SCATTER };
+const char* const kFamilyNames[] = {"elementwise", "reduce", "gather", "scatter_add"};
+
+struct PortInfo {
+  int dtype;
+  uint64_t elements;
+  int map;
+};
+
+uint64_t checked_count(const json::Value& v, const char* what) {
+  const int64_t x = v.as_int(what);
+  if (x < 0) fail(ASK_B200_E_INVALID, std::string(what) + " must be non-negative");
+  return uint64_t(x);
+}
+
+uint64_t mul_checked(uint64_t a, uint64_t b) {
+  if (a && b > UINT64_MAX / a) fail(ASK_B200_E_INVALID, "element count overflows");
+  return a * b;
+}
+
+}  // namespace
+
+struct ask_b200_plan {
+  int family = FAM_ELEMENTWISE;
+  int device = -1;
+  int num_sms = 148;
+  std::vector<PortInfo> inputs, outputs;
+  Program prog{};
+  int spec = 0;
+  int strategy = 0;
+  int grid = 1;
+  int launches = 1;
+  size_t scratch = 0;
+  size_t record_offset = 0;  // sharded reduce: where the per-rank records live in scratch
+  uint64_t count = 0, inner = 1;
+  RedArgs red{};
+  IndexArgs idx{};
+  bool shardable = false;
+  std::string kernel;
+};
+
+struct ask_b200_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 1, rank = 0, device = 0;
+};
+
+namespace {
+
+constexpr int kMaxRanks = 64;
+
+int blocks_per_sm_default(int) { return 8; }
+
+void finish_elementwise(ask_b200_plan& pl) {
+  // Specialisation lookup on the canonical SSA form.
+  pl.spec = EW_GENERIC;
+  for (int s = 1; s < EW_NUM_SPECS; ++s) {
+    Program sp{};
+    if (ew_spec_program(s, &sp) && same_program(sp, pl.prog)) { pl.spec = s; break; }
+  }
+  if (pl.spec == EW_GENERIC) assign_registers(pl.prog);
+  const char* names[] = {"ew_generic", "ew_cfg1", "ew_cfg5b", "ew_softmax_norm_f16", "ew_softmax_norm_bf16"};
+  pl.kernel = names[pl.spec];
+  int occ = blocks_per_sm_default(0);
+  if (pl.device >= 0) check_cuda(ew_occupancy(pl.spec, &occ), "occupancy");
+  const uint64_t units = (pl.count + 3) / 4;
+  const uint64_t needed = (units + kEwThreads - 1) / kEwThreads;
+  const uint64_t cap = uint64_t(std::max(occ, 1)) * uint64_t(pl.num_sms);
+  pl.grid = int(std::max<uint64_t>(1, std::min(needed, cap)));
+  pl.launches = pl.count ? 1 : 0;
+}
+
+void parse_ports(const json::Value& r, const char* key, bool with_map, std::vector<int>& types, std::vector<int>& maps) {
+  const auto& arr = r.at(key).as_array(key);
+  for (const auto& p : arr) {
+    types.push_back(parse_dtype(p.at("dtype").as_str("dtype")));
+    const json::Value* m = p.get("map");
+    maps.push_back(with_map && m ? parse_map(m->as_str("map")) : IM_FULL);
+  }
+}
+
+void build_elementwise(ask_b200_plan& pl, const json::Value& r) {
+  pl.count = checked_count(r.at("count"), "count");
+  const json::Value* in = r.get("inner");
+  pl.inner = in ? checked_count(*in, "inner") : 1;
+  Ports ports;
+  parse_ports(r, "inputs", true, ports.type, ports.map);
+  pl.prog = parse_program(r.at("program"), r.at("results"), ports, true);
+  bool uses_div = false;
+  for (size_t k = 0; k < ports.type.size(); ++k) {
+    uint64_t elems = pl.count;
+    if (ports.map[k] == IM_SCALAR) elems = 1;
+    if (ports.map[k] == IM_OUTER || ports.map[k] == IM_INNER) uses_div = true;
+    if (ports.map[k] == IM_OUTER) elems = pl.inner ? pl.count / pl.inner : 0;
+    if (ports.map[k] == IM_INNER) elems = pl.inner;
+    pl.inputs.push_back({ports.type[k], elems, ports.map[k]});
+  }
+  if (uses_div && (pl.inner == 0 || pl.count % pl.inner != 0))
+    fail(ASK_B200_E_INVALID, "inner must divide count when an outer/inner index map is used");
+  std::vector<int> otypes, omaps;
+  parse_ports(r, "outputs", false, otypes, omaps);
+  if (otypes.size() != pl.prog.n_out) fail(ASK_B200_E_INVALID, "outputs and results differ in length");
+  for (size_t k = 0; k < otypes.size(); ++k) {
+    if (otypes[k] != pl.prog.out_type[k])
+      fail(ASK_B200_E_INVALID, "output " + std::to_string(k) + " type does not match its result");
+    pl.outputs.push_back({otypes[k], pl.count, IM_FULL});
+  }
+  finish_elementwise(pl);
+}
+
+int parse_red_op(const std::string& s) {
+  const std::string n = strip_prefix(s);
+  const char* names[] = {"sum", "prod", "max", "min", "any", "all", "argmax", "argmin"};
+  for (int k = 0; k < kNumRedOps; ++k)
+    if (n == names[k] || n == std::string("reduce_") + names[k]) return k;
+  fail(ASK_B200_E_UNSUPPORTED, "unknown reduction '" + s + "'");
+}
+
+void build_reduce(ask_b200_plan& pl, const json::Value& r) {
+  const uint64_t outer = checked_count(r.at("outer"), "outer");
+  const uint64_t extent = checked_count(r.at("extent"), "extent");
+  const json::Value* in = r.get("inner");
+  const uint64_t inner = in ? checked_count(*in, "inner") : 1;
+  const json::Value* ib = r.get("index_base");
+  const uint64_t index_base = ib ? checked_count(*ib, "index_base") : 0;
+  Ports ports;
+  parse_ports(r, "inputs", true, ports.type, ports.map);
+  pl.prog = parse_program(r.at("program"), r.at("results"), ports, false);
+  const auto& reds = r.at("reductions").as_array("reductions");
+  if (reds.empty() || reds.size() > size_t(kMaxReductions))
+    fail(ASK_B200_E_UNSUPPORTED, "1.." + std::to_string(kMaxReductions) + " reductions per step");
+  RedArgs& a = pl.red;
+  a = RedArgs{};
+  a.outer = outer; a.extent = extent; a.inner = inner; a.index_base = index_base;
+  a.n_red = uint8_t(reds.size());
+  const uint64_t n_outputs = mul_checked(outer, inner);
+  const uint64_t n_elems = mul_checked(n_outputs, extent);
+  for (size_t k = 0; k < ports.type.size(); ++k) {
+    const uint64_t elems = ports.map[k] == IM_FULL ? n_elems : ports.map[k] == IM_SCALAR ? 1 : n_outputs;
+    pl.inputs.push_back({ports.type[k], elems, ports.map[k]});
+  }
+  for (size_t k = 0; k < reds.size(); ++k) {
+    const int op = parse_red_op(reds[k].at("op").as_str("op"));
+    const int64_t src = reds[k].get("value") ? reds[k].at("value").as_int("value") : 0;
+    if (src < 0 || src >= pl.prog.n_out) fail(ASK_B200_E_INVALID, "reduction value names no result");
+    const int t = pl.prog.out_type[src];
+    if ((op == RED_ANY || op == RED_ALL) && t != kBool) fail(ASK_B200_E_INVALID, "reduce_any/all need bool");
+    if ((op == RED_SUM || op == RED_PROD) && t == kBool) fail(ASK_B200_E_INVALID, "reduce_sum/prod need a numeric type");
+    if (red_is_arg(op) && extent == 0) fail(ASK_B200_E_INVALID, "argmax/argmin need a non-empty axis");
+    if ((op == RED_MAX || op == RED_MIN) && extent == 0 && n_outputs)
+      fail(ASK_B200_E_INVALID, "reduce_max/min need a non-empty domain");
+    a.red_op[k] = uint8_t(op);
+    a.red_src[k] = uint8_t(src);
+    a.red_type[k] = uint8_t(t);
+    const int ot = red_is_arg(op) ? kI64 : (op == RED_ANY || op == RED_ALL) ? kBool : t;
+    pl.outputs.push_back({ot, n_outputs, IM_FULL});
+  }
+  if (const json::Value* outs = r.get("outputs")) {
+    const auto& arr = outs->as_array("outputs");
+    if (arr.size() != reds.size()) fail(ASK_B200_E_INVALID, "one output per reduction");
+    for (size_t k = 0; k < arr.size(); ++k)
+      if (parse_dtype(arr[k].at("dtype").as_str("dtype")) != pl.outputs[k].dtype)
+        fail(ASK_B200_E_INVALID, "output " + std::to_string(k) + " type does not match its reduction");
+  }
+  // Strategy.
+  std::string forced = r.get("strategy") ? r.at("strategy").as_str("strategy") : "";
+  if (inner != 1) pl.strategy = RS_COLUMN;
+  else if (forced == "split" || (forced.empty() && outer < uint64_t(pl.num_sms) * 4 && extent >= 32768)) pl.strategy = RS_SPLIT;
+  else pl.strategy = RS_WARP_ROW;
+  if (forced == "warp_row" && inner == 1) pl.strategy = RS_WARP_ROW;
+  // Specialisation.
+  pl.spec = RED_GENERIC;
+  if (pl.strategy != RS_COLUMN)
+    for (int s = 1; s < RED_NUM_SPECS; ++s) {
+      Program sp{};
+      int nr = 0;
+      uint8_t ops[kMaxReductions] = {};
+      if (!red_spec_program(s, &sp, &nr, ops) || !same_program(sp, pl.prog) || nr != a.n_red) continue;
+      bool same = true;
+      for (int k = 0; k < nr; ++k) same = same && ops[k] == a.red_op[k] && a.red_src[k] == 0;
+      if (same) { pl.spec = s; break; }
+    }
+  if (pl.spec == RED_GENERIC) assign_registers(pl.prog);
+  const char* spec_names[] = {"generic", "rowstats_f32", "global_f32", "softmax_max_f16", "softmax_max_bf16",
+                              "softmax_sum_f16", "softmax_sum_bf16"};
+  const char* strat_names[] = {"warp_row", "column", "split"};
+  pl.kernel = std::string("reduce_") + strat_names[pl.strategy] + "_" + spec_names[pl.spec];
+  int occ = blocks_per_sm_default(0);
+  if (pl.device >= 0) check_cuda(red_occupancy(pl.spec, pl.strategy, &occ), "occupancy");
+  const uint64_t cap = uint64_t(std::max(occ, 1)) * uint64_t(pl.num_sms);
+  uint64_t needed;
+  if (pl.strategy == RS_WARP_ROW) needed = (outer + (kRedThreads / 32) - 1) / (kRedThreads / 32);
+  else if (pl.strategy == RS_COLUMN) needed = (n_outputs + kRedThreads - 1) / kRedThreads;
+  else needed = std::max<uint64_t>(1, extent / 8192);
+  pl.grid = int(std::max<uint64_t>(1, std::min(needed, cap)));
+  pl.launches = n_outputs ? (pl.strategy == RS_SPLIT ? 2 : 1) : 0;
+  pl.scratch = 0;
+  if (pl.strategy == RS_SPLIT) {
+    const size_t part = red_split_scratch_bytes(pl.grid, a.n_red) * size_t(outer);
+    pl.record_offset = (part + 255) & ~size_t(255);
+    pl.shardable = outer == 1;
+    // Sharded launches also keep this rank's record and the gathered records.
+    pl.scratch = pl.shardable ? pl.record_offset + size_t(1 + kMaxRanks) * a.n_red * sizeof(RedPartial) : part;
+  }
+}
+
+void build_index(ask_b200_plan& pl, const json::Value& r, bool scatter) {
+  IndexArgs& a = pl.idx;
+  a = IndexArgs{};
+  a.outer = r.get("outer") ? checked_count(r.at("outer"), "outer") : 1;
+  a.dim = checked_count(r.at("dim"), "dim");
+  a.inner = r.get("inner") ? checked_count(r.at("inner"), "inner") : 1;
+  a.n = checked_count(r.at("n"), "n");
+  a.elem_type = parse_dtype(r.at("dtype").as_str("dtype"));
+  a.index_type = parse_dtype(r.at("index_dtype").as_str("index_dtype"));
+  if (a.index_type != kI32 && a.index_type != kI64) fail(ASK_B200_E_INVALID, "indices must be i32 or i64");
+  const uint64_t table = mul_checked(mul_checked(a.outer, a.dim), a.inner);
+  const uint64_t rows = mul_checked(mul_checked(a.outer, a.n), a.inner);
+  if (!scatter) {
+    pl.inputs = {{a.elem_type, table, IM_FULL}, {a.index_type, a.n, IM_FULL}};
+    pl.outputs = {{a.elem_type, rows, IM_FULL}};
+    pl.kernel = "gather_rows";
+    pl.launches = rows ? 1 : 0;
+  } else {
+    if (a.elem_type == kBool) fail(ASK_B200_E_INVALID, "scatter_add needs a numeric type");
+    pl.inputs = {{a.elem_type, table, IM_FULL}, {a.index_type, a.n, IM_FULL}, {a.elem_type, rows, IM_FULL}};
+    pl.outputs = {{a.elem_type, table, IM_FULL}};
+    pl.kernel = a.elem_type == kF32 ? "scatter_add_rows_f32v" : "scatter_add_elems";
+    if (const json::Value* pc = r.get("pre_copy")) {
+      if (pc->at("input").as_int("pre_copy.input") != 0 || pc->at("output").as_int("pre_copy.output") != 0)
+        fail(ASK_B200_E_INVALID, "pre_copy must copy input 0 (base) to output 0");
+    }
+    pl.launches = (table ? 1 : 0) + (rows && a.dim ? 1 : 0);
+  }
+  pl.grid = pl.num_sms * 8;
+}
+
+std::string describe(const ask_b200_plan& pl) {
+  std::ostringstream o;
+  o << "{\"format\":\"ask-b200-recipe\",\"abi_version\":" << ASK_B200_ABI_VERSION << ",\"family\":\""
+    << kFamilyNames[pl.family] << "\",\"kernel\":\"" << pl.kernel << "\",\"device\":" << pl.device
+    << ",\"target\":{\"backend\":\"cuda\",\"arch\":100},\"launch\":{\"grid\":[" << pl.grid << ",1,1],\"block\":["
+    << (pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? kRedThreads : 256)
+    << ",1,1],\"shared_bytes\":0},\"kernels_per_launch\":" << pl.launches << ",\"scratch_bytes\":" << pl.scratch;
+  if (pl.family == FAM_REDUCE) {
+    const char* strat[] = {"warp_row", "column", "split"};
+    o << ",\"strategy\":\"" << strat[pl.strategy] << "\",\"shardable\":" << (pl.shardable ? "true" : "false");
+  }
+  if (pl.family == FAM_ELEMENTWISE || pl.family == FAM_REDUCE)
+    o << ",\"specialized\":" << (pl.spec ? "true" : "false") << ",\"registers\":" << int(pl.prog.n_regs);
+  if (pl.family == FAM_SCATTER) o << ",\"pre_copy\":{\"input\":0,\"output\":0}";
+  o << ",\"port_map\":[";
+  size_t arg = 0;
+  auto port = [&](const PortInfo& p, const char* kind, size_t k) {
+    if (arg) o << ",";
+    o << "{\"argument\":" << arg++ << ",\"logical_port\":\"" << kind << ":" << k << "\",\"element_type\":\""
+      << kTypeNames[p.dtype] << "\",\"elements\":" << p.elements << ",\"storage_bytes\":" << dtype_bytes(p.dtype)
+      << ",\"map\":\"" << map_name(p.map) << "\",\"layout\":\"contiguous_row_major\"}";
+  };
+  for (size_t k = 0; k < pl.inputs.size(); ++k) port(pl.inputs[k], "input", k);
+  for (size_t k = 0; k < pl.outputs.size(); ++k) port(pl.outputs[k], "output", k);
+  o << "],\"requires_disjoint_outputs\":true,\"outputs_must_not_alias_inputs\":"
+    << (pl.family == FAM_SCATTER ? "false" : "true") << "}";
+  return o.str();
+}
+
+bool aligned16(uint64_t p) { return (p & 15u) == 0; }
+
+void check_device(const ask_b200_plan& pl) {
+  if (pl.device < 0) fail(ASK_B200_E_DEVICE, "plan was created host-only (device -1) and cannot launch");
+  int cur = -1;
+  check_cuda(cudaGetDevice(&cur), "cudaGetDevice");
+  if (cur != pl.device)
+    fail(ASK_B200_E_DEVICE, "current device " + std::to_string(cur) + " is not the plan's device " + std::to_string(pl.device));
+}
+
+void check_ports(const ask_b200_plan& pl, const uint64_t* ports, size_t n_ports) {
+  const size_t want = pl.inputs.size() + pl.outputs.size();
+  if (n_ports != want) fail(ASK_B200_E_INVALID, "expected " + std::to_string(want) + " ports, got " + std::to_string(n_ports));
+  if (!ports && want) fail(ASK_B200_E_INVALID, "ports is NULL");
+  for (size_t k = 0; k < want; ++k) {
+    const PortInfo& p = k < pl.inputs.size() ? pl.inputs[k] : pl.outputs[k - pl.inputs.size()];
+    if (p.elements && !ports[k]) fail(ASK_B200_E_INVALID, "port " + std::to_string(k) + " is NULL");
+    if (ports[k] % uint64_t(dtype_bytes(p.dtype)))
+      fail(ASK_B200_E_INVALID, "port " + std::to_string(k) + " is not aligned to its element size");
+  }
+}
+
+// Launch body shared by plain and sharded launches.  `rec_out` (sharded only)
+// receives this rank's per-output records instead of the outputs.
+void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratch, cudaStream_t st, RedPartial* rec_out) {
+  const size_t ni = pl.inputs.size();
+  switch (pl.family) {
+    case FAM_ELEMENTWISE: {
+      EwArgs a{};
+      bool aligned = true;
+      for (size_t k = 0; k < ni; ++k) {
+        a.in[k] = reinterpret_cast<const void*>(ports[k]);
+        if (pl.inputs[k].map == IM_FULL || pl.inputs[k].map == IM_INNER) aligned &= aligned16(ports[k]);
+      }
+      for (size_t k = 0; k < pl.outputs.size(); ++k) {
+        a.out[k] = reinterpret_cast<void*>(ports[ni + k]);
+        aligned &= aligned16(ports[ni + k]);
+      }
+      a.count = pl.count;
+      a.inner = pl.inner ? pl.inner : 1;
+      check_cuda(ew_launch(pl.spec, pl.prog, a, aligned ? 1 : 0, pl.grid, st), "elementwise launch");
+      break;
+    }
+    case FAM_REDUCE: {
+      RedArgs a = pl.red;
+      bool aligned = true;
+      for (size_t k = 0; k < ni; ++k) {
+        a.in[k] = reinterpret_cast<const void*>(ports[k]);
+        if (pl.inputs[k].map == IM_FULL) {
+          aligned &= aligned16(ports[k]);
+          aligned &= (a.extent * uint64_t(dtype_bytes(pl.inputs[k].dtype))) % 16 == 0;
+        }
+      }
+      for (size_t k = 0; k < pl.outputs.size(); ++k) a.out[k] = reinterpret_cast<void*>(ports[ni + k]);
+      if (pl.strategy == RS_SPLIT && !scratch) fail(ASK_B200_E_INVALID, "this plan needs scratch memory");
+      if (scratch && !aligned16(scratch)) fail(ASK_B200_E_INVALID, "scratch must be 16-byte aligned");
+      check_cuda(red_launch(pl.spec, pl.strategy, pl.prog, a, aligned ? 1 : 0, pl.grid,
+                            reinterpret_cast<void*>(scratch), rec_out, st),
+                 "reduce launch");
+      break;
+    }
+    case FAM_GATHER: {
+      IndexArgs a = pl.idx;
+      a.table = reinterpret_cast<const void*>(ports[0]);
+      a.index = reinterpret_cast<const void*>(ports[1]);
+      a.out = reinterpret_cast<void*>(ports[2]);
+      check_cuda(gather_launch(a, 1, pl.grid, st), "gather launch");
+      break;
+    }
+    case FAM_SCATTER: {
+      IndexArgs a = pl.idx;
+      a.base = reinterpret_cast<const void*>(ports[0]);
+      a.index = reinterpret_cast<const void*>(ports[1]);
+      a.table = reinterpret_cast<const void*>(ports[2]);
+      a.out = reinterpret_cast<void*>(ports[3]);
+      check_cuda(scatter_add_launch(a, 1, pl.grid, st), "scatter_add launch");
+      break;
+    }
+    default:
+      fail(ASK_B200_E_INVALID, "corrupt plan");
+  }
+}
+
+// ---- NCCL, loaded at run time ---------------------------------------------------------
+struct Nccl {
+  void* lib = nullptr;
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*getErrorString)(ncclResult_t) = nullptr;
+};
+
+Nccl& nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW);
+    if (!h) return;
+    n.lib = h;
+    n.getUniqueId = reinterpret_cast<decltype(n.getUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+    n.commInitRank = reinterpret_cast<decltype(n.commInitRank)>(dlsym(h, "ncclCommInitRank"));
+    n.commDestroy = reinterpret_cast<decltype(n.commDestroy)>(dlsym(h, "ncclCommDestroy"));
+    n.allGather = reinterpret_cast<decltype(n.allGather)>(dlsym(h, "ncclAllGather"));
+    n.getErrorString = reinterpret_cast<decltype(n.getErrorString)>(dlsym(h, "ncclGetErrorString"));
+  });
+  if (!n.lib || !n.getUniqueId || !n.commInitRank || !n.commDestroy || !n.allGather)
+    fail(ASK_B200_E_NCCL, "libnccl.so.2 could not be loaded");
+  return n;
+}
+
+void check_nccl(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) {
+    const char* s = nccl().getErrorString ? nccl().getErrorString(r) : "error";
+    fail(ASK_B200_E_NCCL, std::string(what) + ": " + s);
+  }
+}
+
+// ---- Zipf tables for the generator ---------------------------------------------------------
+struct ZipfKey {
+  int device;
+  double s;
+  uint64_t n;
+  bool operator<(const ZipfKey& o) const {
+    if (device != o.device) return device < o.device;
+    if (s != o.s) return s < o.s;
+    return n < o.n;
+  }
+};
+
+const double* zipf_table(int device, double s, uint64_t n) {
+  static std::mutex mu;
+  static std::map<ZipfKey, double*> tables;
+  std::lock_guard<std::mutex> lock(mu);
+  const ZipfKey key{device, s, n};
+  auto it = tables.find(key);
+  if (it != tables.end()) return it->second;
+  // Unnormalised cumulative weights sum_{j<=k+1} j^-s, accumulated in order.
+  std::vector<double> cdf(n);
+  double acc = 0.0;
+  for (uint64_t k = 0; k < n; ++k) {
+    acc += std::pow(double(k + 1), -s);
+    cdf[k] = acc;
+  }
+  double* dev = nullptr;
+  check_cuda(cudaMalloc(&dev, n * sizeof(double)), "cudaMalloc(zipf table)");
+  check_cuda(cudaMemcpy(dev, cdf.data(), n * sizeof(double), cudaMemcpyHostToDevice), "zipf table upload");
+  tables[key] = dev;
+  return dev;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ask_b200_abi_version(void) { return ASK_B200_ABI_VERSION; }
+
+const char* ask_b200_last_error(void) { return g_last_error.c_str(); }
+
+int ask_b200_plan_create(const char* recipe_json, int device, ask_b200_plan** out) {
+  return guarded([&] {
+    if (!out) fail(ASK_B200_E_INVALID, "out is NULL");
+    *out = nullptr;
+    if (!recipe_json) fail(ASK_B200_E_INVALID, "recipe is NULL");
+    std::unique_ptr<ask_b200_plan> pl(new ask_b200_plan());
+    pl->device = device;
+    if (device >= 0) {
+      int count = 0;
+      if (cudaGetDeviceCount(&count) != cudaSuccess || device >= count)
+        fail(ASK_B200_E_DEVICE, "CUDA device " + std::to_string(device) + " is not available");
+      cudaDeviceProp prop{};
+      check_cuda(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+      if (prop.major != 10)
+        fail(ASK_B200_E_DEVICE, "this library is built for sm_100a; device " + std::to_string(device) + " is sm_" +
+                                    std::to_string(prop.major) + std::to_string(prop.minor));
+      pl->num_sms = prop.multiProcessorCount;
+    }
+    const json::Value r = json::parse(recipe_json);
+    if (r.kind != json::Value::Object) fail(ASK_B200_E_INVALID, "recipe must be a JSON object");
+    const std::string fam = r.at("family").as_str("family");
+    if (fam == "elementwise") { pl->family = FAM_ELEMENTWISE; build_elementwise(*pl, r); }
+    else if (fam == "reduce") { pl->family = FAM_REDUCE; build_reduce(*pl, r); }
+    else if (fam == "gather") { pl->family = FAM_GATHER; build_index(*pl, r, false); }
+    else if (fam == "scatter_add") { pl->family = FAM_SCATTER; build_index(*pl, r, true); }
+    else fail(ASK_B200_E_UNSUPPORTED, "unknown family '" + fam + "'");
+    if (pl->inputs.size() + pl->outputs.size() > 64)
+      fail(ASK_B200_E_UNSUPPORTED, "the pointer ABI supports at most 64 input and output buffers");
+    *out = pl.release();
+  });
+}
+
+int ask_b200_plan_destroy(ask_b200_plan* plan) {
+  delete plan;
+  return ASK_B200_OK;
+}
+
+int ask_b200_plan_ports(const ask_b200_plan* plan, size_t* n_inputs, size_t* n_outputs) {
+  return guarded([&] {
+    if (!plan) fail(ASK_B200_E_INVALID, "plan is NULL");
+    if (n_inputs) *n_inputs = plan->inputs.size();
+    if (n_outputs) *n_outputs = plan->outputs.size();
+  });
+}
+
+int ask_b200_plan_scratch_bytes(const ask_b200_plan* plan, size_t* bytes) {
+  return guarded([&] {
+    if (!plan || !bytes) fail(ASK_B200_E_INVALID, "NULL argument");
+    *bytes = plan->scratch;
+  });
+}
+
+int ask_b200_plan_describe(const ask_b200_plan* plan, char* buf, size_t cap, size_t* needed) {
+  return guarded([&] {
+    if (!plan) fail(ASK_B200_E_INVALID, "plan is NULL");
+    const std::string d = describe(*plan);
+    if (needed) *needed = d.size() + 1;
+    if (buf && cap) {
+      const size_t n = std::min(cap - 1, d.size());
+      std::memcpy(buf, d.data(), n);
+      buf[n] = '\0';
+    }
+  });
+}
+
+int ask_b200_plan_kernel_launches(const ask_b200_plan* plan, int* launches) {
+  return guarded([&] {
+    if (!plan || !launches) fail(ASK_B200_E_INVALID, "NULL argument");
+    *launches = plan->launches;
+  });
+}
+
+int ask_b200_plan_launch(const ask_b200_plan* plan, const uint64_t* ports, size_t n_ports, uint64_t scratch,
+                         void* stream) {
+  return guarded([&] {
+    if (!plan) fail(ASK_B200_E_INVALID, "plan is NULL");
+    check_ports(*plan, ports, n_ports);
+    check_device(*plan);
+    launch_plan(*plan, ports, scratch, static_cast<cudaStream_t>(stream), nullptr);
+  });
+}
+
+int ask_b200_comm_unique_id(unsigned char id[128]) {
+  return guarded([&] {
+    if (!id) fail(ASK_B200_E_INVALID, "id is NULL");
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId layout");
+    ncclUniqueId uid;
+    check_nccl(nccl().getUniqueId(&uid), "ncclGetUniqueId");
+    std::memcpy(id, &uid, 128);
+  });
+}
+
+int ask_b200_comm_create(const unsigned char id[128], int nranks, int rank, int device, ask_b200_comm** out) {
+  return guarded([&] {
+    if (!id || !out) fail(ASK_B200_E_INVALID, "NULL argument");
+    if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks)
+      fail(ASK_B200_E_INVALID, "rank/nranks out of range (at most " + std::to_string(kMaxRanks) + " ranks)");
+    int cur = -1;
+    check_cuda(cudaGetDevice(&cur), "cudaGetDevice");
+    if (cur != device) fail(ASK_B200_E_DEVICE, "current device must be the communicator's device");
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, 128);
+    std::unique_ptr<ask_b200_comm> c(new ask_b200_comm());
+    c->nranks = nranks; c->rank = rank; c->device = device;
+    check_nccl(nccl().commInitRank(&c->comm, nranks, uid, rank), "ncclCommInitRank");
+    *out = c.release();
+  });
+}
+
+int ask_b200_comm_destroy(ask_b200_comm* comm) {
+  return guarded([&] {
+    if (!comm) return;
+    if (comm->comm) check_nccl(nccl().commDestroy(comm->comm), "ncclCommDestroy");
+    delete comm;
+  });
+}
+
+int ask_b200_plan_launch_sharded(const ask_b200_plan* plan, ask_b200_comm* comm, const uint64_t* ports,
+                                 size_t n_ports, uint64_t scratch, void* stream) {
+  return guarded([&] {
+    if (!plan || !comm) fail(ASK_B200_E_INVALID, "NULL argument");
+    if (plan->family != FAM_REDUCE || !plan->shardable)
+      fail(ASK_B200_E_UNSUPPORTED, "only reduce plans with 0-D outputs (split strategy) combine across ranks; "
+                                   "elementwise shards need no collective and use ask_b200_plan_launch");
+    check_ports(*plan, ports, n_ports);
+    check_device(*plan);
+    if (comm->device != plan->device) fail(ASK_B200_E_DEVICE, "communicator and plan are on different devices");
+    if (!scratch) fail(ASK_B200_E_INVALID, "this plan needs scratch memory");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    char* base = reinterpret_cast<char*>(scratch);
+    RedPartial* mine = reinterpret_cast<RedPartial*>(base + plan->record_offset);
+    RedPartial* all = mine + plan->red.n_red;
+    launch_plan(*plan, ports, scratch, st, mine);
+    const size_t rec_bytes = size_t(plan->red.n_red) * sizeof(RedPartial);
+    check_nccl(nccl().allGather(mine, all, rec_bytes, ncclUint8, comm->comm, st), "ncclAllGather");
+    RedArgs a = plan->red;
+    for (size_t k = 0; k < plan->outputs.size(); ++k) a.out[k] = reinterpret_cast<void*>(ports[plan->inputs.size() + k]);
+    check_cuda(red_combine_records(a, all, comm->nranks, st), "combine launch");
+  });
+}
+
+int ask_b200_generate(int kind, uint64_t seed, uint32_t stream_id, uint64_t offset, uint64_t count, double p0,
+                      double p1, uint64_t dst, void* stream) {
+  return guarded([&] {
+    if (kind < GEN_UNIFORM_F32 || kind > GEN_ZIPF_I32) fail(ASK_B200_E_INVALID, "unknown generator kind");
+    if (count && !dst) fail(ASK_B200_E_INVALID, "dst is NULL");
+    const double* cdf = nullptr;
+    uint64_t zn = 0;
+    if (kind == GEN_ZIPF_I64 || kind == GEN_ZIPF_I32) {
+      if (!(p1 >= 1.0) || p1 > 4294967296.0) fail(ASK_B200_E_INVALID, "Zipf rank count must be in [1, 2^32]");
+      zn = uint64_t(p1);
+      int dev = 0;
+      check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+      cdf = zipf_table(dev, p0, zn);
+    }
+    check_cuda(gen_launch(kind, seed, stream_id, offset, count, p0, p1, cdf, zn, reinterpret_cast<void*>(dst),
+                          static_cast<cudaStream_t>(stream)),
+               "generator launch");
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,614 @@
+// Families R and T: map-reduce over a canonical [outer, extent, inner] domain.
+//
+// One launch evaluates a prologue op program per element and folds every
+// requested reduction (sum, prod, max, min, any, all, argmax, argmin) in a
+// single pass over the input.  Reference behaviour it replaces:
+//   * ScalarEmitter::reduce / accumulate (lib/Lowering/ScalarEmitter.h:263-287,
+//     420-472): initial values sum 0, prod 1, min +inf/INT_MAX, max -inf/INT_MIN,
+//     any false, all true (ScalarEmitter.h:426-439);
+//   * the warp-cooperative reduction (ScalarEmitter.h:288-415) -- one warp per
+//     output, butterfly shuffles -- which the reference only picks when no
+//     argmax/argmin shares the batch (lib/Lowering/CUDA.cpp:51-88);
+//   * argmax/argmin (ScalarEmitter.h:473-529): a candidate wins iff it is NaN
+//     and the best is not, or it is strictly better in an ordered compare, so
+//     ties keep the lowest index and the first NaN wins.  The parallel combine
+//     used here is the lexicographic order (NaN first, better value, lower
+//     index), which is associative and gives the sequential answer bit-exactly.
+// Each reduction's result is written once per output; float sums accumulate in
+// f64 (B200's FP64 rate is far above what an HBM-bound pass needs) and are
+// rounded to the output type at the end, f16/bf16 operands are folded in f32
+// like the reference's warp path (ScalarEmitter.h:311, 335, 414).
+//
+// Strategies (chosen by the plan layer):
+//   RS_WARP_ROW  inner == 1: a warp owns an output row, lanes stride the row
+//                with 16-byte loads, U loads in flight per lane.
+//   RS_COLUMN    inner > 1: a thread owns an output column, loads coalesce
+//                across the inner axis.
+//   RS_SPLIT     few outputs over a huge extent (0-D reductions such as cfg5):
+//                every CTA folds one contiguous chunk into a partial record in
+//                scratch; a second single-CTA-per-output kernel combines the
+//                records in a fixed order, so the result is deterministic.
+#include <cuda_runtime.h>
+#include <float.h>
+
+#include "ask_numerics.cuh"
+#include "kernels.h"
+#include "programs.h"
+#include "vec_io.cuh"
+
+namespace askb {
+
+namespace {
+
+__device__ __forceinline__ double d_of(uint64_t w) { return __longlong_as_double(int64_t(w)); }
+__device__ __forceinline__ uint64_t w_of_d(double d) { return uint64_t(__double_as_longlong(d)); }
+
+__device__ __forceinline__ int64_t signed_of(int t, uint64_t w) {
+  return t == kI32 ? int64_t(i32_of(w)) : int64_t(w);
+}
+
+__device__ __forceinline__ void acc_init(int op, int t, uint64_t& v, int64_t& i) {
+  i = -1;
+  const bool fl = dtype_is_float(t);
+  switch (op) {
+    case RED_SUM: v = fl ? w_of_d(0.0) : 0; break;
+    case RED_PROD: v = fl ? w_of_f32(1.0f) : 1; break;
+    // bool max/min start from APInt::getSigned{Min,Max}Value(1) = true / false
+    // and fold with or / and (ScalarEmitter.h:182, 192, 433-439).
+    case RED_MAX: v = fl ? w_of_f32(-INFINITY) : t == kI32 ? w_of_i32(INT32_MIN) : t == kI64 ? uint64_t(INT64_MIN) : 1; break;
+    case RED_MIN: v = fl ? w_of_f32(INFINITY) : t == kI32 ? w_of_i32(INT32_MAX) : t == kI64 ? uint64_t(INT64_MAX) : 0; break;
+    case RED_ANY: v = 0; break;
+    case RED_ALL: v = 1; break;
+    default: v = 0; break;  // arg reductions start empty (i = -1)
+  }
+}
+
+// true when candidate (v2, i2) beats the current best (v, i).
+__device__ __forceinline__ bool arg_better(bool is_max, int t, uint64_t v2, int64_t i2, uint64_t v, int64_t i) {
+  if (i2 < 0) return false;
+  if (i < 0) return true;
+  if (dtype_is_float(t)) {
+    const float a = f32_of(v2), b = f32_of(v);
+    const bool na = a != a, nb = b != b;
+    if (na || nb) return (na && nb) ? i2 < i : na;
+    if (is_max ? a > b : a < b) return true;
+    if (is_max ? a < b : a > b) return false;
+    return i2 < i;
+  }
+  const int64_t a = t == kBool ? int64_t(v2 & 1u) : signed_of(t, v2);
+  const int64_t b = t == kBool ? int64_t(v & 1u) : signed_of(t, v);
+  if (is_max ? a > b : a < b) return true;
+  if (is_max ? a < b : a > b) return false;
+  return i2 < i;
+}
+
+// Fold (x, xi) into the accumulator.  `partial` means x is itself an
+// accumulator (float sums then carry f64 bits instead of an f32 element).
+template <bool kPartial>
+__device__ __forceinline__ void acc_fold(int op, int t, uint64_t& v, int64_t& i, uint64_t x, int64_t xi) {
+  switch (op) {
+    case RED_SUM:
+      if (dtype_is_float(t)) v = w_of_d(d_of(v) + (kPartial ? d_of(x) : double(f32_of(x))));
+      else if (t == kI32) v = w_of_i32(int_add(i32_of(v), i32_of(x)));
+      else v = uint64_t(int_add(int64_t(v), int64_t(x)));
+      break;
+    case RED_PROD:
+      if (dtype_is_float(t)) v = w_of_f32(__fmul_rn(f32_of(v), f32_of(x)));
+      else if (t == kI32) v = w_of_i32(int_mul(i32_of(v), i32_of(x)));
+      else v = uint64_t(int_mul(int64_t(v), int64_t(x)));
+      break;
+    case RED_MAX:
+      if (dtype_is_float(t)) v = w_of_f32(ask_maximum(f32_of(v), f32_of(x)));
+      else if (t == kBool) v = (v | x) & 1u;
+      else v = signed_of(t, x) > signed_of(t, v) ? x : v;
+      break;
+    case RED_MIN:
+      if (dtype_is_float(t)) v = w_of_f32(ask_minimum(f32_of(v), f32_of(x)));
+      else if (t == kBool) v = (v & x) & 1u;
+      else v = signed_of(t, x) < signed_of(t, v) ? x : v;
+      break;
+    case RED_ANY: v = (v | x) & 1u; break;
+    case RED_ALL: v = (v & x) & 1u; break;
+    default:
+      if (arg_better(op == RED_ARGMAX, t, x, xi, v, i)) { v = x; i = xi; }
+      break;
+  }
+}
+
+// Output word of a finished accumulator, in the output's storage type.
+__device__ __forceinline__ uint64_t acc_result(int op, int t, uint64_t v, int64_t i) {
+  if (red_is_arg(op)) return uint64_t(i);
+  if (op == RED_SUM && dtype_is_float(t)) return w_of_f32(round_to(t, float(d_of(v))));
+  if (op == RED_PROD && dtype_is_float(t)) return w_of_f32(round_to(t, f32_of(v)));
+  return v;
+}
+__device__ __forceinline__ int out_type_of(int op, int t) {
+  return red_is_arg(op) ? int(kI64) : (op == RED_ANY || op == RED_ALL) ? int(kBool) : t;
+}
+
+struct Accs {
+  uint64_t v[kMaxReductions];
+  int64_t i[kMaxReductions];
+};
+
+__device__ __forceinline__ void accs_init(const RedArgs& a, Accs& s) {
+#pragma unroll
+  for (int k = 0; k < kMaxReductions; ++k)
+    if (k < a.n_red) acc_init(a.red_op[k], a.red_type[k], s.v[k], s.i[k]);
+}
+
+__device__ __forceinline__ void accs_merge(const RedArgs& a, Accs& s, const Accs& o) {
+#pragma unroll
+  for (int k = 0; k < kMaxReductions; ++k)
+    if (k < a.n_red) acc_fold<true>(a.red_op[k], a.red_type[k], s.v[k], s.i[k], o.v[k], o.i[k]);
+}
+
+// Butterfly over the 32 lanes; every lane ends with the warp's result.
+__device__ __forceinline__ void accs_warp_reduce(const RedArgs& a, Accs& s) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    Accs o;
+#pragma unroll
+    for (int k = 0; k < kMaxReductions; ++k) {
+      if (k < a.n_red) {
+        o.v[k] = __shfl_xor_sync(0xffffffffu, s.v[k], off);
+        o.i[k] = __shfl_xor_sync(0xffffffffu, s.i[k], off);
+      }
+    }
+    accs_merge(a, s, o);
+  }
+}
+
+// Block-wide fold in a fixed order: warps butterfly, then warp 0 folds the
+// per-warp results.  Result valid in thread 0.
+__device__ __forceinline__ void accs_block_reduce(const RedArgs& a, Accs& s) {
+  __shared__ uint64_t sv[kRedThreads / 32][kMaxReductions];
+  __shared__ int64_t si[kRedThreads / 32][kMaxReductions];
+  accs_warp_reduce(a, s);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+#pragma unroll
+    for (int k = 0; k < kMaxReductions; ++k)
+      if (k < a.n_red) { sv[warp][k] = s.v[k]; si[warp][k] = s.i[k]; }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane < int(blockDim.x >> 5)) {
+#pragma unroll
+      for (int k = 0; k < kMaxReductions; ++k)
+        if (k < a.n_red) { s.v[k] = sv[lane][k]; s.i[k] = si[lane][k]; }
+    } else {
+      accs_init(a, s);
+    }
+    accs_warp_reduce(a, s);
+  }
+  __syncthreads();
+}
+
+// ---- specialised path: compile-time prologue P and reduction set R -------------
+template <int... Ops>
+struct RedSet {
+  static constexpr int N = sizeof...(Ops);
+  ASKB_HD static constexpr int op(int k) {
+    constexpr int o[] = {Ops...};
+    return o[k];
+  }
+};
+
+template <class R>
+struct AccsT {
+  uint64_t v[R::N];
+  int64_t i[R::N];
+};
+
+template <class R, int T, int K>
+__device__ __forceinline__ void set_init(AccsT<R>& s) {
+  if constexpr (K < R::N) {
+    acc_init(R::op(K), T, s.v[K], s.i[K]);
+    set_init<R, T, K + 1>(s);
+  }
+}
+template <class R, int T, int K>
+__device__ __forceinline__ void set_fold_value(AccsT<R>& s, uint64_t x, int64_t xi) {
+  if constexpr (K < R::N) {
+    acc_fold<false>(R::op(K), T, s.v[K], s.i[K], x, xi);
+    set_fold_value<R, T, K + 1>(s, x, xi);
+  }
+}
+template <class R, int T, int K>
+__device__ __forceinline__ void set_merge(AccsT<R>& s, const AccsT<R>& o) {
+  if constexpr (K < R::N) {
+    acc_fold<true>(R::op(K), T, s.v[K], s.i[K], o.v[K], o.i[K]);
+    set_merge<R, T, K + 1>(s, o);
+  }
+}
+template <class R, int T>
+__device__ __forceinline__ void set_warp_reduce(AccsT<R>& s) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    AccsT<R> o;
+#pragma unroll
+    for (int k = 0; k < R::N; ++k) {
+      o.v[k] = __shfl_xor_sync(0xffffffffu, s.v[k], off);
+      o.i[k] = __shfl_xor_sync(0xffffffffu, s.i[k], off);
+    }
+    set_merge<R, T, 0>(s, o);
+  }
+}
+template <class R, int T>
+__device__ __forceinline__ void set_block_reduce(AccsT<R>& s) {
+  __shared__ uint64_t sv[kRedThreads / 32][R::N];
+  __shared__ int64_t si[kRedThreads / 32][R::N];
+  set_warp_reduce<R, T>(s);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+#pragma unroll
+    for (int k = 0; k < R::N; ++k) { sv[warp][k] = s.v[k]; si[warp][k] = s.i[k]; }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane < int(blockDim.x >> 5)) {
+#pragma unroll
+      for (int k = 0; k < R::N; ++k) { s.v[k] = sv[lane][k]; s.i[k] = si[lane][k]; }
+    } else {
+      set_init<R, T, 0>(s);
+    }
+    set_warp_reduce<R, T>(s);
+  }
+  __syncthreads();
+}
+template <class R, int T>
+__device__ __forceinline__ void set_write(const RedArgs& a, const AccsT<R>& s, uint64_t o_idx) {
+#pragma unroll
+  for (int k = 0; k < R::N; ++k) {
+    const int op = R::op(k);
+    word_to_storage(out_type_of(op, T), a.out[k], o_idx, acc_result(op, T, s.v[k], s.i[k]));
+  }
+}
+
+// Prologue loads.  `row` is the linear element index of (o, 0) and `o_idx`
+// the output index used by IM_OUTER ports.
+template <class P, int K, int V>
+__device__ __forceinline__ void spec_load(const RedArgs& a, uint64_t row, uint64_t e, uint64_t e_end, uint64_t o_idx,
+                                          bool vec, uint64_t (&x)[P::kIn][V]) {
+  if constexpr (K < P::kIn) {
+    if constexpr (P::in_map(K) == IM_FULL) {
+      load_port<P::in_type(K), IM_FULL, V>(a.in[K], row + e, row + e_end, 1, vec, x[K]);
+    } else {
+      const uint64_t w = word_from_storage(P::in_type(K), a.in[K], P::in_map(K) == IM_SCALAR ? 0 : o_idx);
+#pragma unroll
+      for (int v = 0; v < V; ++v) x[K][v] = w;
+    }
+    spec_load<P, K + 1, V>(a, row, e, e_end, o_idx, vec, x);
+  }
+}
+
+template <class P, int I, int V>
+__device__ __forceinline__ void spec_exec(uint64_t (&r)[P::kInsn][V], const uint64_t (&x)[P::kIn][V]) {
+  if constexpr (I < P::kInsn) {
+    constexpr Insn ins = P::insn(I);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if constexpr (ins.op == OP_INPUT) r[I][v] = x[ins.a][v];
+      else r[I][v] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][v], r[ins.b][v], r[ins.c][v]);
+    }
+    spec_exec<P, I + 1, V>(r, x);
+  }
+}
+
+// Contiguous span [e0, e1) of row `row`, processed by thread t of T cooperating
+// threads in units of V elements (e0 is a multiple of V), U units in flight.
+template <class P, class R, int V, int U>
+__device__ __forceinline__ void span_spec(const RedArgs& a, uint64_t row, uint64_t o_idx, uint64_t e0, uint64_t e1,
+                                          uint32_t t, uint32_t T, bool aligned, AccsT<R>& s) {
+  constexpr int VT = P::out_type(0);
+  for (uint64_t e = e0 + uint64_t(t) * V; e < e1; e += uint64_t(T) * V * U) {
+    uint64_t x[U][P::kIn][V];
+#pragma unroll
+    for (int q = 0; q < U; ++q) {
+      const uint64_t eq = e + uint64_t(q) * T * V;
+      if (eq < e1) spec_load<P, 0, V>(a, row, eq, e1, o_idx, aligned && eq + V <= e1, x[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < U; ++q) {
+      const uint64_t eq = e + uint64_t(q) * T * V;
+      if (eq < e1) {
+        uint64_t r[P::kInsn][V];
+        spec_exec<P, 0, V>(r, x[q]);
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (eq + v < e1) set_fold_value<R, VT, 0>(s, r[P::out_reg(0)][v], int64_t(a.index_base + eq + v));
+      }
+    }
+  }
+}
+
+// Runtime-program version of span_spec (one unit in flight, registers in local memory).
+template <int V>
+__device__ __forceinline__ void span_generic(const Program& prog, const RedArgs& a, uint64_t row, uint64_t o_idx,
+                                             uint64_t e0, uint64_t e1, uint32_t t, uint32_t T, bool aligned, Accs& s,
+                                             uint64_t (*r)[V]) {
+  for (uint64_t e = e0 + uint64_t(t) * V; e < e1; e += uint64_t(T) * V) {
+    const bool vec = aligned && e + V <= e1;
+    for (int i = 0; i < prog.n_insn; ++i) {
+      const Insn& ins = prog.insn[i];
+      if (ins.op == OP_INPUT) {
+        const int map = prog.in_map[ins.a];
+        uint64_t w[V];
+        if (map == IM_FULL) {
+          rt_load<V>(prog.in_type[ins.a], IM_FULL, a.in[ins.a], row + e, row + e1, 1, vec, w);
+        } else {
+          const uint64_t sv = word_from_storage(prog.in_type[ins.a], a.in[ins.a], map == IM_SCALAR ? 0 : o_idx);
+#pragma unroll
+          for (int v = 0; v < V; ++v) w[v] = sv;
+        }
+#pragma unroll
+        for (int v = 0; v < V; ++v) r[ins.dst][v] = w[v];
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          r[ins.dst][v] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][v], r[ins.b][v], r[ins.c][v]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxReductions; ++k) {
+      if (k < a.n_red) {
+        const int reg = prog.out_reg[a.red_src[k]];
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (e + v < e1)
+            acc_fold<false>(a.red_op[k], a.red_type[k], s.v[k], s.i[k], r[reg][v], int64_t(a.index_base + e + v));
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void write_outputs(const RedArgs& a, const Accs& s, uint64_t o_idx) {
+#pragma unroll
+  for (int k = 0; k < kMaxReductions; ++k) {
+    if (k < a.n_red) {
+      const int op = a.red_op[k], t = a.red_type[k];
+      word_to_storage(out_type_of(op, t), a.out[k], o_idx, acc_result(op, t, s.v[k], s.i[k]));
+    }
+  }
+}
+
+// ---- kernels ---------------------------------------------------------------------
+template <class P, class R, int V, int U>
+__global__ void __launch_bounds__(kRedThreads)
+    red_warp_row_kernel(const __grid_constant__ RedArgs a, int aligned) {
+  constexpr int VT = P::out_type(0);
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t warp = (uint64_t(blockIdx.x) * kRedThreads + threadIdx.x) >> 5;
+  const uint64_t nwarps = (uint64_t(gridDim.x) * kRedThreads) >> 5;
+  for (uint64_t o = warp; o < a.outer; o += nwarps) {
+    AccsT<R> s;
+    set_init<R, VT, 0>(s);
+    span_spec<P, R, V, U>(a, o * a.extent, o, 0, a.extent, lane, 32, aligned != 0, s);
+    set_warp_reduce<R, VT>(s);
+    if (lane == 0) set_write<R, VT>(a, s, o);
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(kRedThreads)
+    red_warp_row_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a, int aligned) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t warp = (uint64_t(blockIdx.x) * kRedThreads + threadIdx.x) >> 5;
+  const uint64_t nwarps = (uint64_t(gridDim.x) * kRedThreads) >> 5;
+  uint64_t r[kMaxRegs][V];
+  for (uint64_t o = warp; o < a.outer; o += nwarps) {
+    Accs s;
+    accs_init(a, s);
+    span_generic<V>(prog, a, o * a.extent, o, 0, a.extent, lane, 32, aligned != 0, s, r);
+    accs_warp_reduce(a, s);
+    if (lane == 0) write_outputs(a, s, o);
+  }
+}
+
+// inner > 1: thread per output (o, n); element (o, e, n) at (o*extent + e)*inner + n.
+__global__ void __launch_bounds__(kRedThreads)
+    red_column_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a) {
+  const uint64_t n_outputs = a.outer * a.inner;
+  uint64_t r[kMaxRegs][1];
+  for (uint64_t o_idx = uint64_t(blockIdx.x) * kRedThreads + threadIdx.x; o_idx < n_outputs;
+       o_idx += uint64_t(gridDim.x) * kRedThreads) {
+    const uint64_t o = o_idx / a.inner, n = o_idx % a.inner;
+    Accs s;
+    accs_init(a, s);
+    for (uint64_t e = 0; e < a.extent; ++e) {
+      const uint64_t idx = (o * a.extent + e) * a.inner + n;
+      for (int i = 0; i < prog.n_insn; ++i) {
+        const Insn& ins = prog.insn[i];
+        if (ins.op == OP_INPUT) {
+          const int map = prog.in_map[ins.a];
+          r[ins.dst][0] = word_from_storage(prog.in_type[ins.a], a.in[ins.a],
+                                            map == IM_FULL ? idx : map == IM_SCALAR ? 0 : o_idx);
+        } else {
+          r[ins.dst][0] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][0], r[ins.b][0], r[ins.c][0]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kMaxReductions; ++k)
+        if (k < a.n_red)
+          acc_fold<false>(a.red_op[k], a.red_type[k], s.v[k], s.i[k], r[prog.out_reg[a.red_src[k]]][0],
+                          int64_t(a.index_base + e));
+    }
+    write_outputs(a, s, o_idx);
+  }
+}
+
+// Chunk of the extent owned by CTA c of G, aligned to whole units of V*U*blockDim.
+__device__ __forceinline__ void split_chunk(uint64_t extent, uint32_t c, uint32_t g, uint64_t granule, uint64_t& e0,
+                                            uint64_t& e1) {
+  const uint64_t granules = (extent + granule - 1) / granule;
+  const uint64_t per = (granules + g - 1) / g;
+  e0 = min(extent, uint64_t(c) * per * granule);
+  e1 = min(extent, e0 + per * granule);
+}
+
+template <class P, class R, int V, int U>
+__global__ void __launch_bounds__(kRedThreads)
+    red_split_kernel(const __grid_constant__ RedArgs a, int aligned, RedPartial* __restrict__ part) {
+  constexpr int VT = P::out_type(0);
+  for (uint64_t o = 0; o < a.outer; ++o) {
+    uint64_t e0, e1;
+    split_chunk(a.extent, blockIdx.x, gridDim.x, uint64_t(V) * 32, e0, e1);
+    AccsT<R> s;
+    set_init<R, VT, 0>(s);
+    span_spec<P, R, V, U>(a, o * a.extent, o, e0, e1, threadIdx.x, kRedThreads, aligned != 0, s);
+    set_block_reduce<R, VT>(s);
+    if (threadIdx.x == 0) {
+      RedPartial* dst = part + (o * gridDim.x + blockIdx.x) * R::N;
+#pragma unroll
+      for (int k = 0; k < R::N; ++k) dst[k] = RedPartial{s.v[k], s.i[k]};
+    }
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(kRedThreads)
+    red_split_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a, int aligned,
+                      RedPartial* __restrict__ part) {
+  uint64_t r[kMaxRegs][V];
+  for (uint64_t o = 0; o < a.outer; ++o) {
+    uint64_t e0, e1;
+    split_chunk(a.extent, blockIdx.x, gridDim.x, uint64_t(V) * 32, e0, e1);
+    Accs s;
+    accs_init(a, s);
+    span_generic<V>(prog, a, o * a.extent, o, e0, e1, threadIdx.x, kRedThreads, aligned != 0, s, r);
+    accs_block_reduce(a, s);
+    if (threadIdx.x == 0) {
+      RedPartial* dst = part + (o * gridDim.x + blockIdx.x) * a.n_red;
+      for (int k = 0; k < a.n_red; ++k) dst[k] = RedPartial{s.v[k], s.i[k]};
+    }
+  }
+}
+
+// Fold n partial records of output o (layout [outer][n][n_red]) in a fixed
+// order.  Writes the outputs, or one record per output when `rec_out` is set.
+__global__ void __launch_bounds__(kRedThreads)
+    red_combine_kernel(const __grid_constant__ RedArgs a, const RedPartial* __restrict__ part, int n,
+                       RedPartial* __restrict__ rec_out) {
+  const uint64_t o = blockIdx.x;
+  Accs s;
+  accs_init(a, s);
+  for (int j = threadIdx.x; j < n; j += kRedThreads) {
+    const RedPartial* src = part + (o * n + j) * a.n_red;
+    Accs x;
+#pragma unroll
+    for (int k = 0; k < kMaxReductions; ++k)
+      if (k < a.n_red) { x.v[k] = src[k].v; x.i[k] = src[k].idx; }
+    accs_merge(a, s, x);
+  }
+  accs_block_reduce(a, s);
+  if (threadIdx.x == 0) {
+    if (rec_out) {
+      for (int k = 0; k < a.n_red; ++k) rec_out[o * a.n_red + k] = RedPartial{s.v[k], s.i[k]};
+    } else {
+      write_outputs(a, s, o);
+    }
+  }
+}
+
+// ---- specialisation table ------------------------------------------------------------
+template <class P> struct RedVec {
+  static constexpr int V = 16 / dtype_bytes(P::in_type(0)) > 8 ? 8 : 16 / dtype_bytes(P::in_type(0));
+  static constexpr int U = V >= 8 ? 2 : 4;
+};
+
+using SetRowStats = RedSet<RED_SUM, RED_MAX, RED_MIN, RED_ARGMAX>;
+using SetGlobal = RedSet<RED_SUM, RED_MIN, RED_ARGMIN>;
+using SetMax = RedSet<RED_MAX>;
+using SetSum = RedSet<RED_SUM>;
+
+// Calls f.template operator()<P, R>() for the specialisation `spec`.
+template <class F>
+bool with_spec(int spec, F&& f) {
+  switch (spec) {
+    case RED_ROWSTATS_F32: f(ProgIdentity<kF32>{}, SetRowStats{}); return true;
+    case RED_GLOBAL_F32: f(ProgIdentity<kF32>{}, SetGlobal{}); return true;
+    case RED_SOFTMAX_MAX_F16: f(ProgSoftmaxMax<kF16>{}, SetMax{}); return true;
+    case RED_SOFTMAX_MAX_BF16: f(ProgSoftmaxMax<kBF16>{}, SetMax{}); return true;
+    case RED_SOFTMAX_SUM_F16: f(ProgSoftmaxSum<kF16>{}, SetSum{}); return true;
+    case RED_SOFTMAX_SUM_BF16: f(ProgSoftmaxSum<kBF16>{}, SetSum{}); return true;
+    default: return false;
+  }
+}
+
+const void* kernel_ptr(int spec, int strategy) {
+  const void* ptr = nullptr;
+  const bool found = with_spec(spec, [&](auto p, auto r) {
+    using P = decltype(p);
+    using R = decltype(r);
+    ptr = strategy == RS_WARP_ROW
+              ? reinterpret_cast<const void*>(&red_warp_row_kernel<P, R, RedVec<P>::V, RedVec<P>::U>)
+              : reinterpret_cast<const void*>(&red_split_kernel<P, R, RedVec<P>::V, RedVec<P>::U>);
+  });
+  if (found && strategy != RS_COLUMN) return ptr;
+  if (strategy == RS_WARP_ROW) return reinterpret_cast<const void*>(&red_warp_row_generic<4>);
+  if (strategy == RS_COLUMN) return reinterpret_cast<const void*>(&red_column_generic);
+  return reinterpret_cast<const void*>(&red_split_generic<4>);
+}
+
+}  // namespace
+
+bool red_spec_program(int spec, Program* out, int* n_red, uint8_t* ops) {
+  return with_spec(spec, [&](auto p, auto r) {
+    using P = decltype(p);
+    using R = decltype(r);
+    *out = program_of<P>();
+    *n_red = R::N;
+    for (int k = 0; k < R::N; ++k) ops[k] = uint8_t(R::op(k));
+  });
+}
+
+cudaError_t red_occupancy(int spec, int strategy, int* blocks_per_sm) {
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kernel_ptr(spec, strategy), kRedThreads, 0);
+}
+
+size_t red_split_scratch_bytes(int grid, int n_red) { return size_t(grid) * size_t(n_red) * sizeof(RedPartial); }
+
+cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArgs& a, int aligned, int grid,
+                       void* scratch, RedPartial* rec_out, cudaStream_t st) {
+  if (a.outer == 0 || a.inner == 0) return cudaSuccess;
+  if (strategy == RS_COLUMN) {
+    red_column_generic<<<grid, kRedThreads, 0, st>>>(prog, a);
+    return cudaGetLastError();
+  }
+  cudaError_t err = cudaSuccess;
+  const bool found = with_spec(spec, [&](auto p, auto r) {
+    using P = decltype(p);
+    using R = decltype(r);
+    constexpr int V = RedVec<P>::V, U = RedVec<P>::U;
+    if (strategy == RS_WARP_ROW) {
+      red_warp_row_kernel<P, R, V, U><<<grid, kRedThreads, 0, st>>>(a, aligned);
+      err = cudaGetLastError();
+      return;
+    }
+    RedPartial* part = static_cast<RedPartial*>(scratch);
+    red_split_kernel<P, R, V, U><<<grid, kRedThreads, 0, st>>>(a, aligned, part);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return;
+    red_combine_kernel<<<unsigned(a.outer), kRedThreads, 0, st>>>(a, part, grid, rec_out);
+    err = cudaGetLastError();
+  });
+  if (found) return err;
+  if (strategy == RS_WARP_ROW) {
+    red_warp_row_generic<4><<<grid, kRedThreads, 0, st>>>(prog, a, aligned);
+    return cudaGetLastError();
+  }
+  RedPartial* part = static_cast<RedPartial*>(scratch);
+  red_split_generic<4><<<grid, kRedThreads, 0, st>>>(prog, a, aligned, part);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  red_combine_kernel<<<unsigned(a.outer), kRedThreads, 0, st>>>(a, part, grid, rec_out);
+  return cudaGetLastError();
+}
+
+cudaError_t red_combine_records(const RedArgs& a, const RedPartial* records, int n, cudaStream_t st) {
+  red_combine_kernel<<<unsigned(a.outer), kRedThreads, 0, st>>>(a, records, n, nullptr);
+  return cudaGetLastError();
+}
+
+}  // namespace askb

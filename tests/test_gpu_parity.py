@@ -1,0 +1,502 @@
+"""GPU parity: every kernel family against the CPU oracle, through the C ABI.
+
+Bit-exact: integer/bitwise work, max/min, argmax/argmin, gather, i32
+scatter_add, casts and correctly rounded float ops.  Tolerances (stated per
+test) for transcendental functions (CUDA's vs the host libm the reference's
+host path calls) and for float sums (the reference leaves the order free,
+docs/en/ir.md:69).  Full BASELINE sizes are checked through sampled rows and
+size-independent properties where the oracle would take too long.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import ask_b200
+import oracle
+from ask_b200 import recipes as R
+from gpu_util import (NUMPY, bf16_to_f32, empty_dev, f16_to_f32, from_dev, gen_dev, run_plan, to_dev, ulp_f32)
+from kat_cases import build, load_cases
+
+pytestmark = pytest.mark.gpu
+THREADS = 16
+CASES = load_cases()
+
+
+def same_with_nan(a: np.ndarray, b: np.ndarray) -> bool:
+    a, b = np.asarray(a), np.asarray(b)
+    if a.dtype.kind == "f":
+        nan = np.isnan(a)
+        return bool(np.array_equal(nan, np.isnan(b)) and np.array_equal(a[~nan].view(np.uint32 if a.itemsize == 4
+                                                                                         else np.uint64),
+                                                                        b[~nan].view(np.uint32 if b.itemsize == 4
+                                                                                      else np.uint64)))
+    return bool(np.array_equal(a, b))
+
+
+# ---- documented known answers -----------------------------------------------------
+@pytest.mark.parametrize("case", CASES, ids=[f"{i}-{c['kind']}" for i, c in enumerate(CASES)])
+def test_kat_on_gpu(device, case):
+    kind, rec, ins, check = build(case)
+    plan_types = [o["element_type"] for o in ask_b200.Plan(rec, -1).describe()["port_map"][len(ins):]]
+    outs = run_plan(rec, ins, plan_types)
+    assert check(outs), f"{case} -> {outs}"
+
+
+# ---- generator ------------------------------------------------------------------
+@pytest.mark.parametrize("kind,p0,p1,dt", [(0, -4.0, 4.0, torch.float32), (0, 0.0, 1.0, torch.float32),
+                                           (4, 0, 0, torch.int32), (5, 1.1, 1 << 20, torch.int64),
+                                           (6, 1.1, 1000, torch.int32)])
+def test_generator_matches_host(device, kind, p0, p1, dt):
+    for offset in (0, 12345, (1 << 32) - 100):
+        g = gen_dev(kind, 0xA5C4, 3, 4099, p0, p1, dt, offset).cpu().numpy()
+        h = oracle.generate(kind, 0xA5C4, 3, offset, 4099, p0, p1)
+        assert np.array_equal(g.view(np.uint8), h.view(np.uint8)), f"kind {kind} offset {offset}"
+
+
+def test_normal_generator_close_to_host(device):
+    g = gen_dev(1, 0xA5C2, 0, 100000, 0.0, 1.0, torch.float32).cpu().numpy()
+    h = oracle.generate(1, 0xA5C2, 0, 0, 100000, 0.0, 1.0)
+    assert np.max(np.abs(g - h)) <= 1e-6
+    assert abs(float(g.mean())) < 0.02 and abs(float(g.std()) - 1.0) < 0.02
+
+
+# ---- cfg1: fused elementwise ---------------------------------------------------------
+def cfg1_tolerance(a, b, c):
+    t0 = np.maximum(np.abs(np.exp(a.astype(np.float64)) * b), np.abs(c))
+    t1 = np.maximum(np.abs(np.maximum(a, b)), np.abs(np.tanh(c.astype(np.float64))))
+    return 4 * ulp_f32(t0.astype(np.float32)), 4 * ulp_f32(t1.astype(np.float32))
+
+
+def check_cfg1(a, b, c, y0, y1):
+    r0, r1 = oracle.cfg1(a, b, c, threads=THREADS)
+    tol0, tol1 = cfg1_tolerance(a, b, c)
+    for got, want, tol in ((y0, r0, tol0), (y1, r1, tol1)):
+        nan = np.isnan(want)
+        assert np.array_equal(nan, np.isnan(got))
+        fin = ~nan & np.isfinite(want)
+        assert np.array_equal(got[~nan & ~fin], want[~nan & ~fin])  # infinities exactly
+        err = np.abs(got[fin].astype(np.float64) - want[fin])
+        assert np.all(err <= tol[fin]), f"max err {err.max()} at {np.argmax(err - tol[fin])}"
+
+
+SPECIAL = np.array([0.0, -0.0, 1.0, -1.0, np.inf, -np.inf, np.nan, 88.0, 89.0, -104.0, 1e-40, -1e-45,
+                    3.4e38, 0.5, 20.0, -20.0], np.float32)
+
+
+@pytest.mark.parametrize("n", [1, 3, 4, 5, 17, 255, 1000, 4099])
+@pytest.mark.parametrize("offset", [0, 4])
+def test_cfg1_edges_and_tails(device, n, offset):
+    rng = np.random.default_rng(n)
+    a = rng.choice(SPECIAL, n).astype(np.float32)
+    b = rng.choice(SPECIAL, n).astype(np.float32)
+    c = rng.uniform(-4, 4, n).astype(np.float32)
+    c[::3] = rng.choice(SPECIAL, len(c[::3]))
+    y0, y1 = run_plan(R.cfg1_step(n), [a, b, c], ["f32", "f32"], offset_bytes=offset)
+    check_cfg1(a, b, c, y0, y1)
+
+
+def test_cfg1_full_size(device):
+    n = 4096 * 4096
+    a, b, c = (gen_dev(0, 0xA5C1, s, n, -4.0, 4.0, torch.float32) for s in range(3))
+    plan = ask_b200.Plan(R.cfg1_step(n), 0)
+    y0, y1 = torch.empty_like(a), torch.empty_like(a)
+    plan.launch([a, b, c], [y0, y1], None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    check_cfg1(*(t.cpu().numpy() for t in (a, b, c, y0, y1)))
+
+
+# ---- cfg2: row reductions --------------------------------------------------------------
+def check_rowstats(x, rows, cols, got):
+    s, mx, mn, am = got
+    rs, rmx, rmn, ram = oracle.rowstats(x, rows, cols, threads=THREADS)
+    assert same_with_nan(mx, rmx) and same_with_nan(mn, rmn)
+    assert np.array_equal(am, ram)
+    absum = np.abs(x.reshape(rows, cols).astype(np.float64)).sum(axis=1)
+    ref64 = x.reshape(rows, cols).astype(np.float64).sum(axis=1)
+    fin = np.isfinite(ref64)
+    assert np.all(np.abs(s[fin].astype(np.float64) - ref64[fin]) <= 2.0 ** -20 * absum[fin] + 1e-30)
+
+
+def test_cfg2_full_size(device):
+    rows, cols = 65536, 1024
+    x = gen_dev(1, 0xA5C2, 0, rows * cols, 0.0, 1.0, torch.float32)
+    plan = ask_b200.Plan(R.cfg2_step(rows, cols), 0)
+    outs = [torch.empty(rows, dtype=torch.float32, device="cuda") for _ in range(3)] + \
+           [torch.empty(rows, dtype=torch.int64, device="cuda")]
+    plan.launch([x], outs, None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    check_rowstats(x.cpu().numpy(), rows, cols, [o.cpu().numpy() for o in outs])
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 31), (5, 32), (7, 33), (9, 100), (64, 1024), (33, 4097),
+                                       (2, 70000)])
+def test_cfg2_edges(device, rows, cols):
+    rng = np.random.default_rng(rows * 1000 + cols)
+    x = rng.standard_normal(rows * cols).astype(np.float32)
+    # ties, signed zeros and NaNs inside rows
+    x[::7] = 2.5
+    x[3::11] = -0.0
+    x[5::13] = 0.0
+    if rows > 2:
+        x[cols * 2 + min(5, cols - 1)] = np.nan
+        x[cols * 2 + cols - 1] = np.nan
+    outs = run_plan(R.cfg2_step(rows, cols), [x], ["f32", "f32", "f32", "i64"])
+    check_rowstats(x, rows, cols, outs)
+
+
+# ---- cfg3: softmax partition -------------------------------------------------------------
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_cfg3_softmax_full_size(device, dtype):
+    rows, cols = 32768, 4096
+    kind = 2 if dtype == "f16" else 3
+    x = gen_dev(kind, 0xA5C3, 0, rows * cols, 0.0, 2.0, torch.int16)
+    steps = [ask_b200.Plan(s, 0) for s in R.cfg3_steps(dtype, rows, cols)]
+    m = torch.empty(rows, dtype=torch.float32, device="cuda")
+    s = torch.empty(rows, dtype=torch.float32, device="cuda")
+    y = torch.empty(rows * cols, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream()
+    steps[0].launch([x], [m], None, st)
+    steps[1].launch([x, m], [s], None, st)
+    steps[2].launch([x, m, s], [y], None, st)
+    torch.cuda.synchronize()
+    sample = np.unique(np.concatenate([np.arange(64), np.random.default_rng(3).integers(0, rows, 448)]))
+    xh = x.view(rows, cols)[torch.from_numpy(sample).cuda()].cpu().numpy().view(np.uint16).reshape(-1)
+    rm, rs, ry = oracle.softmax(dtype, xh, len(sample), cols, threads=THREADS)
+    gm, gs = m.cpu().numpy()[sample], s.cpu().numpy()[sample]
+    gy = y.view(rows, cols)[torch.from_numpy(sample).cuda()].cpu().numpy().view(np.uint16).reshape(-1)
+    assert np.array_equal(gm, rm)
+    assert np.all(np.abs(gs.astype(np.float64) - rs) <= 2.0 ** -20 * rs)
+    conv = f16_to_f32 if dtype == "f16" else bf16_to_f32
+    gyv, ryv = conv(gy), conv(ry)
+    step = np.spacing(np.abs(ryv).astype(np.float16)).astype(np.float32) if dtype == "f16" else \
+        np.abs(bf16_to_f32(ry + 1) - ryv)
+    assert np.all(np.abs(gyv - ryv) <= step + 1e-45), "softmax output differs by more than 1 ulp"
+    # each output row sums to ~1
+    rowsum = gyv.reshape(len(sample), cols).astype(np.float64).sum(axis=1)
+    assert np.all(np.abs(rowsum - 1.0) < 0.02)
+
+
+# ---- cfg4: gather / scatter_add ---------------------------------------------------------
+@pytest.mark.parametrize("itype", ["i64", "i32"])
+@pytest.mark.parametrize("inner,dtype", [(256, "f32"), (3, "f32"), (8, "f16"), (5, "i64"), (64, "bool")])
+def test_gather_small_with_out_of_bounds(device, itype, inner, dtype):
+    rows, n = 97, 301
+    rng = np.random.default_rng(inner)
+    table = rng.integers(0, 255, rows * inner * np.dtype(NUMPY[dtype]).itemsize, dtype=np.uint8).view(NUMPY[dtype])
+    if dtype == "bool":
+        table = (table & 1).astype(np.uint8)
+    idx = rng.integers(-5, rows + 5, n).astype(np.int64 if itype == "i64" else np.int32)
+    idx[:4] = [0, rows - 1, -1, rows]
+    (out,) = run_plan(R.gather(dtype, itype, rows, inner, n), [table, idx], [dtype])
+    want = oracle.gather(table, idx, 1, rows, inner)
+    assert np.array_equal(out.view(np.uint8), want.view(np.uint8))
+
+
+def zipf_index(n, rows, dt=torch.int64):
+    return gen_dev(5 if dt == torch.int64 else 6, 0xA5C4, 1, n, 1.1, rows, dt)
+
+
+def test_cfg4_gather_full_size(device):
+    rows, dim, n = 1 << 20, 256, 1 << 23
+    table = gen_dev(1, 0xA5C4, 0, rows * dim, 0.0, 0.02, torch.float32)
+    idx = zipf_index(n, rows)
+    out = torch.empty(n * dim, dtype=torch.float32, device="cuda")
+    ask_b200.Plan(R.cfg4_gather_step(rows, dim, n), 0).launch([table, idx], [out], None,
+                                                              torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    sample = torch.from_numpy(np.random.default_rng(4).integers(0, n, 4096)).cuda()
+    got = out.view(n, dim)[sample]
+    want = table.view(rows, dim)[idx[sample]]
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+    # the index distribution is the Zipf head the survey computes: row 0 ~ 12.4%
+    frac0 = float((idx == 0).sum()) / n
+    assert 0.11 < frac0 < 0.14
+
+
+@pytest.mark.parametrize("dtype", ["i32", "f32", "i64"])
+@pytest.mark.parametrize("inner", [256, 5])
+def test_scatter_add_small(device, dtype, inner):
+    rows, n = 61, 2000
+    rng = np.random.default_rng(7 + inner)
+    idx = rng.integers(-3, rows + 3, n).astype(np.int64)
+    idx[:50] = 0  # hot row
+    if dtype == "f32":
+        base = rng.standard_normal(rows * inner).astype(np.float32)
+        upd = rng.standard_normal(n * inner).astype(np.float32)
+    else:
+        info = np.iinfo(NUMPY[dtype])
+        base = rng.integers(info.min, info.max, rows * inner, dtype=NUMPY[dtype])
+        upd = rng.integers(info.min, info.max, n * inner, dtype=NUMPY[dtype])
+    (out,) = run_plan(R.scatter_add(dtype, "i64", rows, inner, n), [base, idx, upd], [dtype])
+    if dtype == "f32":
+        ref64, abs64 = oracle.scatter_add_f64(base, idx, upd, 1, rows, inner)
+        assert np.all(np.abs(out - ref64) <= 2.0 ** -20 * (abs64 + np.abs(base)) + 1e-30)
+    else:
+        assert np.array_equal(out, oracle.scatter_add(dtype, base, idx, upd, 1, rows, inner))
+
+
+def test_cfg4_scatter_full_size(device):
+    rows, dim, n = 1 << 20, 256, 1 << 23
+    idx = zipf_index(n, rows)
+    grad = gen_dev(1, 0xA5C4, 2, n * dim, 0.0, 1.0, torch.float32)
+    base = torch.zeros(rows * dim, dtype=torch.float32, device="cuda")
+    out = torch.empty_like(base)
+    ask_b200.Plan(R.cfg4_scatter_step(rows, dim, n), 0).launch([base, idx, grad], [out], None,
+                                                               torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    sample_rows = [0, 1, 2, 7, 100, 5000, 123456, rows - 1]
+    idx_h = idx.cpu().numpy()
+    for r in sample_rows:
+        sel = torch.from_numpy(np.nonzero(idx_h == r)[0]).cuda()
+        ref = grad.view(n, dim)[sel].double().sum(dim=0) if sel.numel() else torch.zeros(dim, dtype=torch.float64,
+                                                                                          device="cuda")
+        absum = grad.view(n, dim)[sel].double().abs().sum(dim=0) if sel.numel() else ref
+        got = out.view(rows, dim)[r].double()
+        assert torch.all((got - ref).abs() <= 2.0 ** -20 * absum + 1e-30), f"row {r}"
+    # linearity: column sums of the table equal column sums of all updates
+    col_out = out.view(rows, dim).double().sum(dim=0)
+    col_upd = grad.view(n, dim).double().sum(dim=0)
+    col_abs = grad.view(n, dim).double().abs().sum(dim=0)
+    assert torch.all((col_out - col_upd).abs() <= 2.0 ** -20 * col_abs)
+
+
+def test_cfg4_scatter_i32_bit_exact(device):
+    rows, dim, n = 1 << 14, 256, 1 << 16
+    idx = zipf_index(n, rows)
+    upd = gen_dev(4, 0xA5C4, 5, n * dim, 0, 0, torch.int32)
+    base = gen_dev(4, 0xA5C4, 6, rows * dim, 0, 0, torch.int32)
+    out = torch.empty_like(base)
+    ask_b200.Plan(R.cfg4_scatter_step(rows, dim, n, dtype="i32"), 0).launch(
+        [base, idx, upd], [out], None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    want = oracle.scatter_add("i32", base.cpu().numpy(), idx.cpu().numpy(), upd.cpu().numpy(), 1, rows, dim)
+    assert np.array_equal(out.cpu().numpy(), want)
+
+
+# ---- cfg5: global reduction and i32 chain ---------------------------------------------
+@pytest.mark.parametrize("n", [1, 100, 4097, 1 << 20, (1 << 24) + 3])
+def test_cfg5a_against_oracle(device, n):
+    x = gen_dev(0, 0xA5C5, 0, n, 0.0, 1.0, torch.float32)
+    if n > 10:
+        x[n // 3] = 0.0  # duplicate minima: the lowest index must win
+    outs = [torch.empty(1, dtype=torch.float32, device="cuda") for _ in range(2)] + \
+           [torch.empty(1, dtype=torch.int64, device="cuda")]
+    plan = ask_b200.Plan(R.cfg5a_step(n), 0)
+    scratch = torch.full((max(plan.scratch_bytes, 16),), 0x7F, dtype=torch.uint8, device="cuda")
+    plan.launch([x], outs, scratch, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    s64, sref, mn, am = oracle.cfg5a(x.cpu().numpy(), threads=THREADS)
+    gs, gm, ga = float(outs[0].item()), float(outs[1].item()), int(outs[2].item())
+    assert abs(gs - s64) <= 2.0 ** -20 * s64 + 1e-30
+    assert gm == mn and ga == am
+
+
+def test_cfg5a_nan_wins_first(device):
+    x = np.random.default_rng(0).random(100000).astype(np.float32)
+    x[777] = np.nan
+    x[70000] = np.nan
+    x[5] = -1.0
+    s, m, a = run_plan(R.cfg5a_step(x.size), [x], ["f32", "f32", "i64"])
+    assert np.isnan(s[0]) and np.isnan(m[0]) and a[0] == 777
+
+
+def test_cfg5a_full_size(device):
+    n = 1 << 32
+    x = gen_dev(0, 0xA5C5, 0, n, 0.0, 1.0, torch.float32)
+    outs = [torch.empty(1, dtype=torch.float32, device="cuda") for _ in range(2)] + \
+           [torch.empty(1, dtype=torch.int64, device="cuda")]
+    plan = ask_b200.Plan(R.cfg5a_step(n), 0)
+    scratch = torch.empty(plan.scratch_bytes, dtype=torch.uint8, device="cuda")
+    plan.launch([x], outs, scratch, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    total, mn, first = 0.0, math.inf, -1
+    chunk = 1 << 28
+    for c0 in range(0, n, chunk):
+        part = x[c0:c0 + chunk]
+        total += float(part.double().sum())
+        pm = float(part.min())
+        if pm < mn:
+            mn, first = pm, c0 + int(torch.nonzero(part == pm)[0])
+    assert abs(float(outs[0].item()) - total) <= 2.0 ** -20 * total
+    assert float(outs[1].item()) == mn and int(outs[2].item()) == first
+
+
+@pytest.mark.parametrize("n", [1, 7, 1000, 1 << 20, (1 << 22) + 5])
+@pytest.mark.parametrize("offset", [0, 4])
+def test_cfg5b_bit_exact(device, n, offset):
+    rng = np.random.default_rng(n)
+    x = rng.integers(-(2 ** 31), 2 ** 31, n, dtype=np.int64).astype(np.int32)
+    y = rng.integers(-(2 ** 31), 2 ** 31, n, dtype=np.int64).astype(np.int32)
+    (z,) = run_plan(R.cfg5b_step(n), [x, y], ["i32"], offset_bytes=offset)
+    assert np.array_equal(z, oracle.cfg5b(x, y))
+
+
+def test_cfg5b_full_size_sampled(device):
+    n = 1 << 31
+    x = gen_dev(4, 0xA5C5, 1, n, 0, 0, torch.int32)
+    y = gen_dev(4, 0xA5C5, 2, n, 0, 0, torch.int32)
+    z = torch.empty_like(x)
+    ask_b200.Plan(R.cfg5b_step(n), 0).launch([x, y], [z], None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    for c0 in (0, n // 2 - 12345, n - (1 << 20)):
+        sl = slice(c0, c0 + (1 << 20))
+        assert np.array_equal(z[sl].cpu().numpy(), oracle.cfg5b(x[sl].cpu().numpy(), y[sl].cpu().numpy()))
+
+
+# ---- generic (runtime-interpreted) programs ---------------------------------------------
+FLOAT_BINARY = ["add", "mul", "div", "maximum", "minimum", "floordiv", "mod"]
+FLOAT_UNARY = ["abs", "floor", "ceil", "round", "sqrt"]
+INT_BINARY = ["add", "mul", "floordiv", "mod", "pow", "maximum", "minimum", "bitwise_and", "bitwise_or",
+              "bitwise_xor", "shift_left", "shift_right"]
+
+
+def random_program(rng, dtype):
+    p = R.Program()
+    vals = [p.input(dtype), p.input(dtype), p.input(dtype, "scalar")]
+    for _ in range(10):
+        r = rng.random()
+        a, b = vals[rng.integers(len(vals))], vals[rng.integers(len(vals))]
+        if dtype in ("f32", "f16", "bf16"):
+            if r < 0.55:
+                vals.append(p.op(FLOAT_BINARY[rng.integers(len(FLOAT_BINARY))], a, b))
+            elif r < 0.8:
+                vals.append(p.op(FLOAT_UNARY[rng.integers(len(FLOAT_UNARY))], a))
+            else:
+                c = p.compare(["lt", "le", "eq", "ne", "gt", "ge"][rng.integers(6)], a, b)
+                vals.append(p.select(c, a, b))
+        else:
+            if r < 0.8:
+                vals.append(p.op(INT_BINARY[rng.integers(len(INT_BINARY))], a, b))
+            else:
+                vals.append(p.abs(a))
+    outs = [vals[-1], vals[-3], p.cast(vals[-2], "f32" if dtype != "f32" else "i32"),
+            p.compare("gt", vals[-1], vals[-4])]
+    return p, outs
+
+
+def random_inputs(rng, dtype, n):
+    if dtype == "f32":
+        x = rng.standard_normal(n).astype(np.float32) * 4
+        x[::5] = rng.choice(SPECIAL, len(x[::5]))
+        return x
+    if dtype == "f16":
+        return (rng.standard_normal(n) * 8).astype(np.float16).view(np.uint16)
+    if dtype == "bf16":
+        return (rng.standard_normal(n).astype(np.float32) * 8).view(np.uint32).__rshift__(16).astype(np.uint16)
+    if dtype == "i32":
+        x = rng.integers(-100, 100, n).astype(np.int32)
+        x[::7] = rng.integers(-(2 ** 31), 2 ** 31, len(x[::7]), dtype=np.int64).astype(np.int32)
+        return x
+    x = rng.integers(-100, 100, n).astype(np.int64)
+    x[::7] = rng.integers(-(2 ** 63), 2 ** 63 - 1, len(x[::7]), dtype=np.int64)
+    return x
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16", "i32", "i64"])
+@pytest.mark.parametrize("seed", range(6))
+def test_generic_programs_match_oracle(device, dtype, seed):
+    rng = np.random.default_rng(seed * 31 + len(dtype))
+    p, outs = random_program(rng, dtype)
+    n = 1031
+    rec = R.elementwise(p, outs, n)
+    ins = [random_inputs(rng, dtype, n), random_inputs(rng, dtype, n), random_inputs(rng, dtype, 1)]
+    assert ask_b200.Plan(rec, -1).describe()["kernel"] == "ew_generic"
+    got = run_plan(rec, ins, [o.dtype for o in outs])
+    want = oracle.elementwise(rec, ins)
+    for k, (g, w) in enumerate(zip(got, want)):
+        if outs[k].dtype == "f32":
+            assert same_with_nan(g, w), f"output {k}"
+        elif outs[k].dtype in ("f16", "bf16"):
+            conv = f16_to_f32 if outs[k].dtype == "f16" else bf16_to_f32
+            assert same_with_nan(conv(g), conv(w)), f"output {k}"
+        else:
+            assert np.array_equal(g, w), f"output {k}"
+
+
+@pytest.mark.parametrize("op", ["exp", "log", "sin", "cos", "tanh", "erf", "pow"])
+def test_transcendentals_within_ulps(device, op):
+    rng = np.random.default_rng(11)
+    n = 50000
+    x = rng.uniform(-10, 10, n).astype(np.float32)
+    y = rng.uniform(-3, 3, n).astype(np.float32)
+    if op in ("log",):
+        x = np.abs(x) + np.float32(1e-3)
+    if op == "pow":
+        x = np.abs(x)
+    p = R.Program()
+    a, b = p.input("f32"), p.input("f32")
+    r = p.op(op, a, b) if op == "pow" else p.op(op, a)
+    rec = R.elementwise(p, [r], n)
+    (got,) = run_plan(rec, [x, y], ["f32"])
+    (want,) = oracle.elementwise(rec, [x, y])
+    fin = np.isfinite(want)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    err = np.abs(got[fin].astype(np.float64) - want[fin]) / ulp_f32(want[fin])
+    assert err.max() <= 4, f"{op}: {err.max()} ulp"
+
+
+# ---- reductions with prologues, column reductions, generic reductions ---------------------
+@pytest.mark.parametrize("outer,extent,inner", [(3, 5, 7), (1, 1000, 33), (16, 64, 4), (2, 3, 1000)])
+def test_column_reductions(device, outer, extent, inner):
+    rng = np.random.default_rng(outer + extent + inner)
+    x = rng.standard_normal(outer * extent * inner).astype(np.float32)
+    x[::9] = 1.5
+    p = R.Program()
+    v = p.input("f32")
+    rec = R.reduce(p, v, ["sum", "max", "min", "argmax", "argmin", "prod"], outer, extent, inner)
+    got = run_plan(rec, [x], ["f32", "f32", "f32", "i64", "i64", "f32"])
+    want = oracle.reduce(rec, [x])
+    assert np.array_equal(got[1], want[1]) and np.array_equal(got[2], want[2])
+    assert np.array_equal(got[3], want[3]) and np.array_equal(got[4], want[4])
+    xx = x.reshape(outer, extent, inner).astype(np.float64)
+    tol = 2.0 ** -20 * np.abs(xx).sum(axis=1).reshape(-1)
+    assert np.all(np.abs(got[0] - xx.sum(axis=1).reshape(-1)) <= tol + 1e-30)
+    rel = np.abs(got[5].astype(np.float64) - want[5]) / np.maximum(np.abs(want[5]), 1e-30)
+    assert np.all((rel <= 1e-5) | (np.abs(want[5]) < 1e-30))
+
+
+@pytest.mark.parametrize("dtype", ["i32", "i64", "bool"])
+def test_integer_and_bool_reductions(device, dtype):
+    rng = np.random.default_rng(5)
+    rows, cols = 37, 301
+    if dtype == "bool":
+        x = (rng.random(rows * cols) < 0.01).astype(np.uint8)
+        ops = ["any", "all", "max", "min", "argmax", "argmin"]
+    else:
+        x = rng.integers(-1000, 1000, rows * cols).astype(NUMPY[dtype])
+        ops = ["sum", "prod", "max", "min", "argmax", "argmin"]
+    p = R.Program()
+    v = p.input(dtype)
+    rec = R.reduce(p, v, ops, rows, cols)
+    plan_types = [o["element_type"] for o in ask_b200.Plan(rec, -1).describe()["port_map"][1:]]
+    got = run_plan(rec, [x], plan_types)
+    want = oracle.reduce(rec, [x])
+    for g, w, op in zip(got, want, ops):
+        assert np.array_equal(g, w), op
+
+
+def test_reduce_with_prologue_program(device):
+    rows, cols = 50, 777
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal(rows * cols).astype(np.float32)
+    w = rng.standard_normal(rows).astype(np.float32)
+    p = R.Program()
+    xv, wv = p.input("f32"), p.input("f32", "outer")
+    val = p.mul(p.abs(p.add(xv, wv)), p.const("f32", 0.5))
+    rec = R.reduce(p, val, ["max", "argmin", "sum"], rows, cols)
+    assert ask_b200.Plan(rec, -1).describe()["kernel"].endswith("generic")
+    got = run_plan(rec, [x, w], ["f32", "i64", "f32"])
+    want = oracle.reduce(rec, [x, w])
+    assert np.array_equal(got[0], want[0]) and np.array_equal(got[1], want[1])
+    ref = np.abs(x.reshape(rows, cols).astype(np.float32) + w[:, None]) * np.float32(0.5)
+    assert np.allclose(got[2], ref.astype(np.float64).sum(axis=1), rtol=1e-6)
+
+
+def test_split_reduction_ignores_stale_scratch(device):
+    x = np.random.default_rng(1).random(1 << 20).astype(np.float32)
+    rec = R.cfg5a_step(x.size)
+    a = run_plan(rec, [x], ["f32", "f32", "i64"], scratch_fill=0xFF)
+    b = run_plan(rec, [x], ["f32", "f32", "i64"], scratch_fill=0x00)
+    assert all(np.array_equal(p, q) for p, q in zip(a, b))  # deterministic, scratch fully overwritten
