@@ -1,7 +1,7 @@
 """ask_b200: B200-native (sm_100a) kernels for ASK's data-parallel hot path.
 
 Python binding of the C ABI in include/ask_b200.h (libask_b200.so, built
-in-tree by ``python -m ask_b200.build``).  A :class:`Plan` is one owned ASK
+in-tree by ``python ask_b200/build.py``).  A :class:`Plan` is one owned ASK
 execution-plan step -- the unit ask::lowerToCUDALLVM compiles and the Runtime's
 step launcher runs (lib/Lowering/CUDA.cpp:152-419, lib/Runtime/CUDA.cpp:360-371)
 -- described by a recipe (see :mod:`ask_b200.recipes`).  Ports are device
@@ -65,7 +65,7 @@ class AskB200Error(RuntimeError):
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIBRARY_PATH):
         raise ImportError(
-            f"{LIBRARY_PATH} is missing: build it with `python -m ask_b200.build` "
+            f"{LIBRARY_PATH} is missing: build it with `python ask_b200/build.py` "
             "(there is no CPU fallback for the ask_b200 kernels)")
     lib = ctypes.CDLL(LIBRARY_PATH)
     for name, (res, args) in _SIGNATURES.items():

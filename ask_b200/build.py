@@ -7,7 +7,8 @@ the CUDA runtime version another framework in the process loaded.
 
 Flags: -gencode arch=compute_100a,code=sm_100a (B200 only), -O3, -lineinfo,
 -fmad=false (ASK forbids multiply-add contraction, docs/en/codegen.md:55-57),
-no fast-math.  Usage: python -m ask_b200.build [--verbose] [--ptxas-info]
+no fast-math.  Usage: python ask_b200/build.py [--verbose] [--ptxas-info]
+(run it as a script: importing the ask_b200 package needs the built library)
 """
 from __future__ import annotations
 

@@ -21,8 +21,11 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def lib_built():
     """Build (or reuse) libask_b200.so; building needs only nvcc, no GPU."""
-    from ask_b200 import build as b
-    b.build()
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("ask_b200_build", os.path.join(ROOT, "ask_b200", "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.build()
     return True
 
 
