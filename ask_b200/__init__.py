@@ -43,6 +43,7 @@ _SIGNATURES = {
     "ask_b200_plan_describe": (ctypes.c_int, [_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     "ask_b200_plan_kernel_launches": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_int)]),
     "ask_b200_plan_launch": (ctypes.c_int, [_p, ctypes.POINTER(_u64), ctypes.c_size_t, _u64, _p]),
+    "ask_b200_plan_launch_noalloc": (ctypes.c_int, [_p, ctypes.POINTER(_u64), ctypes.c_size_t, _p]),
     "ask_b200_comm_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
     "ask_b200_comm_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             ctypes.POINTER(_p)]),
@@ -142,6 +143,12 @@ class Plan:
         None for the legacy default stream)."""
         arr, n = self._ports(inputs, outputs)
         _check(_lib.ask_b200_plan_launch(self._h, arr, n, _ptr(scratch), _stream_handle(stream)))
+
+    def launch_noalloc(self, inputs: Sequence, outputs: Sequence, stream=None) -> None:
+        """Reduce plans only: scratch comes from the library's fixed device
+        array (see ask_b200_plan_launch_noalloc in include/ask_b200.h)."""
+        arr, n = self._ports(inputs, outputs)
+        _check(_lib.ask_b200_plan_launch_noalloc(self._h, arr, n, _stream_handle(stream)))
 
     def launch_sharded(self, comm: "Comm", inputs: Sequence, outputs: Sequence, scratch, stream=None) -> None:
         arr, n = self._ports(inputs, outputs)

@@ -915,6 +915,29 @@ int ask_b200_plan_launch_sharded(const ask_b200_plan* plan, ask_b200_comm* comm,
   });
 }
 
+// Used by the fixed-scratch entry point (noalloc.cu): launch a reduce plan with
+// scratch memory the caller did not allocate, after checking it is large enough.
+int askb_internal_launch_reduce_fixed_scratch(const ask_b200_plan* plan, const uint64_t* ports, size_t n_ports,
+                                              void* scratch, size_t capacity, void* stream) {
+  return guarded([&] {
+    if (!plan) fail(ASK_B200_E_INVALID, "plan is NULL");
+    if (plan->family != FAM_REDUCE)
+      fail(ASK_B200_E_UNSUPPORTED, "the fixed-scratch launch serves reduce plans only");
+    check_ports(*plan, ports, n_ports);
+    check_device(*plan);
+    const size_t needed =
+        plan->strategy == RS_SPLIT ? red_split_scratch_bytes(plan->grid, plan->red.n_red) * size_t(plan->red.outer) : 0;
+    if (needed > capacity)
+      fail(ASK_B200_E_INVALID, "plan needs " + std::to_string(needed) + " bytes of scratch; the fixed scratch array "
+                               "holds at most " + std::to_string(capacity) + " bytes (use ask_b200_plan_launch "
+                               "with caller-provided scratch)");
+    launch_plan(*plan, ports, needed ? reinterpret_cast<uint64_t>(scratch) : 0, static_cast<cudaStream_t>(stream),
+                nullptr);
+  });
+}
+
+void askb_internal_set_error(const char* message) { g_last_error = message ? message : ""; }
+
 int ask_b200_generate(int kind, uint64_t seed, uint32_t stream_id, uint64_t offset, uint64_t count, double p0,
                       double p1, uint64_t dst, void* stream) {
   return guarded([&] {

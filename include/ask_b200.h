@@ -105,6 +105,28 @@ ASK_B200_API int ask_b200_plan_launch(const ask_b200_plan *plan, const uint64_t 
                          void *stream);
 
 /*
+ * Launch a reduce plan without any allocation by the caller or the library.
+ * This entry point has no counterpart in the reference.  It exists for callers
+ * that cannot call cudaMalloc when they launch: code running while a CUDA graph
+ * is captured in global mode, callers whose device memory is wholly pre-planned
+ * by a framework pool, and hosts with a fixed device-memory budget.  A split
+ * reduction's scratch (one partial record per CTA) then comes from a
+ * file-scope device array of ASK_B200_NOALLOC_SCRATCH_BYTES (1 MiB) that every
+ * GPU loading this library holds until the process exits; plans needing more
+ * scratch (ask_b200_plan_scratch_bytes beyond the partial records of
+ * outer * grid * reductions * 16 bytes) are rejected with ASK_B200_E_INVALID.
+ * Only reduce plans are accepted (others: ASK_B200_E_UNSUPPORTED).  The first
+ * call on a device looks up the array's address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls share the array, which
+ * keeps the last call's contents (the kernels overwrite every record they
+ * read), so calls that overlap on the GPU race and must be serialised by the
+ * caller.  Ports and stream are as for ask_b200_plan_launch.
+ */
+#define ASK_B200_NOALLOC_SCRATCH_BYTES (1u << 20)
+ASK_B200_API int ask_b200_plan_launch_noalloc(const ask_b200_plan *plan, const uint64_t *ports, size_t n_ports,
+                                              void *stream);
+
+/*
  * Sharded plans.  A reduce plan whose outputs are 0-D may be split along its
  * leading axis across ranks (one process per GPU): every rank builds the plan
  * for its own slice with "index_base" set to the slice's global offset, and
