@@ -111,6 +111,94 @@ __global__ void __launch_bounds__(kEwThreads)
   }
 }
 
+// ---- hand-written functor kernels for the hottest programs ------------------------
+// Software-pipelined grid-stride loop over whole 16-byte units: the loads of the
+// next unit are in flight while the current unit is computed, so latency is
+// hidden without depending on other warps.  Used only when every port is
+// 16-byte aligned and the element count is a multiple of the unit; the
+// interpreter kernels above serve every other case.
+template <class F>
+__global__ void __launch_bounds__(kEwThreads) ew_functor_kernel(const __grid_constant__ EwArgs a, uint64_t units) {
+  const uint64_t stride = uint64_t(gridDim.x) * kEwThreads;
+  uint64_t u = uint64_t(blockIdx.x) * kEwThreads + threadIdx.x;
+  if (u >= units) return;
+  typename F::In cur = F::load(a, u), nxt;
+  for (; u < units; u += stride) {
+    const uint64_t un = u + stride;
+    if (un < units) nxt = F::load(a, un);
+    F::store(a, u, F::compute(a, cur));
+    cur = nxt;
+  }
+}
+
+// ProgCfg1: y0 = exp(a)*b + c ; y1 = maximum(a, b) + tanh(c)*(-1), 4 elements per unit.
+struct FnCfg1 {
+  static constexpr int V = 4;
+  static constexpr bool kRowMapped = false;
+  struct In { uint4 a, b, c; };
+  struct Out { float y0[4], y1[4]; };
+  __device__ static In load(const EwArgs& e, uint64_t u) {
+    return In{ld_stream_v4(static_cast<const uint4*>(e.in[0]) + u), ld_stream_v4(static_cast<const uint4*>(e.in[1]) + u),
+              ld_stream_v4(static_cast<const uint4*>(e.in[2]) + u)};
+  }
+  __device__ static Out compute(const EwArgs&, const In& x) {
+    const float a[4] = {__uint_as_float(x.a.x), __uint_as_float(x.a.y), __uint_as_float(x.a.z), __uint_as_float(x.a.w)};
+    const float b[4] = {__uint_as_float(x.b.x), __uint_as_float(x.b.y), __uint_as_float(x.b.z), __uint_as_float(x.b.w)};
+    const float c[4] = {__uint_as_float(x.c.x), __uint_as_float(x.c.y), __uint_as_float(x.c.z), __uint_as_float(x.c.w)};
+    Out o;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      o.y0[v] = __fadd_rn(__fmul_rn(expf(a[v]), b[v]), c[v]);
+      o.y1[v] = __fadd_rn(ask_maximum(a[v], b[v]), __fmul_rn(tanhf(c[v]), -1.0f));
+    }
+    return o;
+  }
+  __device__ static void store(const EwArgs& e, uint64_t u, const Out& o) {
+    st_stream_v4(static_cast<uint4*>(e.out[0]) + u, make_uint4(__float_as_uint(o.y0[0]), __float_as_uint(o.y0[1]),
+                                                                __float_as_uint(o.y0[2]), __float_as_uint(o.y0[3])));
+    st_stream_v4(static_cast<uint4*>(e.out[1]) + u, make_uint4(__float_as_uint(o.y1[0]), __float_as_uint(o.y1[1]),
+                                                                __float_as_uint(o.y1[2]), __float_as_uint(o.y1[3])));
+  }
+};
+
+// ProgSoftmaxNorm<T>: y = cast(exp(cast(x, f32) + m*(-1)) / s, T), 8 elements per
+// unit; m and s are indexed by the row (unit*8 / inner).
+template <int T>
+struct FnSoftmaxNorm {
+  static constexpr int V = 8;
+  static constexpr bool kRowMapped = true;  // m, s are indexed by unit*8 / inner
+  struct In { uint4 x; float nm, s; };
+  using Out = uint4;
+  __device__ static float widen(uint32_t h) {
+    if constexpr (T == kF16) return __half2float(__ushort_as_half(uint16_t(h)));
+    else return __uint_as_float(h << 16);
+  }
+  __device__ static uint32_t narrow(float f) {
+    if constexpr (T == kF16) return __half_as_ushort(__float2half_rn(f));
+    else return bf16_bits_rne(f);
+  }
+  __device__ static In load(const EwArgs& e, uint64_t u) {
+    const uint64_t row = udiv(u * V, e.inner);
+    return In{ld_stream_v4(static_cast<const uint4*>(e.in[0]) + u),
+              __fmul_rn(__ldg(static_cast<const float*>(e.in[1]) + row), -1.0f),
+              __ldg(static_cast<const float*>(e.in[2]) + row)};
+  }
+  __device__ static Out compute(const EwArgs&, const In& x) {
+    const uint32_t w[4] = {x.x.x, x.x.y, x.x.z, x.x.w};
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = __fdiv_rn(expf(__fadd_rn(widen(w[j] & 0xffffu), x.nm)), x.s);
+      const float hi = __fdiv_rn(expf(__fadd_rn(widen(w[j] >> 16), x.nm)), x.s);
+      r[j] = narrow(lo) | (narrow(hi) << 16);
+    }
+    return make_uint4(r[0], r[1], r[2], r[3]);
+  }
+  __device__ static void store(const EwArgs& e, uint64_t u, const Out& o) {
+    st_stream_v4(static_cast<uint4*>(e.out[0]) + u, o);
+  }
+};
+
 template <class P>
 struct EwSpecKernels {
   static constexpr int kV = 4, kU = 2;
@@ -119,10 +207,10 @@ struct EwSpecKernels {
 
 void* ew_kernel_ptr(int spec) {
   switch (spec) {
-    case EW_CFG1: return EwSpecKernels<ProgCfg1>::vec();
+    case EW_CFG1: return reinterpret_cast<void*>(&ew_functor_kernel<FnCfg1>);
     case EW_CFG5B: return EwSpecKernels<ProgCfg5b>::vec();
-    case EW_SOFTMAX_NORM_F16: return EwSpecKernels<ProgSoftmaxNorm<kF16>>::vec();
-    case EW_SOFTMAX_NORM_BF16: return EwSpecKernels<ProgSoftmaxNorm<kBF16>>::vec();
+    case EW_SOFTMAX_NORM_F16: return reinterpret_cast<void*>(&ew_functor_kernel<FnSoftmaxNorm<kF16>>);
+    case EW_SOFTMAX_NORM_BF16: return reinterpret_cast<void*>(&ew_functor_kernel<FnSoftmaxNorm<kBF16>>);
     default: return reinterpret_cast<void*>(&ew_generic_kernel<4>);
   }
 }
@@ -145,9 +233,26 @@ cudaError_t ew_occupancy(int spec, int* blocks_per_sm) {
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, ew_kernel_ptr(spec), kEwThreads, 0);
 }
 
+template <class F>
+bool functor_ok(const EwArgs& a, int aligned) {
+  return aligned && a.count % F::V == 0 && (!F::kRowMapped || a.inner.d % F::V == 0);
+}
+
 cudaError_t ew_launch(int spec, const Program& prog, const EwArgs& args, int aligned, int grid, cudaStream_t stream) {
   if (args.count == 0) return cudaSuccess;
   const dim3 g(grid), b(kEwThreads);
+  if (spec == EW_CFG1 && functor_ok<FnCfg1>(args, aligned)) {
+    ew_functor_kernel<FnCfg1><<<g, b, 0, stream>>>(args, args.count / FnCfg1::V);
+    return cudaGetLastError();
+  }
+  if (spec == EW_SOFTMAX_NORM_F16 && functor_ok<FnSoftmaxNorm<kF16>>(args, aligned)) {
+    ew_functor_kernel<FnSoftmaxNorm<kF16>><<<g, b, 0, stream>>>(args, args.count / 8);
+    return cudaGetLastError();
+  }
+  if (spec == EW_SOFTMAX_NORM_BF16 && functor_ok<FnSoftmaxNorm<kBF16>>(args, aligned)) {
+    ew_functor_kernel<FnSoftmaxNorm<kBF16>><<<g, b, 0, stream>>>(args, args.count / 8);
+    return cudaGetLastError();
+  }
   switch (spec) {
     case EW_CFG1:
       ew_spec_kernel<ProgCfg1, 4, 2><<<g, b, 0, stream>>>(args, aligned);

@@ -22,12 +22,36 @@ enum EwSpec : int {
   EW_NUM_SPECS
 };
 
+// Division by a run-time invariant divisor d with a multiply-high and shifts
+// (Granlund & Montgomery, "Division by Invariant Integers using
+// Multiplication", PLDI 1994, unsigned case): for dividends below 2^32,
+//   t = mulhi32(m, n); q = (t + ((n - t) >> s1)) >> s2
+// with l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1, s1 = min(l, 1),
+// s2 = max(l - 1, 0).  `wide` falls back to 64-bit division.
+struct U32Div {
+  uint64_t d;
+  uint32_t m, s1, s2, wide;
+};
+
 struct EwArgs {
   const void* in[kMaxIn];
   void* out[kMaxOut];
   uint64_t count;
-  uint64_t inner;  // IM_OUTER / IM_INNER divisor
+  U32Div inner;  // IM_OUTER / IM_INNER divisor
 };
+
+inline U32Div make_u32div(uint64_t d, uint64_t max_dividend) {
+  U32Div q{d ? d : 1, 0, 0, 0, 1};
+  if (d == 0 || d > 0xffffffffull || max_dividend > 0xffffffffull) return q;
+  uint32_t l = 0;
+  while ((uint64_t(1) << l) < d) ++l;
+  const unsigned __int128 num = ((unsigned __int128)1 << 32) * ((unsigned __int128)((uint64_t(1) << l) - d));
+  q.m = uint32_t(uint64_t(num / d) + 1);
+  q.s1 = l < 1 ? l : 1;
+  q.s2 = l > 1 ? l - 1 : 0;
+  q.wide = 0;
+  return q;
+}
 
 bool ew_spec_program(int spec, Program* out);
 cudaError_t ew_occupancy(int spec, int* blocks_per_sm);

@@ -519,7 +519,8 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   if (forced == "warp_row" && inner == 1) pl.strategy = RS_WARP_ROW;
   // Specialisation.
   pl.spec = RED_GENERIC;
-  if (pl.strategy != RS_COLUMN)
+  // The specialised kernels index elements of a row with 32 bits.
+  if (pl.strategy != RS_COLUMN && extent <= (uint64_t(1) << 32))
     for (int s = 1; s < RED_NUM_SPECS; ++s) {
       Program sp{};
       int nr = 0;
@@ -652,7 +653,7 @@ void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratc
         aligned &= aligned16(ports[ni + k]);
       }
       a.count = pl.count;
-      a.inner = pl.inner ? pl.inner : 1;
+      a.inner = make_u32div(pl.inner ? pl.inner : 1, pl.count);
       check_cuda(ew_launch(pl.spec, pl.prog, a, aligned ? 1 : 0, pl.grid, st), "elementwise launch");
       break;
     }

@@ -9,8 +9,17 @@
 #include <stdint.h>
 
 #include "ask_numerics.cuh"
+#include "kernels.h"
 
 namespace askb {
+
+__device__ __forceinline__ uint64_t udiv(uint64_t n, const U32Div& q) {
+  if (q.wide) return n / q.d;
+  const uint32_t x = uint32_t(n);
+  const uint32_t t = __umulhi(x, q.m);
+  return (t + ((x - t) >> q.s1)) >> q.s2;
+}
+__device__ __forceinline__ uint64_t umod(uint64_t n, const U32Div& q) { return n - udiv(n, q) * q.d; }
 
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   uint4 r;
@@ -149,39 +158,30 @@ __device__ __forceinline__ void store_unit_rt(int t, void* p, uint64_t base, con
 }
 
 // ---- ports: typed, index-mapped unit access -----------------------------------
-__device__ __forceinline__ uint64_t map_index(int map, uint64_t i, uint64_t inner) {
-  switch (map) {
-    case IM_FULL: return i;
-    case IM_SCALAR: return 0;
-    case IM_OUTER: return i / inner;
-    default: return i % inner;
-  }
-}
-
 // Load V elements of an input for the aligned unit starting at `base`.
 // `vec` is true when the unit is complete and the port is 16-byte aligned.
 template <int T, int MAP, int V>
-__device__ __forceinline__ void load_port(const void* p, uint64_t base, uint64_t n, uint64_t inner, bool vec,
+__device__ __forceinline__ void load_port(const void* p, uint64_t base, uint64_t n, const U32Div& inner, bool vec,
                                           uint64_t (&w)[V]) {
   if constexpr (MAP == IM_SCALAR) {
     const uint64_t s = word_from_storage(T, p, 0);
 #pragma unroll
     for (int v = 0; v < V; ++v) w[v] = s;
   } else if constexpr (MAP == IM_OUTER) {
-    if (vec && inner % V == 0) {
-      const uint64_t s = word_from_storage(T, p, base / inner);
+    if (vec && inner.d % V == 0) {
+      const uint64_t s = word_from_storage(T, p, udiv(base, inner));
 #pragma unroll
       for (int v = 0; v < V; ++v) w[v] = s;
     } else {
 #pragma unroll
-      for (int v = 0; v < V; ++v) w[v] = (base + v < n) ? word_from_storage(T, p, (base + v) / inner) : 0;
+      for (int v = 0; v < V; ++v) w[v] = (base + v < n) ? word_from_storage(T, p, udiv(base + v, inner)) : 0;
     }
   } else if constexpr (MAP == IM_INNER) {
     if constexpr (V > 1 && (V * dtype_bytes(T)) % 4 == 0) {
-      if (vec && inner % V == 0) { load_unit<T, V>(p, base % inner, w); return; }
+      if (vec && inner.d % V == 0) { load_unit<T, V>(p, umod(base, inner), w); return; }
     }
 #pragma unroll
-    for (int v = 0; v < V; ++v) w[v] = (base + v < n) ? word_from_storage(T, p, (base + v) % inner) : 0;
+    for (int v = 0; v < V; ++v) w[v] = (base + v < n) ? word_from_storage(T, p, umod(base + v, inner)) : 0;
   } else {
     if constexpr (V > 1 && (V * dtype_bytes(T)) % 4 == 0) {
       if (vec) { load_unit<T, V>(p, base, w); return; }
@@ -202,8 +202,8 @@ __device__ __forceinline__ void store_port(void* p, uint64_t base, uint64_t n, b
 }
 
 template <int V>
-__device__ __forceinline__ void rt_load(int t, int map, const void* p, uint64_t base, uint64_t n, uint64_t inner,
-                                        bool vec, uint64_t (&w)[V]) {
+__device__ __forceinline__ void rt_load(int t, int map, const void* p, uint64_t base, uint64_t n,
+                                        const U32Div& inner, bool vec, uint64_t (&w)[V]) {
 #define ASKB_LOAD_MAP(T)                                                         \
   switch (map) {                                                                 \
     case IM_FULL: load_port<T, IM_FULL, V>(p, base, n, inner, vec, w); break;    \

@@ -384,6 +384,7 @@ def main():
 
     peak, peak_kind = peaks()
     kernels = []
+    grids = [pl.describe()["launch"]["grid"][0] for pl in w.plans]
     for (name, nbytes, _), ms in zip(w.kernels, per_kernel_ms):
         gbs = nbytes / (ms * 1e-3) / 1e9
         kernels.append({"kernel": name, "bytes_per_launch": nbytes, "ms": round(ms, 4), "gbs": round(gbs, 1),
@@ -406,6 +407,7 @@ def main():
         cpu = {"value": round(bps / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
                "sample": desc + f", {secs:.1f} s timed", "cpu": cpu_model()}
 
+    w.config["grids"] = grids
     line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded Philox4x32-10)",
@@ -524,6 +526,7 @@ def reference_arm(args, world, rank):
         bps, secs, desc = cpu_sample(args.workload, threads, budget_s=2.0)
         vals.append(bps / 1e9)
     value = statistics.median(vals)
+    w.config["grids"] = grids
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "impl": "reference", "vs_baseline": None,
             "data": "synthetic (seeded Philox4x32-10)", "config": {"workload": args.workload},

@@ -142,6 +142,11 @@ def test_cfg2_edges(device, rows, cols):
     if rows > 2:
         x[cols * 2 + min(5, cols - 1)] = np.nan
         x[cols * 2 + cols - 1] = np.nan
+    if rows > 1 and cols > 2:  # infinities without NaN: exact refold of that row's values
+        x[cols + 1] = np.inf
+        x[cols + 2] = -np.inf
+    if rows > 4:
+        x[cols * 4:cols * 5] = -0.0  # an all negative-zero row: max/min must be -0, argmax/argmin 0
     outs = run_plan(R.cfg2_step(rows, cols), [x], ["f32", "f32", "f32", "i64"])
     check_rowstats(x, rows, cols, outs)
 
@@ -291,6 +296,23 @@ def test_cfg5a_against_oracle(device, n):
     gs, gm, ga = float(outs[0].item()), float(outs[1].item()), int(outs[2].item())
     assert abs(gs - s64) <= 2.0 ** -20 * s64 + 1e-30
     assert gm == mn and ga == am
+
+
+@pytest.mark.parametrize("special", ["inf", "-inf", "negzero"])
+def test_cfg5a_specials(device, special):
+    x = np.random.default_rng(1).random(300001).astype(np.float32) + 1.0
+    if special == "inf":
+        x[123457] = np.inf
+    elif special == "-inf":
+        x[200000] = -np.inf
+        x[200003] = -np.inf
+    else:
+        x[77777] = -0.0
+        x[99999] = 0.0
+    s, m, a = run_plan(R.cfg5a_step(x.size), [x], ["f32", "f32", "i64"])
+    s64, _, mn, am = oracle.cfg5a(x)
+    assert same_with_nan(m, np.array([mn], np.float32)) and a[0] == am
+    assert (np.isinf(s[0]) and np.isinf(s64)) or abs(float(s[0]) - s64) <= 2.0 ** -20 * abs(s64)
 
 
 def test_cfg5a_nan_wins_first(device):
@@ -500,3 +522,21 @@ def test_split_reduction_ignores_stale_scratch(device):
     a = run_plan(rec, [x], ["f32", "f32", "i64"], scratch_fill=0xFF)
     b = run_plan(rec, [x], ["f32", "f32", "i64"], scratch_fill=0x00)
     assert all(np.array_equal(p, q) for p, q in zip(a, b))  # deterministic, scratch fully overwritten
+
+
+@pytest.mark.parametrize("inner", [1, 3, 4, 7, 1000, 4096])
+@pytest.mark.parametrize("offset", [0, 4])
+def test_elementwise_index_maps(device, inner, offset):
+    rows = 37
+    n = rows * inner
+    rng = np.random.default_rng(inner + offset)
+    p = R.Program()
+    x, r, c, s = p.input("f32"), p.input("f32", "outer"), p.input("f32", "inner"), p.input("f32", "scalar")
+    y = p.add(p.mul(x, r), p.mul(c, s))
+    z = p.maximum(p.add(x, c), r)
+    rec = R.elementwise(p, [y, z], n, inner=inner)
+    ins = [rng.standard_normal(n).astype(np.float32), rng.standard_normal(rows).astype(np.float32),
+           rng.standard_normal(inner).astype(np.float32), np.array([1.5], np.float32)]
+    got = run_plan(rec, ins, ["f32", "f32"], offset_bytes=offset)
+    want = oracle.elementwise(rec, ins)
+    assert same_with_nan(got[0], want[0]) and same_with_nan(got[1], want[1])
