@@ -339,6 +339,10 @@ struct FastAcc {
   float fs;
   uint32_t kmax, kmin;
   uint32_t amax_k, amax_i, amin_k, amin_i;
+  // fast (all-finite) path: float extremes and arg candidates, folded into the
+  // key fields above by fast_settle once a span's vector part is done
+  float vmax, vmin, bmax, bmin;
+  uint32_t bmax_i, bmin_i;
 };
 
 __device__ __forceinline__ void fast_init(FastAcc& s) {
@@ -346,6 +350,8 @@ __device__ __forceinline__ void fast_init(FastAcc& s) {
   s.kmax = 0u; s.kmin = 0xffffffffu;
   s.amax_k = 0u; s.amax_i = 0xffffffffu;
   s.amin_k = 0xffffffffu; s.amin_i = 0xffffffffu;
+  s.vmax = -INFINITY; s.vmin = INFINITY; s.bmax = -INFINITY; s.bmin = INFINITY;
+  s.bmax_i = 0xffffffffu; s.bmin_i = 0xffffffffu;
 }
 
 template <class R>
@@ -397,40 +403,39 @@ __device__ __forceinline__ void fast_fold_full(FastAcc& s, const float (&x)[V], 
 #pragma unroll
     for (int v = 0; v < V; ++v) s.fs = __fmaf_rn(x[v], 0.0f, s.fs);  // NaN once any value is not finite
   }
-  uint32_t k[V];
-#pragma unroll
-  for (int v = 0; v < V; ++v) k[v] = fkey(x[v]);
+  // With finite values fmaxf/fminf (FMNMX) are llvm.maximum/minimum: on sm_100
+  // they order -0 below +0 in either operand order (pinned by the GPU tests
+  // whose extrema are zeros of both signs).  Ordered compares tie -0 with +0,
+  // as the reference's argmax/argmin do.
   if constexpr (set_has<R, RED_MAX>() || set_has<R, RED_ARGMAX>()) {
-    uint32_t m = k[0];
+    float m = x[0];
 #pragma unroll
-    for (int v = 1; v < V; ++v) m = max(m, k[v]);
-    if constexpr (set_has<R, RED_MAX>()) s.kmax = max(s.kmax, m);
+    for (int v = 1; v < V; ++v) m = fmaxf(m, x[v]);
+    if constexpr (set_has<R, RED_MAX>()) s.vmax = fmaxf(s.vmax, m);
     if constexpr (set_has<R, RED_ARGMAX>()) {
-      const uint32_t mc = canon_key(m);
-      if (mc > s.amax_k) {
+      if (m > s.bmax) {
         uint32_t pos = V - 1;
 #pragma unroll
         for (int v = V - 1; v >= 0; --v)
-          if (canon_key(k[v]) == mc) pos = v;
-        s.amax_k = mc;
-        s.amax_i = idx0 + pos;
+          if (x[v] == m) pos = v;
+        s.bmax = m;
+        s.bmax_i = idx0 + pos;
       }
     }
   }
   if constexpr (set_has<R, RED_MIN>() || set_has<R, RED_ARGMIN>()) {
-    uint32_t m = k[0];
+    float m = x[0];
 #pragma unroll
-    for (int v = 1; v < V; ++v) m = min(m, k[v]);
-    if constexpr (set_has<R, RED_MIN>()) s.kmin = min(s.kmin, m);
+    for (int v = 1; v < V; ++v) m = fminf(m, x[v]);
+    if constexpr (set_has<R, RED_MIN>()) s.vmin = fminf(s.vmin, m);
     if constexpr (set_has<R, RED_ARGMIN>()) {
-      const uint32_t mc = canon_key(m);
-      if (mc < s.amin_k) {
+      if (m < s.bmin) {
         uint32_t pos = V - 1;
 #pragma unroll
         for (int v = V - 1; v >= 0; --v)
-          if (canon_key(k[v]) == mc) pos = v;
-        s.amin_k = mc;
-        s.amin_i = idx0 + pos;
+          if (x[v] == m) pos = v;
+        s.bmin = m;
+        s.bmin_i = idx0 + pos;
       }
     }
   }
@@ -452,6 +457,20 @@ __device__ __forceinline__ bool fast_all_finite(const FastAcc& s) {
   } else {
     return true;
   }
+}
+
+// Move the fast path's float state into the key fields.  Returns false when
+// the span must be refolded exactly because a value was not finite.
+template <class R>
+__device__ __forceinline__ bool fast_settle(FastAcc& s) {
+  if (!fast_all_finite<R>(s)) return false;
+  if constexpr (set_has<R, RED_MAX>()) s.kmax = max(s.kmax, fkey(s.vmax));
+  if constexpr (set_has<R, RED_MIN>()) s.kmin = min(s.kmin, fkey(s.vmin));
+  if constexpr (set_has<R, RED_ARGMAX>())
+    if (s.bmax_i != 0xffffffffu) { s.amax_k = canon_key(fkey(s.bmax)); s.amax_i = s.bmax_i; }
+  if constexpr (set_has<R, RED_ARGMIN>())
+    if (s.bmin_i != 0xffffffffu) { s.amin_k = canon_key(fkey(s.bmin)); s.amin_i = s.bmin_i; }
+  return true;
 }
 
 // Fold one value (tails).
@@ -651,9 +670,9 @@ __device__ __forceinline__ void span_src(const RedArgs& a, const typename S::Row
       fast_fold_full<R, V>(s, x, uint32_t(e));
     }
     fast_flush(s);
-    if (!fast_all_finite<R>(s)) {
-      // NaN or infinity among this thread's values: refold them exactly
-      // (NaN-aware keys), in the same increasing index order.
+    if (!fast_settle<R>(s)) {
+      // NaN or infinity among this thread's values, or a zero extremum:
+      // refold them exactly (NaN-aware keys) in the same increasing order.
       fast_init(s);
       span_scalar<S, R>(a, rw, row, e0 + uint64_t(t) * V, e1, uint64_t(T) * V, s);
       return;
