@@ -594,7 +594,9 @@ std::string describe(const ask_b200_plan& pl) {
     << ",1,1],\"shared_bytes\":0},\"kernels_per_launch\":" << pl.launches << ",\"scratch_bytes\":" << pl.scratch;
   if (pl.family == FAM_REDUCE) {
     const char* strat[] = {"warp_row", "column", "split"};
-    o << ",\"strategy\":\"" << strat[pl.strategy] << "\",\"shardable\":" << (pl.shardable ? "true" : "false");
+    o << ",\"strategy\":\"" << strat[pl.strategy] << "\",\"shardable\":" << (pl.shardable ? "true" : "false")
+      << ",\"outer\":" << pl.red.outer << ",\"extent\":" << pl.red.extent << ",\"inner\":" << pl.red.inner
+      << ",\"index_base\":" << pl.red.index_base;
   }
   if (pl.family == FAM_ELEMENTWISE || pl.family == FAM_REDUCE)
     o << ",\"specialized\":" << (pl.spec ? "true" : "false") << ",\"registers\":" << int(pl.prog.n_regs);

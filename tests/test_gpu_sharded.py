@@ -1,0 +1,112 @@
+"""Sharded cfg5 on several GPUs (one process per GPU): the all-gather combine of
+ask_b200_plan_launch_sharded must give every rank the single-GPU answer, and
+the i32 shards (no collective) must equal the corresponding slice.  Skipped
+when fewer than two GPUs are visible."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+N = (1 << 26) + 12345
+SEED = 0xA5C5
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    comm = None
+    try:
+        import ask_b200
+        from ask_b200 import recipes as R
+        uid = [ask_b200.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = ask_b200.Comm(uid[0], world, rank, rank)
+        st = torch.cuda.current_stream()
+        b, e = R.shard_range(N, world, rank)
+        x = torch.empty(e - b, dtype=torch.float32, device="cuda")
+        ask_b200.generate(0, SEED, 0, b, e - b, 0.0, 1.0, x, st)
+        if rank == world - 1:
+            x[-5] = 0.0   # a minimum in the last shard ...
+        if rank == 0:
+            x[7] = 0.0    # ... and an earlier one in the first
+        plan = ask_b200.Plan(R.cfg5a_step(e - b, index_base=b), rank)
+        outs = [torch.empty(1, device="cuda"), torch.empty(1, device="cuda"),
+                torch.empty(1, dtype=torch.int64, device="cuda")]
+        scratch = torch.empty(plan.scratch_bytes, dtype=torch.uint8, device="cuda")
+        for _ in range(3):  # repeated launches reuse scratch and records
+            plan.launch_sharded(comm, [x], outs, scratch, st)
+        torch.cuda.synchronize()
+        # the i32 chain on this rank's slice
+        nb = (1 << 24) + 7
+        bb, be = R.shard_range(nb, world, rank)
+        xi = torch.empty(be - bb, dtype=torch.int32, device="cuda")
+        yi = torch.empty_like(xi)
+        ask_b200.generate(4, SEED, 1, bb, be - bb, 0, 0, xi, st)
+        ask_b200.generate(4, SEED, 2, bb, be - bb, 0, 0, yi, st)
+        z = torch.empty_like(xi)
+        ask_b200.Plan(R.cfg5b_step(be - bb), rank).launch([xi, yi], [z], None, st)
+        torch.cuda.synchronize()
+        queue.put((rank, (float(outs[0].item()), float(outs[1].item()), int(outs[2].item())),
+                   (bb, z.cpu().numpy())))
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_sharded_cfg5_matches_single_gpu(device):
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    import ask_b200
+    import oracle
+    from ask_b200 import recipes as R
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        r, red, ew = queue.get(timeout=300)
+        got[r] = (red, ew)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    # single-GPU reference on device 0
+    x = torch.empty(N, dtype=torch.float32, device="cuda:0")
+    ask_b200.generate(0, SEED, 0, 0, N, 0.0, 1.0, x, torch.cuda.current_stream())
+    b_last, _ = R.shard_range(N, world, world - 1)
+    x[N - 5] = 0.0
+    x[7] = 0.0
+    plan = ask_b200.Plan(R.cfg5a_step(N), 0)
+    outs = [torch.empty(1, device="cuda"), torch.empty(1, device="cuda"), torch.empty(1, dtype=torch.int64, device="cuda")]
+    plan.launch([x], outs, torch.empty(plan.scratch_bytes, dtype=torch.uint8, device="cuda"), torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    ref = (float(outs[0].item()), float(outs[1].item()), int(outs[2].item()))
+    assert ref[1] == 0.0 and ref[2] == 7
+    for r in range(world):
+        s, m, a = got[r][0]
+        assert m == ref[1] and a == ref[2]
+        assert abs(s - ref[0]) <= 2.0 ** -20 * ref[0]
+    assert len({got[r][0] for r in range(world)}) == 1  # identical on all ranks
+    nb = (1 << 24) + 7
+    xi = oracle.generate(4, SEED, 1, 0, nb, 0, 0)
+    yi = oracle.generate(4, SEED, 2, 0, nb, 0, 0)
+    z = oracle.cfg5b(xi, yi)
+    for r in range(world):
+        bb, zz = got[r][1]
+        assert np.array_equal(zz, z[bb:bb + zz.size])
