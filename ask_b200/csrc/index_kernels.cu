@@ -204,16 +204,20 @@ cudaError_t gather_launch(const IndexArgs& a, int aligned, int grid, cudaStream_
   return cudaGetLastError();
 }
 
-cudaError_t scatter_add_launch(const IndexArgs& a, int aligned, int grid, cudaStream_t st) {
+cudaError_t scatter_add_launch(const IndexArgs& a, int aligned, int grid, void* scratch, int sms, cudaStream_t st) {
   const int es = dtype_bytes(a.elem_type);
   const uint64_t base_bytes = a.outer * a.dim * a.inner * uint64_t(es);
+  const uint64_t total = a.outer * a.n * a.inner;
+  // the sorted path does its own (partial) pre_copy
+  if (total && a.dim && scratch && aligned && scatter_sorted_ok(a) && ptr_aligned16(a.table) && ptr_aligned16(a.out) &&
+      ptr_aligned16(a.base))
+    return scatter_sorted_launch(a, scratch, sms, st);
   if (a.base != a.out && base_bytes) {
     copy_bytes<<<grid, kIdxThreads, 0, st>>>(a.base, a.out, base_bytes,
                                              ptr_aligned16(a.base) && ptr_aligned16(a.out) ? 1 : 0);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  const uint64_t total = a.outer * a.n * a.inner;
   if (total == 0 || a.dim == 0) return cudaSuccess;
   const uint64_t row_bytes = a.inner * uint64_t(es);
   if (a.elem_type == kF32 && aligned && row_bytes % 16 == 0 && ptr_aligned16(a.table) && ptr_aligned16(a.out) &&

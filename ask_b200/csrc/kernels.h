@@ -117,7 +117,12 @@ struct IndexArgs {
   int elem_type, index_type;
 };
 cudaError_t gather_launch(const IndexArgs& a, int aligned, int grid, cudaStream_t stream);
-cudaError_t scatter_add_launch(const IndexArgs& a, int aligned, int grid, cudaStream_t stream);
+// `scratch` (scatter_sorted_scratch_bytes) enables the sorted path when
+// scatter_sorted_ok holds; without it the element-atomic path runs.
+cudaError_t scatter_add_launch(const IndexArgs& a, int aligned, int grid, void* scratch, int sms, cudaStream_t stream);
+bool scatter_sorted_ok(const IndexArgs& a);
+size_t scatter_sorted_scratch_bytes(const IndexArgs& a);
+cudaError_t scatter_sorted_launch(const IndexArgs& a, void* scratch, int sms, cudaStream_t stream);
 
 // ---- input synthesis (Philox4x32-10) -------------------------------------------------
 enum GenKind : int { GEN_UNIFORM_F32 = 0, GEN_NORMAL_F32, GEN_NORMAL_F16, GEN_NORMAL_BF16, GEN_I32, GEN_ZIPF_I64, GEN_ZIPF_I32 };

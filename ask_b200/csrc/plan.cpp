@@ -575,12 +575,14 @@ void build_index(ask_b200_plan& pl, const json::Value& r, bool scatter) {
     if (a.elem_type == kBool) fail(ASK_B200_E_INVALID, "scatter_add needs a numeric type");
     pl.inputs = {{a.elem_type, table, IM_FULL}, {a.index_type, a.n, IM_FULL}, {a.elem_type, rows, IM_FULL}};
     pl.outputs = {{a.elem_type, table, IM_FULL}};
-    pl.kernel = a.elem_type == kF32 ? "scatter_add_rows_f32v" : "scatter_add_elems";
+    pl.kernel = scatter_sorted_ok(a) ? "scatter_add_sorted_rows" :
+                a.elem_type == kF32 ? "scatter_add_rows_f32v" : "scatter_add_elems";
+    if (scatter_sorted_ok(a)) pl.scratch = scatter_sorted_scratch_bytes(a);
     if (const json::Value* pc = r.get("pre_copy")) {
       if (pc->at("input").as_int("pre_copy.input") != 0 || pc->at("output").as_int("pre_copy.output") != 0)
         fail(ASK_B200_E_INVALID, "pre_copy must copy input 0 (base) to output 0");
     }
-    pl.launches = (table ? 1 : 0) + (rows && a.dim ? 1 : 0);
+    pl.launches = (table ? 1 : 0) + (rows && a.dim ? (scatter_sorted_ok(a) ? 8 : 1) : 0);
   }
   pl.grid = pl.num_sms * 8;
 }
@@ -691,7 +693,10 @@ void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratc
       a.index = reinterpret_cast<const void*>(ports[1]);
       a.table = reinterpret_cast<const void*>(ports[2]);
       a.out = reinterpret_cast<void*>(ports[3]);
-      check_cuda(scatter_add_launch(a, 1, pl.grid, st), "scatter_add launch");
+      if (pl.scratch && !scratch) fail(ASK_B200_E_INVALID, "this plan needs scratch memory");
+      if (scratch && !aligned16(scratch)) fail(ASK_B200_E_INVALID, "scratch must be 16-byte aligned");
+      check_cuda(scatter_add_launch(a, 1, pl.grid, reinterpret_cast<void*>(scratch), pl.num_sms, st),
+                 "scatter_add launch");
       break;
     }
     default:

@@ -196,7 +196,7 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         w.dtype = dt
         w.e2e = {"inputs": [x], "results": [y]}
     elif name in ("cfg4g", "cfg4s"):
-        rows, dim, n = 1 << 20, 256, 1 << 23
+        rows, dim, n = 1 << 20, 256, (1 << 21) if small else (1 << 23)
         idx = gen(5, SEED["cfg4"], 1, n, 1.1, rows, torch.int64)
         if name == "cfg4g":
             table = gen(1, SEED["cfg4"], 0, rows * dim, 0.0, 0.02, torch.float32)
@@ -213,8 +213,9 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
             base = torch.zeros(rows * dim, dtype=torch.float32, device=dev)
             out = torch.empty_like(base)
             p = ask_b200.Plan(R.cfg4_scatter_step(rows, dim, n), rank_device())
-            w.kernels = [("scatter_add_rows_f32v", 8 * n + 4 * n * dim + 8 * rows * dim,
-                          lambda: p.launch([base, idx, grad], [out], None, st))]
+            scratch = torch.empty(max(p.scratch_bytes, 16), dtype=torch.uint8, device=dev)
+            w.kernels = [("scatter_add_sorted_rows", 8 * n + 4 * n * dim + 8 * rows * dim,
+                          lambda: p.launch([base, idx, grad], [out], scratch, st))]
             w.config = {"workload": "cfg4 scatter_add: grad f32 [2^23,256] into zeros [2^20,256], idx Zipf(1.1)",
                         "l2": "8 GiB updates > L2"}
             w.e2e = {"inputs": [base, idx, grad], "results": [out]}
@@ -313,7 +314,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--small", action="store_true", help="cfg5 at 1/16 size (profiling captures only)")
+    ap.add_argument("--small", action="store_true", help="cfg5 at 1/16 size, cfg4 with 2^21 update rows (profiling captures only)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -44,7 +44,7 @@ def host_plan(recipe):
     ("cfg5a", R.cfg5a_step(), "reduce_split_global_f32"),
     ("cfg5b", R.cfg5b_step(), "ew_cfg5b"),
     ("cfg4g", R.cfg4_gather_step(), "gather_rows"),
-    ("cfg4s", R.cfg4_scatter_step(), "scatter_add_rows_f32v"),
+    ("cfg4s", R.cfg4_scatter_step(), "scatter_add_sorted_rows"),
 ])
 def test_config_recipes_select_specialised_kernels(name, recipe, kernel):
     d = host_plan(recipe).describe()

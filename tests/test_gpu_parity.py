@@ -242,14 +242,76 @@ def test_scatter_add_small(device, dtype, inner):
         assert np.array_equal(out, oracle.scatter_add(dtype, base, idx, upd, 1, rows, inner))
 
 
+def _scatter_sorted(dtype, outer, rows, inner, n, in_place, seed, zipf=True):
+    """Runs the sorted scatter path on mixed Zipf-head and uniform indices
+    (with out-of-range ones) and checks it against the oracle."""
+    rng = np.random.default_rng(seed)
+    idx = rng.integers(-2, rows + 2, n).astype(np.int64)
+    if zipf:
+        head = zipf_index(n, rows).cpu().numpy()
+        take = rng.random(n) < 0.5
+        idx[take] = head[take]
+    tdt = {"f32": torch.float32, "i32": torch.int32}[dtype]
+    if dtype == "f32":
+        base = rng.standard_normal(outer * rows * inner).astype(np.float32)
+        upd = rng.standard_normal(outer * n * inner).astype(np.float32)
+    else:
+        base = rng.integers(-2 ** 31, 2 ** 31 - 1, outer * rows * inner, dtype=np.int32)
+        upd = rng.integers(-2 ** 31, 2 ** 31 - 1, outer * n * inner, dtype=np.int32)
+    plan = ask_b200.Plan(R.scatter_add(dtype, "i64", rows, inner, n, outer=outer), 0)
+    assert plan.describe()["kernel"] == "scatter_add_sorted_rows"
+    d_base = torch.from_numpy(base).cuda()
+    d_out = d_base if in_place else torch.empty_like(d_base)
+    scratch = torch.full((plan.scratch_bytes,), 0x5A, dtype=torch.uint8, device="cuda")
+    plan.launch([d_base, torch.from_numpy(idx).cuda(), torch.from_numpy(upd).cuda()], [d_out], scratch,
+                torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    out = d_out.cpu().numpy()
+    del d_base, d_out, scratch
+    if dtype == "f32":
+        ref64, abs64 = oracle.scatter_add_f64(base, idx, upd, outer, rows, inner)
+        assert np.all(np.abs(out - ref64) <= 2.0 ** -20 * (abs64 + np.abs(base)) + 1e-30)
+    else:
+        assert np.array_equal(out, oracle.scatter_add("i32", base, idx, upd, outer, rows, inner))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "i32"])
+@pytest.mark.parametrize("outer,rows,inner,n,in_place", [
+    (1, 1000, 16, 50000, False),    # 64-byte rows: 4 column vectors, most lanes idle
+    (1, 3000, 300, 20000, False),   # 1200-byte rows: the wide-row variant with a ragged last pass
+    (3, 500, 64, 7000, False),      # outer > 1: row keys o * dim + index
+    (1, 2000, 256, 60000, True),    # in place: out is base, nothing is pre-copied
+    (2, 700, 32, 9000, True),
+])
+def test_scatter_sorted_shapes(device, dtype, outer, rows, inner, n, in_place):
+    _scatter_sorted(dtype, outer, rows, inner, n, in_place, seed=rows + inner)
+
+
+@pytest.mark.parametrize("rows", [(1 << 22) + 1000, (1 << 24) + 5])
+def test_scatter_sorted_large_tables(device, rows):
+    # past 2^22 and 2^24 rows the histogram keeps 2 and then 1 counter copies
+    _scatter_sorted("i32", 1, rows, 16, 1 << 18, False, seed=11)
+
+
+def test_scatter_sorted_no_valid_index(device):
+    rows, inner, n = 300, 64, 5000
+    idx = np.full(n, rows, np.int64)
+    idx[::2] = -1
+    base = np.arange(rows * inner, dtype=np.int32)
+    upd = np.ones(n * inner, np.int32)
+    (out,) = run_plan(R.scatter_add("i32", "i64", rows, inner, n), [base, idx, upd], ["i32"], scratch_fill=0x33)
+    assert np.array_equal(out, base)
+
+
 def test_cfg4_scatter_full_size(device):
     rows, dim, n = 1 << 20, 256, 1 << 23
     idx = zipf_index(n, rows)
     grad = gen_dev(1, 0xA5C4, 2, n * dim, 0.0, 1.0, torch.float32)
     base = torch.zeros(rows * dim, dtype=torch.float32, device="cuda")
     out = torch.empty_like(base)
-    ask_b200.Plan(R.cfg4_scatter_step(rows, dim, n), 0).launch([base, idx, grad], [out], None,
-                                                               torch.cuda.current_stream())
+    plan = ask_b200.Plan(R.cfg4_scatter_step(rows, dim, n), 0)
+    scratch = torch.empty(max(plan.scratch_bytes, 16), dtype=torch.uint8, device="cuda")
+    plan.launch([base, idx, grad], [out], scratch, torch.cuda.current_stream())
     torch.cuda.synchronize()
     sample_rows = [0, 1, 2, 7, 100, 5000, 123456, rows - 1]
     idx_h = idx.cpu().numpy()
@@ -273,8 +335,10 @@ def test_cfg4_scatter_i32_bit_exact(device):
     upd = gen_dev(4, 0xA5C4, 5, n * dim, 0, 0, torch.int32)
     base = gen_dev(4, 0xA5C4, 6, rows * dim, 0, 0, torch.int32)
     out = torch.empty_like(base)
-    ask_b200.Plan(R.cfg4_scatter_step(rows, dim, n, dtype="i32"), 0).launch(
-        [base, idx, upd], [out], None, torch.cuda.current_stream())
+    plan = ask_b200.Plan(R.cfg4_scatter_step(rows, dim, n, dtype="i32"), 0)
+    assert plan.describe()["kernel"] == "scatter_add_sorted_rows"
+    scratch = torch.full((max(plan.scratch_bytes, 16),), 0xA5, dtype=torch.uint8, device="cuda")  # stale contents
+    plan.launch([base, idx, upd], [out], scratch, torch.cuda.current_stream())
     torch.cuda.synchronize()
     want = oracle.scatter_add("i32", base.cpu().numpy(), idx.cpu().numpy(), upd.cpu().numpy(), 1, rows, dim)
     assert np.array_equal(out.cpu().numpy(), want)
