@@ -163,11 +163,23 @@ struct FnCfg1 {
 
 // ProgSoftmaxNorm<T>: y = cast(exp(cast(x, f32) + m*(-1)) / s, T), 8 elements per
 // unit; m and s are indexed by the row (unit*8 / inner).
+//
+// The division is the correctly rounded f32 quotient, computed from the row's
+// correctly rounded reciprocal y = RN(1/s) by Markstein's correction: with
+// q0 = RN(e*y) and two steps r = fma(-q, s, e) (exact when q is within an ulp
+// of e/s and no value is subnormal), q' = fma(r, y, q), the last q equals
+// RN(e/s) (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990).  The
+// theorem's conditions -- s and y normal, a normal quotient -- are checked;
+// a unit that fails them (a zero, subnormal, infinite or NaN operand or
+// result, which softmax rows reach only at their extremes) is recomputed with
+// the IEEE division.  One reciprocal per row replaces one per element, and
+// the division no longer occupies the special-function unit per element.
 template <int T>
 struct FnSoftmaxNorm {
   static constexpr int V = 8;
   static constexpr bool kRowMapped = true;  // m, s are indexed by unit*8 / inner
-  struct In { uint4 x; float nm, s; };
+  struct In { uint4 x; float nm, s, y; };
   using Out = uint4;
   __device__ static float widen(uint32_t h) {
     if constexpr (T == kF16) return __half2float(__ushort_as_half(uint16_t(h)));
@@ -177,20 +189,50 @@ struct FnSoftmaxNorm {
     if constexpr (T == kF16) return __half_as_ushort(__float2half_rn(f));
     else return bf16_bits_rne(f);
   }
+  // Two non-NaN values rounded to nearest-even and packed (lo in bits 0..15):
+  // one cvt.rn.{f16,bf16}x2.f32.  For bf16 this equals bf16_bits_rne on every
+  // non-NaN input; NaN inputs take narrow() (the payload-preserving rule).
+  __device__ static uint32_t narrow2(float lo, float hi) {
+    uint32_t r;
+    if constexpr (T == kF16)
+      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    else
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  }
   __device__ static In load(const EwArgs& e, uint64_t u) {
     const uint64_t row = udiv(u * V, e.inner);
+    const float s = __ldg(static_cast<const float*>(e.in[2]) + row);
     return In{ld_stream_v4(static_cast<const uint4*>(e.in[0]) + u),
-              __fmul_rn(__ldg(static_cast<const float*>(e.in[1]) + row), -1.0f),
-              __ldg(static_cast<const float*>(e.in[2]) + row)};
+              __fmul_rn(__ldg(static_cast<const float*>(e.in[1]) + row), -1.0f), s, __frcp_rn(s)};
   }
   __device__ static Out compute(const EwArgs&, const In& x) {
     const uint32_t w[4] = {x.x.x, x.x.y, x.x.z, x.x.w};
-    uint32_t r[4];
+    float e[8], q[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float lo = __fdiv_rn(expf(__fadd_rn(widen(w[j] & 0xffffu), x.nm)), x.s);
-      const float hi = __fdiv_rn(expf(__fadd_rn(widen(w[j] >> 16), x.nm)), x.s);
-      r[j] = narrow(lo) | (narrow(hi) << 16);
+      e[2 * j] = expf(__fadd_rn(widen(w[j] & 0xffffu), x.nm));
+      e[2 * j + 1] = expf(__fadd_rn(widen(w[j] >> 16), x.nm));
+    }
+    const float s = x.s, y = x.y;
+    bool ok = s >= 0x1p-100f && s <= 0x1p100f;  // s and y = RN(1/s) normal (false for NaN)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float t = __fmul_rn(e[k], y);
+      t = __fmaf_rn(__fmaf_rn(-t, s, e[k]), y, t);
+      t = __fmaf_rn(__fmaf_rn(-t, s, e[k]), y, t);
+      q[k] = t;
+      ok &= (t >= 0x1p-124f && t <= 0x1p126f) || e[k] == 0.0f;
+    }
+    uint32_t r[4];
+    if (ok) {  // every q is finite
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = narrow2(q[2 * j], q[2 * j + 1]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[k] = __fdiv_rn(e[k], s);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = narrow(q[2 * j]) | (narrow(q[2 * j + 1]) << 16);
     }
     return make_uint4(r[0], r[1], r[2], r[3]);
   }
