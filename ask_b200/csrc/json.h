@@ -22,6 +22,7 @@ struct Value {
   double num = 0.0;
   int64_t integer = 0;
   bool is_integer = false;
+  bool negative = false;  // the literal had a minus sign (integer may hold a u64 above INT64_MAX)
   std::string str;
   std::vector<Value> items;
   std::vector<std::pair<std::string, Value>> fields;
@@ -162,6 +163,7 @@ class Parser {
     }
     std::string text(start, p_);
     v.kind = Value::Number;
+    v.negative = text[0] == '-';
     v.num = std::strtod(text.c_str(), nullptr);
     if (integral) {
       errno = 0;

@@ -1,0 +1,272 @@
+"""Runtime layer: sessions, device buffers, prepared programs and events.
+
+Python binding of include/ask_b200_runtime.h.  The names follow the reference
+Runtime's C++ API (include/ask/Runtime/CUDA.h:66-175) so code written against
+``ask::runtime`` reads the same: ``Session.create``, ``allocate``,
+``importBuffer``, ``prepareProgram(sizes, inputs, outputs, steps, graph)``,
+``PreparedProgram.submit/run``, ``DeviceBuffer.pointer/size/readonly/
+copyFromHost/copyToHost``, ``Event.query/wait`` and ``Session.stats``.  A
+:class:`PlanStep` holds an ask_b200 recipe (one owned step, see
+:mod:`ask_b200.recipes`) in place of the reference's loaded cubin kernel.
+
+``check_allocation`` and ``assign_slots`` expose the plan verifier and the
+slot assigners on the host (no GPU needed).
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+from . import AskB200Error, OK, _lib
+
+_p = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_u64 = ctypes.c_uint64
+_TEXT = [ctypes.c_char_p, _sz, ctypes.POINTER(_sz)]
+
+# Every entry point declared in include/ask_b200_runtime.h, with its ctypes signature.
+RUNTIME_SIGNATURES = {
+    "ask_b200_session_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(_p)]),
+    "ask_b200_session_release": (ctypes.c_int, [_p]),
+    "ask_b200_session_synchronize": (ctypes.c_int, [_p]),
+    "ask_b200_session_reap": (ctypes.c_int, [_p]),
+    "ask_b200_session_stream": (ctypes.c_int, [_p, ctypes.POINTER(_p)]),
+    "ask_b200_session_wait_stream": (ctypes.c_int, [_p, _p]),
+    "ask_b200_session_stats": (ctypes.c_int, [_p] + _TEXT),
+    "ask_b200_buffer_allocate": (ctypes.c_int, [_p, _sz, ctypes.POINTER(_p)]),
+    "ask_b200_buffer_import": (ctypes.c_int, [_p, _u64, _sz, ctypes.c_int, ctypes.POINTER(_p)]),
+    "ask_b200_buffer_info": (ctypes.c_int, [_p, ctypes.POINTER(_u64), ctypes.POINTER(_sz), ctypes.POINTER(ctypes.c_int)]),
+    "ask_b200_buffer_copy_from_host": (ctypes.c_int, [_p, _p, _sz]),
+    "ask_b200_buffer_copy_to_host": (ctypes.c_int, [_p, _p, _sz]),
+    "ask_b200_buffer_release": (ctypes.c_int, [_p]),
+    "ask_b200_program_prepare": (ctypes.c_int, [_p, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(_p)]),
+    "ask_b200_program_describe": (ctypes.c_int, [_p] + _TEXT),
+    "ask_b200_program_submit": (ctypes.c_int, [_p, ctypes.POINTER(_p), _sz, ctypes.POINTER(_p), _sz,
+                                               ctypes.POINTER(_p)]),
+    "ask_b200_program_run": (ctypes.c_int, [_p, ctypes.POINTER(_p), _sz, ctypes.POINTER(_p), _sz, ctypes.POINTER(_p)]),
+    "ask_b200_program_release": (ctypes.c_int, [_p]),
+    "ask_b200_event_query": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_int)]),
+    "ask_b200_event_wait": (ctypes.c_int, [_p]),
+    "ask_b200_event_release": (ctypes.c_int, [_p]),
+    "ask_b200_allocation_check": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)] + _TEXT),
+    "ask_b200_allocation_assign": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int] + _TEXT),
+}
+
+for _name, (_res, _args) in RUNTIME_SIGNATURES.items():
+    _fn = getattr(_lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+class CUDAError(AskB200Error):
+    """A failed runtime call (the reference's ask::runtime::CUDAError)."""
+
+
+def _check(status: int) -> None:
+    if status != OK:
+        raise CUDAError(status, _lib.ask_b200_last_error().decode())
+
+
+def _text(fn, *args) -> str:
+    need = _sz()
+    _check(fn(*args, None, 0, ctypes.byref(need)))
+    buf = ctypes.create_string_buffer(need.value)
+    _check(fn(*args, buf, need.value, ctypes.byref(need)))
+    return buf.value.decode()
+
+
+@dataclass
+class PlanStep:
+    """One program step: an ask_b200 recipe bound to logical buffers.
+
+    ``inputs``/``outputs`` bind the recipe's ports in port-map order;
+    ``preCopy`` = (source, destination) is the reference's PlanStep::preCopy.
+    """
+    recipe: dict
+    inputs: Sequence[int]
+    outputs: Sequence[int]
+    preCopy: Optional[tuple] = None
+
+    def to_json(self) -> dict:
+        d = {"recipe": self.recipe if isinstance(self.recipe, str) else json.dumps(self.recipe),
+             "inputs": [int(i) for i in self.inputs], "outputs": [int(o) for o in self.outputs]}
+        if self.preCopy is not None:
+            d["pre_copy"] = {"source": int(self.preCopy[0]), "destination": int(self.preCopy[1])}
+        return d
+
+
+class DeviceBuffer:
+    def __init__(self, handle: _p, session: "Session"):
+        self._h = handle
+        self.session = session
+        ptr, size, ro = _u64(), _sz(), ctypes.c_int()
+        _check(_lib.ask_b200_buffer_info(handle, ctypes.byref(ptr), ctypes.byref(size), ctypes.byref(ro)))
+        self._ptr, self._size, self._ro = ptr.value, size.value, bool(ro.value)
+
+    def pointer(self) -> int:
+        return self._ptr
+
+    def size(self) -> int:
+        return self._size
+
+    def readonly(self) -> bool:
+        return self._ro
+
+    def copyFromHost(self, data) -> None:
+        mv = memoryview(data).cast("B")
+        buf = (ctypes.c_char * len(mv)).from_buffer_copy(mv) if len(mv) else None
+        _check(_lib.ask_b200_buffer_copy_from_host(self._h, buf, len(mv)))
+
+    def copyToHost(self) -> bytes:
+        buf = ctypes.create_string_buffer(self._size)
+        _check(_lib.ask_b200_buffer_copy_to_host(self._h, buf, self._size))
+        return buf.raw[:self._size]
+
+    def __eq__(self, other) -> bool:  # same storage (the reference compares shared_ptr identity)
+        return isinstance(other, DeviceBuffer) and other._ptr == self._ptr and other._size == self._size
+
+    def __hash__(self) -> int:
+        return hash((self._ptr, self._size))
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            _lib.ask_b200_buffer_release(self._h)
+            self._h = None
+
+
+class Event:
+    def __init__(self, handle: _p):
+        self._h = handle
+
+    def query(self) -> bool:
+        done = ctypes.c_int()
+        _check(_lib.ask_b200_event_query(self._h, ctypes.byref(done)))
+        return bool(done.value)
+
+    def wait(self) -> None:
+        _check(_lib.ask_b200_event_wait(self._h))
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            _lib.ask_b200_event_release(self._h)
+            self._h = None
+
+
+def _handles(buffers) -> ctypes.Array:
+    arr = (_p * max(len(buffers), 1))()
+    for i, b in enumerate(buffers):
+        arr[i] = b._h if b is not None else None
+    return arr
+
+
+class PreparedProgram:
+    def __init__(self, handle: _p, session: "Session", n_outputs: int):
+        self._h = handle
+        self.session = session
+        self._n_outputs = n_outputs
+
+    def describe(self) -> dict:
+        return json.loads(_text(_lib.ask_b200_program_describe, self._h))
+
+    def submit(self, inputs: Sequence[DeviceBuffer], outputs: Sequence[DeviceBuffer]) -> Event:
+        ev = _p()
+        _check(_lib.ask_b200_program_submit(self._h, _handles(inputs), len(inputs), _handles(outputs), len(outputs),
+                                            ctypes.byref(ev)))
+        return Event(ev)
+
+    def run(self, inputs: Sequence[DeviceBuffer]):
+        outs = (_p * max(self._n_outputs, 1))()
+        ev = _p()
+        _check(_lib.ask_b200_program_run(self._h, _handles(inputs), len(inputs), outs, self._n_outputs,
+                                         ctypes.byref(ev)))
+        return [DeviceBuffer(_p(outs[i]), self.session) for i in range(self._n_outputs)], Event(ev)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            _lib.ask_b200_program_release(self._h)
+            self._h = None
+
+
+class Session:
+    """One device and its non-blocking stream (ask::runtime::Session)."""
+
+    def __init__(self, handle: _p, device: int):
+        self._h = handle
+        self._device = device
+
+    @staticmethod
+    def create(device: int = 0) -> "Session":
+        h = _p()
+        _check(_lib.ask_b200_session_create(int(device), ctypes.byref(h)))
+        return Session(h, device)
+
+    def device(self) -> int:
+        return self._device
+
+    def allocate(self, nbytes: int) -> DeviceBuffer:
+        h = _p()
+        _check(_lib.ask_b200_buffer_allocate(self._h, int(nbytes), ctypes.byref(h)))
+        return DeviceBuffer(h, self)
+
+    def importBuffer(self, pointer: int, nbytes: int, readonly: bool = False) -> DeviceBuffer:
+        h = _p()
+        _check(_lib.ask_b200_buffer_import(self._h, int(pointer), int(nbytes), 1 if readonly else 0, ctypes.byref(h)))
+        return DeviceBuffer(h, self)
+
+    def importTensor(self, tensor, readonly: bool = False) -> DeviceBuffer:
+        """A torch tensor's storage as a buffer (the tensor must stay alive)."""
+        return self.importBuffer(int(tensor.data_ptr()), tensor.numel() * tensor.element_size(), readonly)
+
+    def prepareProgram(self, sizes: Sequence[int], inputs: Sequence[int], outputs: Sequence[int],
+                       steps: Sequence[PlanStep], graph: bool = False) -> PreparedProgram:
+        text = json.dumps({"buffer_sizes": [int(s) for s in sizes], "inputs": [int(i) for i in inputs],
+                           "outputs": [int(o) for o in outputs], "steps": [s.to_json() for s in steps]})
+        h = _p()
+        _check(_lib.ask_b200_program_prepare(self._h, text.encode(), 1 if graph else 0, ctypes.byref(h)))
+        return PreparedProgram(h, self, len(outputs))
+
+    def stream(self) -> int:
+        s = _p()
+        _check(_lib.ask_b200_session_stream(self._h, ctypes.byref(s)))
+        return s.value or 0
+
+    def waitForExternalStream(self, stream) -> None:
+        handle = stream if isinstance(stream, int) else int(stream.cuda_stream)
+        _check(_lib.ask_b200_session_wait_stream(self._h, handle))
+
+    def synchronize(self) -> None:
+        _check(_lib.ask_b200_session_synchronize(self._h))
+
+    def reap(self) -> None:
+        _check(_lib.ask_b200_session_reap(self._h))
+
+    def stats(self) -> dict:
+        return json.loads(_text(_lib.ask_b200_session_stats, self._h))
+
+    def close(self) -> None:
+        if self._h:
+            _check(_lib.ask_b200_session_release(self._h))
+            self._h = None
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            _lib.ask_b200_session_release(self._h)
+            self._h = None
+
+
+def check_allocation(allocation: dict):
+    """The plan verifier: returns (passed, explanation)."""
+    ok = ctypes.c_int()
+    need = _sz()
+    text = json.dumps(allocation).encode()
+    _check(_lib.ask_b200_allocation_check(text, ctypes.byref(ok), None, 0, ctypes.byref(need)))
+    buf = ctypes.create_string_buffer(need.value)
+    _check(_lib.ask_b200_allocation_check(text, ctypes.byref(ok), buf, need.value, ctypes.byref(need)))
+    return bool(ok.value), buf.value.decode()
+
+
+def assign_slots(plan: dict, graph: bool = False) -> dict:
+    """Slot assignment for a plan with buffer_sizes; returns the allocation fields."""
+    return json.loads(_text(_lib.ask_b200_allocation_assign, json.dumps(plan).encode(), 1 if graph else 0))

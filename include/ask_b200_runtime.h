@@ -1,0 +1,122 @@
+/*
+ * ask_b200_runtime.h -- the runtime layer that hosts ask_b200 plans as the
+ * steps of an execution plan: sessions, device buffers, prepared programs and
+ * completion events.  It mirrors the reference Runtime's C++ surface
+ * (include/ask/Runtime/CUDA.h:66-175; lib/Runtime/CUDA.cpp:679-1005) with a
+ * "recipe step" kind in place of a loaded cubin kernel: each step is an
+ * ask_b200 plan whose ports are bound to logical buffers of the program.
+ *
+ *   Session            one device, one non-blocking stream, usage counters
+ *                      (Session::create / allocate / importBuffer /
+ *                      prepareProgram / synchronize / reap / stats)
+ *   DeviceBuffer       device memory owned by the session or imported
+ *   PreparedProgram    buffer sizes, public inputs/outputs and steps, verified
+ *                      once (the reference's PASS plan check,
+ *                      lib/Pass/Pass.cpp:12-208) with internal buffers mapped
+ *                      to reusable workspace slots; submit() binds the public
+ *                      ports, run() also allocates the outputs
+ *   Event              completion of one submission; it keeps the submission's
+ *                      buffers and workspace alive until the GPU is done
+ *
+ * Graph mode (graph = 1) records each step as a child graph of one CUDA graph
+ * per workspace, with the plan's data dependencies as edges, and replays it;
+ * later submissions whose public addresses changed re-record only the steps
+ * bound to those ports (cudaGraphExecChildGraphNodeSetParams).
+ *
+ * A program is JSON:
+ *   {"buffer_sizes": [bytes, ...], "inputs": [buffer, ...], "outputs": [buffer, ...],
+ *    "steps": [{"recipe": "<ask_b200 recipe JSON text>", "inputs": [buffer, ...],
+ *               "outputs": [buffer, ...], "pre_copy": {"source": b, "destination": b}}]}
+ * A step's inputs and outputs bind the recipe's ports in port-map order; each
+ * bound buffer's size must equal the port's bytes.  A plan that needs scratch
+ * gets a private logical buffer, as the reference does for a cuBLASLt
+ * workspace (lib/Runtime/CUDA.cpp:759-764).  "pre_copy" is the reference's
+ * PlanStep::preCopy (include/ask/Runtime/CUDA.h:50-62): a device-to-device
+ * copy enqueued before the step.  A scatter_add recipe already performs its own
+ * pre-copy (out = base) inside its launch and needs none.
+ *
+ * All entry points return 0 or a negative ASK_B200_E_* status with the
+ * message in ask_b200_last_error() (ask_b200.h).  Handles are reference
+ * counted: *_release drops the caller's handle, and an object lives on while
+ * another object (an event, a program, a buffer) still needs it.
+ */
+#ifndef ASK_B200_RUNTIME_H
+#define ASK_B200_RUNTIME_H
+
+#include "ask_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct ask_b200_session ask_b200_session;
+typedef struct ask_b200_buffer ask_b200_buffer;
+typedef struct ask_b200_program ask_b200_program;
+typedef struct ask_b200_event ask_b200_event;
+
+/* Session::create(device) (lib/Runtime/CUDA.cpp:418-441). */
+ASK_B200_API int ask_b200_session_create(int device, ask_b200_session **out);
+/* Session::close + drop the handle: waits for pending submissions first. */
+ASK_B200_API int ask_b200_session_release(ask_b200_session *session);
+ASK_B200_API int ask_b200_session_synchronize(ask_b200_session *session);
+/* Session::reap: retire completed submissions (their workspaces become idle). */
+ASK_B200_API int ask_b200_session_reap(ask_b200_session *session);
+/* The session's cudaStream_t (Session::stream). */
+ASK_B200_API int ask_b200_session_stream(ask_b200_session *session, void **stream);
+/* Session::waitForExternalStream: later work waits for `stream`'s current tail. */
+ASK_B200_API int ask_b200_session_wait_stream(ask_b200_session *session, void *stream);
+/* Session::stats as a JSON object of counters (written as ask_b200_plan_describe). */
+ASK_B200_API int ask_b200_session_stats(ask_b200_session *session, char *buf, size_t cap, size_t *needed);
+
+/* Session::allocate / importBuffer, DeviceBuffer::pointer/size/readonly/copy*. */
+ASK_B200_API int ask_b200_buffer_allocate(ask_b200_session *session, size_t bytes, ask_b200_buffer **out);
+ASK_B200_API int ask_b200_buffer_import(ask_b200_session *session, uint64_t pointer, size_t bytes, int readonly,
+                                        ask_b200_buffer **out);
+ASK_B200_API int ask_b200_buffer_info(const ask_b200_buffer *buffer, uint64_t *pointer, size_t *bytes, int *readonly);
+ASK_B200_API int ask_b200_buffer_copy_from_host(ask_b200_buffer *buffer, const void *src, size_t bytes);
+ASK_B200_API int ask_b200_buffer_copy_to_host(const ask_b200_buffer *buffer, void *dst, size_t bytes);
+ASK_B200_API int ask_b200_buffer_release(ask_b200_buffer *buffer);
+
+/* Session::prepareProgram(sizes, inputs, outputs, steps, graph). */
+ASK_B200_API int ask_b200_program_prepare(ask_b200_session *session, const char *program_json, int graph,
+                                          ask_b200_program **out);
+/* JSON: slots and capacities, buffer-to-slot assignments, dependencies, step kernels. */
+ASK_B200_API int ask_b200_program_describe(const ask_b200_program *program, char *buf, size_t cap, size_t *needed);
+/* PreparedProgram::submit(inputs, outputs). */
+ASK_B200_API int ask_b200_program_submit(ask_b200_program *program, ask_b200_buffer *const *inputs, size_t n_inputs,
+                                         ask_b200_buffer *const *outputs, size_t n_outputs, ask_b200_event **event);
+/* PreparedProgram::run(inputs): outputs[] receives new handles (an output
+ * that is a program input is that input's buffer). */
+ASK_B200_API int ask_b200_program_run(ask_b200_program *program, ask_b200_buffer *const *inputs, size_t n_inputs,
+                                      ask_b200_buffer **outputs, size_t n_outputs, ask_b200_event **event);
+ASK_B200_API int ask_b200_program_release(ask_b200_program *program);
+
+/* Event::query / Event::wait. */
+ASK_B200_API int ask_b200_event_query(ask_b200_event *event, int *done);
+ASK_B200_API int ask_b200_event_wait(ask_b200_event *event);
+ASK_B200_API int ask_b200_event_release(ask_b200_event *event);
+
+/*
+ * The plan verifier on its own (pass::checkAllocationPlan,
+ * lib/Pass/Pass.h:50-53), host only.  JSON:
+ *   {"buffer_count": n, "public_inputs": [...], "public_outputs": [...],
+ *    "steps": [{"inputs": [...], "outputs": [...]}], "buffer_sizes": [...],
+ *    "assignments": [[buffer, slot], ...], "slot_capacity_bytes": [...],
+ *    "graph": false, "dependencies": [[...], ...]}
+ * *pass is 1 or 0; buf receives the explanation ("" on pass).  Omitting
+ * "buffer_sizes" checks the plan alone (pass::checkPlan).
+ */
+ASK_B200_API int ask_b200_allocation_check(const char *allocation_json, int *pass, char *buf, size_t cap,
+                                           size_t *needed);
+/*
+ * The slot assigners on their own, host only: from the plan fields above plus
+ * "buffer_sizes", write {"assignments": ..., "slot_capacity_bytes": ...,
+ * "dependencies": ...} for stream order (graph = 0) or graph order (graph = 1).
+ */
+ASK_B200_API int ask_b200_allocation_assign(const char *plan_json, int graph, char *buf, size_t cap, size_t *needed);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASK_B200_RUNTIME_H */

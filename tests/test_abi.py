@@ -30,6 +30,27 @@ def test_library_exports_every_declared_symbol(lib_built):
     assert set(names) == set(ask_b200.exported_symbols())
 
 
+def test_runtime_library_exports_every_declared_symbol(lib_built):
+    from ask_b200 import runtime as rt
+    lib = ctypes.CDLL(ask_b200.LIBRARY_PATH)
+    text = open(os.path.join(ROOT, "include", "ask_b200_runtime.h")).read()
+    names = sorted(set(re.findall(r"ASK_B200_API\s+int\s+(ask_b200_[a-z_0-9]+)\s*\(", text)))
+    assert len(names) >= 20
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared in include/ask_b200_runtime.h but not exported"
+    assert set(names) == set(rt.RUNTIME_SIGNATURES)
+
+
+def test_runtime_session_without_gpu_is_an_error():
+    import torch
+    from ask_b200 import runtime as rt
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(rt.CUDAError) as err:
+        rt.Session.create(0)
+    assert err.value.status == ask_b200.E_DEVICE
+
+
 def test_abi_version():
     assert ask_b200.abi_version() == 1
 
