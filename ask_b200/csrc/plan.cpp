@@ -19,7 +19,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cmath>
+#include <functional>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -309,6 +311,49 @@ int operand_count(int op) {
   return 1;  // cast and the unary ops
 }
 
+// Canonical instruction order: every input instruction first (by port, then
+// position), then what the results need, depth first with operands left to
+// right; instructions no result needs are dropped.  Recipes that write the
+// same expression DAG in different textual orders (hand-written, or lowered
+// from a step's MLIR) then get the same program and the same specialised
+// kernel.
+Program canonical(const Program& p) {
+  std::vector<int> id(p.n_insn, -1);
+  Program q = p;
+  q.n_insn = 0;
+  auto remap = [&](Insn x) {
+    const int n = operand_count(x.op);
+    if (n >= 1) x.a = uint8_t(id[x.a]);
+    if (n >= 2) x.b = uint8_t(id[x.b]);
+    if (n >= 3) x.c = uint8_t(id[x.c]);
+    return x;
+  };
+  auto push = [&](int i) {
+    Insn x = remap(p.insn[i]);
+    x.dst = q.n_insn;
+    id[i] = q.n_insn;
+    q.insn[q.n_insn++] = x;
+  };
+  std::vector<int> inputs;
+  for (int i = 0; i < p.n_insn; ++i)
+    if (p.insn[i].op == OP_INPUT) inputs.push_back(i);
+  std::stable_sort(inputs.begin(), inputs.end(), [&](int x, int y) { return p.insn[x].a < p.insn[y].a; });
+  for (int i : inputs) push(i);
+  std::function<void(int)> visit = [&](int i) {
+    if (id[i] >= 0) return;
+    const Insn& x = p.insn[i];
+    const int n = operand_count(x.op);
+    if (n >= 1) visit(x.a);
+    if (n >= 2) visit(x.b);
+    if (n >= 3) visit(x.c);
+    push(i);
+  };
+  for (int k = 0; k < p.n_out; ++k) visit(p.out_reg[k]);
+  for (int k = 0; k < p.n_out; ++k) q.out_reg[k] = uint8_t(id[p.out_reg[k]]);
+  q.n_regs = q.n_insn;
+  return q;
+}
+
 void assign_registers(Program& p) {
   const int n = p.n_insn;
   std::vector<int> last(n, -1);
@@ -434,7 +479,7 @@ void build_elementwise(ask_b200_plan& pl, const json::Value& r) {
   pl.inner = in ? checked_count(*in, "inner") : 1;
   Ports ports;
   parse_ports(r, "inputs", true, ports.type, ports.map);
-  pl.prog = parse_program(r.at("program"), r.at("results"), ports, true);
+  pl.prog = canonical(parse_program(r.at("program"), r.at("results"), ports, true));
   bool uses_div = false;
   for (size_t k = 0; k < ports.type.size(); ++k) {
     uint64_t elems = pl.count;
@@ -474,7 +519,7 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   const uint64_t index_base = ib ? checked_count(*ib, "index_base") : 0;
   Ports ports;
   parse_ports(r, "inputs", true, ports.type, ports.map);
-  pl.prog = parse_program(r.at("program"), r.at("results"), ports, false);
+  pl.prog = canonical(parse_program(r.at("program"), r.at("results"), ports, false));
   const auto& reds = r.at("reductions").as_array("reductions");
   if (reds.empty() || reds.size() > size_t(kMaxReductions))
     fail(ASK_B200_E_UNSUPPORTED, "1.." + std::to_string(kMaxReductions) + " reductions per step");

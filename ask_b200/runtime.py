@@ -270,3 +270,33 @@ def check_allocation(allocation: dict):
 def assign_slots(plan: dict, graph: bool = False) -> dict:
     """Slot assignment for a plan with buffer_sizes; returns the allocation fields."""
     return json.loads(_text(_lib.ask_b200_allocation_assign, json.dumps(plan).encode(), 1 if graph else 0))
+
+
+# ---- lowering adapter (include/ask_b200_lower.h) --------------------------------------
+_LOWER_SIGNATURES = {
+    "ask_b200_lower_step": (ctypes.c_int, [ctypes.c_char_p] + _TEXT),
+    "ask_b200_lower_report": (ctypes.c_int, [ctypes.c_char_p] + _TEXT),
+}
+for _name, (_res, _args) in _LOWER_SIGNATURES.items():
+    _fn = getattr(_lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+def lower_step(step_source: str) -> dict:
+    """One ASK step source (MLIR text) -> {"recipe": ..., "input_arguments": [...]}."""
+    return json.loads(_text(_lib.ask_b200_lower_step, step_source.encode()))
+
+
+def lower_report(report) -> dict:
+    """A partition report (execution_plan + step_sources) -> a runtime program."""
+    text = report if isinstance(report, str) else json.dumps(report)
+    return json.loads(_text(_lib.ask_b200_lower_report, text.encode()))
+
+
+def prepare_report(session: Session, report, graph: bool = False) -> PreparedProgram:
+    """Lower a partition report and prepare it as a program on `session`."""
+    program = lower_report(report)
+    h = _p()
+    _check(_lib.ask_b200_program_prepare(session._h, json.dumps(program).encode(), 1 if graph else 0, ctypes.byref(h)))
+    return PreparedProgram(h, session, len(program["outputs"]))

@@ -1,0 +1,47 @@
+/*
+ * ask_b200_lower.h -- lowering adapter from ASK step sources to ask_b200
+ * recipes, the replacement for ask::lowerToCUDALLVM on sm_100
+ * (lib/Lowering/CUDA.cpp:152-419, reached through codegen(..., {CUDALLVM, 100})
+ * or `ask-opt --emit-cuda-llvm --cuda-arch 100`, tools/ask-opt.cpp:115-133).
+ *
+ * Input is what the reference's partitioner emits (lib/Frontend/Partition.cpp):
+ * each owned step's module printed as MLIR text ("step_sources") and the
+ * execution plan that binds steps to buffers.  The supported subset is the hot
+ * path: elementwise ops over the step's iteration shape with scalar and
+ * leading/trailing-axis broadcasts, reductions (sum, prod, max, min, any, all,
+ * argmax, argmin) over one contiguous block of axes, gather and scatter_add.
+ * Steps outside it fail with ASK_B200_E_UNSUPPORTED and a message naming the
+ * op (transpose, slice, pad, concatenate and iota need index maps these
+ * kernels do not have; matmul and external steps are not recipe steps).
+ */
+#ifndef ASK_B200_LOWER_H
+#define ASK_B200_LOWER_H
+
+#include "ask_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/*
+ * One step source (a module holding one func.func of ASK ops) to
+ * {"recipe": {...}, "input_arguments": [k, ...]}: recipe input port i reads the
+ * function's argument input_arguments[i]; outputs follow the function's return
+ * order.  Text is written as by ask_b200_plan_describe.
+ */
+ASK_B200_API int ask_b200_lower_step(const char *step_source, char *buf, size_t cap, size_t *needed);
+
+/*
+ * A partition report ({"execution_plan": {...}, "step_sources": {...}}, the
+ * reference's report fields) to a runtime program for
+ * ask_b200_program_prepare (ask_b200_runtime.h): buffer sizes from the plan's
+ * buffer shapes and element types, public inputs and outputs, and one recipe
+ * step per owned step with its ports bound to the plan's buffers.
+ */
+ASK_B200_API int ask_b200_lower_report(const char *report_json, char *buf, size_t cap, size_t *needed);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASK_B200_LOWER_H */

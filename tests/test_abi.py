@@ -39,6 +39,11 @@ def test_runtime_library_exports_every_declared_symbol(lib_built):
     for name in names:
         assert hasattr(lib, name), f"{name} declared in include/ask_b200_runtime.h but not exported"
     assert set(names) == set(rt.RUNTIME_SIGNATURES)
+    text = open(os.path.join(ROOT, "include", "ask_b200_lower.h")).read()
+    lowered = sorted(set(re.findall(r"ASK_B200_API\s+int\s+(ask_b200_[a-z_0-9]+)\s*\(", text)))
+    assert lowered == sorted(rt._LOWER_SIGNATURES)
+    for name in lowered:
+        assert hasattr(lib, name)
 
 
 def test_runtime_session_without_gpu_is_an_error():

@@ -1,0 +1,306 @@
+"""Lowering adapter: ASK step sources (MLIR text) -> recipes -> programs.
+
+The step sources below are written in the form the reference's partitioner
+prints (lib/Frontend/Partition.cpp:178-273: one func.func per owned step, ASK
+ops in MLIR generic form, ask.* attributes on ops and arguments).  Each config
+of the benchmark is lowered and must select the same specialised kernel as
+its hand-written recipe; a partition report with three softmax steps and one
+with gather -> scatter_add become runtime programs.  The GPU tests run lowered
+programs against the hand-written recipes, bit for bit.
+"""
+import json
+
+import numpy as np
+import pytest
+
+import ask_b200
+from ask_b200 import recipes as R
+from ask_b200 import runtime as rt
+
+
+def ttype(shape, dt):
+    mlir = {"bool": "i1"}.get(dt, dt)
+    return f"tensor<{'x'.join(str(d) for d in shape)}{'x' if shape else ''}{mlir}>"
+
+
+class Step:
+    """Builds one step source in the printed MLIR form."""
+
+    def __init__(self, name="ask_kernel_0", kernel="kernel0"):
+        self.name, self.kernel = name, kernel
+        self.args, self.lines, self.n = [], [], 0
+
+    def arg(self, shape, dt):
+        k = len(self.args)
+        self.args.append((shape, dt))
+        return f"%arg{k}", shape, dt
+
+    def op(self, name, operands, shape, dt, attrs=""):
+        v = f"%{self.n}"
+        self.n += 1
+        a = f'{{ask.id = "{self.kernel}.op{self.n}", ask.value_id = "v{self.n}"{", " + attrs if attrs else ""}}}'
+        ins = ", ".join(o[0] for o in operands)
+        tys = ", ".join(ttype(o[1], o[2]) if o[1] is not None else o[2] for o in operands)
+        out = ttype(shape, dt) if shape is not None else dt
+        self.lines.append(f'    {v} = "ask.{name}"({ins}) {a} : ({tys}) -> {out}')
+        return v, shape, dt
+
+    def const(self, value, dt):
+        v = f"%{self.n}"
+        self.n += 1
+        self.lines.append(f'    {v} = "ask.constant"() {{ask.id = "{self.kernel}.scalar{self.n}", value = {value} : {dt}}}'
+                          f" : () -> {dt}")
+        return v, None, dt
+
+    def splat(self, c, shape):
+        return self.op("splat", [c], shape, c[2], f"shape = array<i64: {', '.join(map(str, shape))}>")
+
+    def text(self, results):
+        args = ", ".join(f'%arg{k}: {ttype(s, d)} {{ask.source_value_id = "x{k}", ask.value_id = "{self.kernel}.arg{k}"}}'
+                         for k, (s, d) in enumerate(self.args))
+        res = ", ".join(ttype(r[1], r[2]) for r in results)
+        ret = ", ".join(r[0] for r in results)
+        return ("module {\n"
+                f"  func.func @{self.name}({args}) -> ({res}) attributes {{ask.kernel_id = \"{self.kernel}\", "
+                f"ask.kernel_kind = \"owned\", ask.source_function = \"main\"}} {{\n"
+                + "\n".join(self.lines) + "\n"
+                f"    return {ret} : {res}\n  }}\n}}\n")
+
+
+def cfg1_source(n=4096):
+    s = Step()
+    a, b, c = (s.arg([n, n], "f32") for _ in range(3))
+    sh = [n, n]
+    y0 = s.op("add", [s.op("mul", [s.op("exp", [a], sh, "f32"), b], sh, "f32"), c], sh, "f32", 'overflow = "wrap"')
+    m = s.op("maximum", [a, b], sh, "f32")
+    neg = s.op("mul", [s.op("tanh", [c], sh, "f32"), s.splat(s.const("-1.000000e+00", "f32"), sh)], sh, "f32")
+    y1 = s.op("add", [m, neg], sh, "f32")
+    return s.text([y0, y1])
+
+
+def cfg2_source(rows=65536, cols=1024):
+    s = Step()
+    x = s.arg([rows, cols], "f32")
+    outs = [s.op(f"reduce_{k}", [x], [rows], "f32", "axes = array<i64: 1>") for k in ("sum", "max", "min")]
+    outs.append(s.op("argmax", [x], [rows], "i64", "axis = 1 : i64"))
+    return s.text(outs)
+
+
+def cfg3_sources(dt="f16", rows=32768, cols=4096):
+    sh = [rows, cols]
+    s0 = Step("ask_kernel_0", "kernel0")
+    x = s0.arg(sh, dt)
+    m = s0.op("reduce_max", [s0.op("cast", [x], sh, "f32")], [rows], "f32", "axes = array<i64: 1>")
+    src0 = s0.text([m])
+
+    def shifted(s):
+        x = s.arg(sh, dt)
+        m = s.arg([rows], "f32")
+        xf = s.op("cast", [x], sh, "f32")
+        mb = s.op("broadcast_in_dim", [m], sh, "f32", f"dimensions = array<i64: 0>, shape = array<i64: {rows}, {cols}>")
+        neg = s.op("mul", [mb, s.splat(s.const("-1.000000e+00", "f32"), sh)], sh, "f32")
+        return s.op("exp", [s.op("add", [xf, neg], sh, "f32", 'overflow = "wrap"')], sh, "f32")
+
+    s1 = Step("ask_kernel_1", "kernel1")
+    e = shifted(s1)
+    src1 = s1.text([s1.op("reduce_sum", [e], [rows], "f32", "axes = array<i64: 1>")])
+    s2 = Step("ask_kernel_2", "kernel2")
+    e = shifted(s2)
+    sarg = s2.arg([rows], "f32")
+    sb = s2.op("broadcast_in_dim", [sarg], sh, "f32", f"dimensions = array<i64: 0>, shape = array<i64: {rows}, {cols}>")
+    y = s2.op("cast", [s2.op("div", [e, sb], sh, "f32")], sh, dt)
+    return [src0, src1, s2.text([y])]
+
+
+def cfg4_sources(rows=1 << 20, dim=256, n=1 << 23):
+    g = Step("ask_kernel_0", "kernel0")
+    t, i = g.arg([rows, dim], "f32"), g.arg([n], "i64")
+    gsrc = g.text([g.op("gather", [t, i], [n, dim], "f32", "axis = 0 : i64")])
+    s = Step("ask_kernel_1", "kernel1")
+    base, idx, upd = s.arg([rows, dim], "f32"), s.arg([n], "i64"), s.arg([n, dim], "f32")
+    ssrc = s.text([s.op("scatter_add", [base, idx, upd], [rows, dim], "f32", "axis = 0 : i64")])
+    return gsrc, ssrc
+
+
+def cfg5_sources(na=1 << 32, nb=1 << 31):
+    a = Step()
+    x = a.arg([na], "f32")
+    outs = [a.op("reduce_sum", [x], [], "f32", "axes = array<i64: 0>"),
+            a.op("reduce_min", [x], [], "f32", "axes = array<i64: 0>"),
+            a.op("argmin", [x], [], "i64", "axis = 0 : i64")]
+    b = Step()
+    x, y = b.arg([nb], "i32"), b.arg([nb], "i32")
+    sh = [nb]
+    t = b.op("bitwise_xor", [b.op("shift_left", [x, b.splat(b.const(3, "i32"), sh)], sh, "i32"),
+                             b.op("shift_right", [x, b.splat(b.const(5, "i32"), sh)], sh, "i32")], sh, "i32")
+    z = b.op("add", [b.op("bitwise_and", [t, b.splat(b.const(2147483647, "i32"), sh)], sh, "i32"), y], sh, "i32",
+             'overflow = "wrap"')
+    return a.text(outs), b.text([z])
+
+
+def kernel_of(recipe):
+    return ask_b200.Plan(recipe, device=-1).describe()["kernel"]
+
+
+@pytest.mark.parametrize("name,source,hand", [
+    ("cfg1", lambda: cfg1_source(), lambda: R.cfg1_step()),
+    ("cfg2", lambda: cfg2_source(), lambda: R.cfg2_step()),
+    ("cfg5a", lambda: cfg5_sources()[0], lambda: R.cfg5a_step()),
+    ("cfg5b", lambda: cfg5_sources()[1], lambda: R.cfg5b_step()),
+    ("cfg4g", lambda: cfg4_sources()[0], lambda: R.cfg4_gather_step()),
+    ("cfg4s", lambda: cfg4_sources()[1], lambda: R.cfg4_scatter_step()),
+])
+def test_configs_lower_to_the_specialised_kernels(name, source, hand):
+    out = rt.lower_step(source())
+    lowered, want = ask_b200.Plan(out["recipe"], -1).describe(), ask_b200.Plan(hand(), -1).describe()
+    for key in ("family", "kernel", "strategy", "port_map", "scratch_bytes"):
+        assert lowered.get(key) == want.get(key), key
+    assert out["input_arguments"] == list(range(len(out["input_arguments"])))
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_softmax_steps_lower_to_the_specialised_kernels(dt):
+    for src, hand in zip(cfg3_sources(dt), R.cfg3_steps(dt)):
+        assert kernel_of(rt.lower_step(src)["recipe"]) == kernel_of(hand)
+
+
+def test_constants_keep_their_exact_value():
+    s = Step()
+    x = s.arg([8], "f16")
+    c = s.splat(s.const("0x7E00", "f16"), [8])  # a NaN printed as its bit pattern
+    d = s.splat(s.const("1.000000e-01", "f16"), [8])
+    y = s.op("add", [s.op("maximum", [x, c], [8], "f16"), d], [8], "f16")
+    r = rt.lower_step(s.text([y]))["recipe"]
+    consts = [i for i in r["program"] if i[0] == "const"]
+    assert consts == [["const", "f16", "bits:0x7E00"], ["const", "f16", "1.000000e-01"]]
+    ask_b200.Plan(r, -1)
+
+
+def test_index_maps():
+    s = Step()
+    x = s.arg([4, 8], "f32")
+    row = s.arg([4], "f32")
+    col = s.arg([8], "f32")
+    one = s.arg([], "f32")
+    rb = s.op("broadcast_in_dim", [row], [4, 8], "f32", "dimensions = array<i64: 0>, shape = array<i64: 4, 8>")
+    cb = s.op("broadcast_in_dim", [col], [4, 8], "f32", "dimensions = array<i64: 1>, shape = array<i64: 4, 8>")
+    ob = s.op("broadcast_in_dim", [one], [4, 8], "f32", "dimensions = array<i64>, shape = array<i64: 4, 8>")
+    y = s.op("add", [s.op("mul", [x, rb], [4, 8], "f32"), s.op("add", [cb, ob], [4, 8], "f32")], [4, 8], "f32")
+    r = rt.lower_step(s.text([y]))["recipe"]
+    assert [p["map"] for p in r["inputs"]] == ["full", "outer", "inner", "scalar"]
+    assert r["inner"] == 8
+    ask_b200.Plan(r, -1)
+
+
+@pytest.mark.parametrize("op,attrs,shape", [
+    ("transpose", "permutation = array<i64: 1, 0>", [8, 4]),
+    ("slice", "start_indices = array<i64: 0, 0>, limit_indices = array<i64: 4, 4>, strides = array<i64: 1, 1>", [4, 4]),
+])
+def test_general_index_maps_are_unsupported(op, attrs, shape):
+    s = Step()
+    x = s.arg([4, 8], "f32")
+    y = s.op(op, [x], shape, "f32", attrs)
+    with pytest.raises(rt.CUDAError) as err:
+        rt.lower_step(s.text([y]))
+    assert err.value.status == ask_b200.E_UNSUPPORTED and op in str(err.value)
+
+
+def test_malformed_sources_are_invalid():
+    for text in ["module {}", "module { func.func @f(%arg0: tensor<?xf32>) -> tensor<?xf32> { return %arg0 : tensor<?xf32> } }"]:
+        with pytest.raises(rt.CUDAError) as err:
+            rt.lower_step(text)
+        assert err.value.status == ask_b200.E_INVALID
+
+
+def report(sources, buffers, inputs, outputs, steps):
+    return {"execution_plan": {"schema_version": 1, "kind": "ask.cuda.execution_plan", "inputs": inputs,
+                               "outputs": outputs, "buffers": buffers,
+                               "steps": [{"id": f"kernel{k}", "kind": "owned", "function": f"ask_kernel_{k}",
+                                          "inputs": i, "outputs": o, "depends_on": []} for k, (i, o) in enumerate(steps)]},
+            "step_sources": {f"kernel{k}": src for k, src in enumerate(sources)}}
+
+
+def softmax_report(dt, rows, cols):
+    buffers = [{"id": "v_x", "shape": [rows, cols], "element_type": dt},
+               {"id": "v_m", "shape": [rows], "element_type": "f32"},
+               {"id": "v_s", "shape": [rows], "element_type": "f32"},
+               {"id": "v_y", "shape": [rows, cols], "element_type": dt}]
+    return report(cfg3_sources(dt, rows, cols), buffers, ["v_x"], ["v_y"],
+                  [(["v_x"], ["v_m"]), (["v_x", "v_m"], ["v_s"]), (["v_x", "v_m", "v_s"], ["v_y"])])
+
+
+def scatter_report(rows, dim, n):
+    g, s = cfg4_sources(rows, dim, n)
+    buffers = [{"id": "table", "shape": [rows, dim], "element_type": "f32"},
+               {"id": "idx", "shape": [n], "element_type": "i64"},
+               {"id": "base", "shape": [rows, dim], "element_type": "f32"},
+               {"id": "g", "shape": [n, dim], "element_type": "f32"},
+               {"id": "out", "shape": [rows, dim], "element_type": "f32"}]
+    return report([g, s], buffers, ["table", "idx", "base"], ["out"],
+                  [(["table", "idx"], ["g"]), (["base", "idx", "g"], ["out"])])
+
+
+def test_report_lowers_to_a_program():
+    prog = rt.lower_report(softmax_report("f16", 32768, 4096))
+    assert prog["buffer_sizes"] == [2 * 32768 * 4096, 4 * 32768, 4 * 32768, 2 * 32768 * 4096]
+    assert prog["inputs"] == [0] and prog["outputs"] == [3]
+    assert [s["inputs"] for s in prog["steps"]] == [[0], [0, 1], [0, 1, 2]]
+    assert [kernel_of(json.loads(s["recipe"])) for s in prog["steps"]] == [
+        "reduce_warp_row_softmax_max_f16", "reduce_warp_row_softmax_sum_f16", "ew_softmax_norm_f16"]
+    prog = rt.lower_report(scatter_report(1 << 20, 256, 1 << 23))
+    assert [s["inputs"] for s in prog["steps"]] == [[0, 1], [2, 1, 3]]
+
+
+def test_non_owned_steps_are_unsupported():
+    r = softmax_report("f16", 8, 16)
+    r["execution_plan"]["steps"][1]["kind"] = "external"
+    with pytest.raises(rt.CUDAError) as err:
+        rt.lower_report(r)
+    assert err.value.status == ask_b200.E_UNSUPPORTED
+
+
+# ---- on the GPU: lowered programs against the hand-written recipes ------------------------
+@pytest.mark.gpu
+@pytest.mark.parametrize("graph", [False, True])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_lowered_softmax_program_matches_hand_recipes(device, graph, dt):
+    import torch
+    from gpu_util import gen_dev
+    rows, cols = 256, 4096
+    x = gen_dev(2 if dt == "f16" else 3, 0xA5C3, 0, rows * cols, 0.0, 2.0, torch.int16)
+    session = rt.Session.create(0)
+    hand = session.prepareProgram(
+        [2 * rows * cols, 4 * rows, 4 * rows, 2 * rows * cols], [0], [3],
+        [rt.PlanStep(s, i, o) for s, i, o in zip(R.cfg3_steps(dt, rows, cols), [[0], [0, 1], [0, 1, 2]], [[1], [2], [3]])],
+        graph)
+    lowered = rt.prepare_report(session, softmax_report(dt, rows, cols), graph)
+    xin = session.importTensor(x, readonly=True)
+    session.waitForExternalStream(torch.cuda.current_stream())
+    (a,), ea = hand.run([xin])
+    (b,), eb = lowered.run([xin])
+    ea.wait()
+    eb.wait()
+    assert a.copyToHost() == b.copyToHost()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("graph", [False, True])
+def test_lowered_gather_scatter_program(device, graph):
+    import torch
+    from gpu_util import gen_dev
+    rows, dim, n = 2048, 64, 20000
+    table = (gen_dev(4, 0xA5C4, 0, rows * dim, 0, 0, torch.int32) % 1000).float()  # small integers
+    idx = gen_dev(5, 0xA5C4, 1, n, 1.1, rows, torch.int64)
+    base = torch.zeros(rows * dim, dtype=torch.float32, device="cuda")
+    session = rt.Session.create(0)
+    program = rt.prepare_report(session, scatter_report(rows, dim, n), graph)
+    ins = [session.importTensor(t, readonly=True) for t in (table, idx, base)]
+    session.waitForExternalStream(torch.cuda.current_stream())
+    (out,), ev = program.run(ins)
+    ev.wait()
+    got = np.frombuffer(out.copyToHost(), np.float32).reshape(rows, dim)
+    t, ix = table.view(rows, dim).cpu().numpy().astype(np.float64), idx.cpu().numpy()
+    want = np.zeros((rows, dim))
+    np.add.at(want, ix, t[ix])
+    # integer-valued f32 updates: every partial sum is exact, so the result is too
+    assert np.array_equal(got, want.astype(np.float32))
