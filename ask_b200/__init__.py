@@ -144,6 +144,19 @@ class Plan:
         arr, n = self._ports(inputs, outputs)
         _check(_lib.ask_b200_plan_launch(self._h, arr, n, _ptr(scratch), _stream_handle(stream)))
 
+    def bind(self, inputs: Sequence, outputs: Sequence, scratch=None, stream=None):
+        """A zero-argument callable that enqueues the step on fixed ports: the
+        port array and handles are marshalled once, so a loop of launches pays
+        only the C call (the tensors must outlive the callable)."""
+        arr, n = self._ports(inputs, outputs)
+        fn, h, sc, st = _lib.ask_b200_plan_launch, self._h, _ptr(scratch), _stream_handle(stream)
+
+        def launch() -> None:
+            status = fn(h, arr, n, sc, st)
+            if status != OK:
+                _check(status)
+        return launch
+
     def launch_noalloc(self, inputs: Sequence, outputs: Sequence, stream=None) -> None:
         """Reduce plans only: scratch comes from the library's fixed device
         array (see ask_b200_plan_launch_noalloc in include/ask_b200.h)."""

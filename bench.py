@@ -112,6 +112,29 @@ class Workload:
         return sum(p.kernel_launches for p in self.plans)
 
 
+def static_config(name, world, small=False):
+    """The `config` object of a workload's bench line (both arms print it)."""
+    if name == "cfg5":
+        return {"workload": "cfg5: sum/min/argmin over 2^32 f32 U[0,1) + i32 chain over 2^31, "
+                            "leading-axis shards" + (" (SMALL profiling case)" if small else ""),
+                "elements_f32": (1 << 28) if small else (1 << 32), "elements_i32": (1 << 27) if small else (1 << 31),
+                "parallelism": f"shard{world}", "l2": "inputs 40 GB >> 126 MB L2, no flush needed"}
+    if name == "cfg1":
+        return {"workload": "cfg1: y0=exp(a)*b+c, y1=max(a,b)-tanh(c), f32 [4096,4096]",
+                "l2": "320 MB per step > 126 MB L2"}
+    if name == "cfg2":
+        return {"workload": "cfg2: row sum/max/min/argmax, f32 [65536,1024]", "l2": "256 MB > L2"}
+    if name in ("cfg3", "cfg3bf"):
+        dt = "f16" if name == "cfg3" else "bf16"
+        return {"workload": f"cfg3: 3-step softmax plan, {dt} [32768,4096]", "l2": "256 MB input > L2"}
+    if name == "cfg4g":
+        return {"workload": "cfg4 gather: table f32 [2^20,256], idx i64 Zipf(1.1) [2^23]", "l2": "8 GiB output > L2"}
+    if name == "cfg4s":
+        return {"workload": "cfg4 scatter_add: grad f32 [2^23,256] into zeros [2^20,256], idx Zipf(1.1)",
+                "l2": "8 GiB updates > L2"}
+    raise SystemExit(f"unknown workload {name}")
+
+
 def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
     st = torch.cuda.current_stream()
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -139,20 +162,17 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         z = torch.empty_like(xi)
         scratch = torch.empty(max(pa.scratch_bytes, 16), dtype=torch.uint8, device=dev)
 
-        def run_a():
-            if world > 1:
+        if world > 1:
+            def run_a():
                 pa.launch_sharded(comm, [x], outs, scratch, st)
-            else:
-                pa.launch([x], outs, scratch, st)
+        else:
+            run_a = pa.bind([x], outs, scratch, st)
 
         w.plans = [pa, pb]
         w.kernels = [("reduce_split_global_f32", 4 * (a1 - a0), run_a),
-                     ("ew_cfg5b", 12 * (b1 - b0), lambda: pb.launch([xi, yi], [z], None, st))]
+                     ("ew_cfg5b", 12 * (b1 - b0), pb.bind([xi, yi], [z], None, st))]
         w.global_bytes = 4 * na + 12 * nb
-        w.config = {"workload": "cfg5: sum/min/argmin over 2^32 f32 U[0,1) + i32 chain over 2^31, "
-                                "leading-axis shards" + (" (SMALL profiling case)" if small else ""),
-                    "elements_f32": na, "elements_i32": nb,
-                    "parallelism": f"shard{world}", "l2": "inputs 40 GB >> 126 MB L2, no flush needed"}
+        w.config = static_config(name, world, small)
         w.tensors = {"x": x, "xi": xi, "yi": yi, "z": z, "outs": outs, "scratch": scratch}
         w.e2e = {"inputs": [x, xi, yi], "results": outs + [z]}
         return w
@@ -164,9 +184,8 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         y0, y1 = torch.empty_like(a), torch.empty_like(a)
         p = ask_b200.Plan(R.cfg1_step(n), rank_device())
         w.plans = [p]
-        w.kernels = [("ew_cfg1", 20 * n, lambda: p.launch([a, b, c], [y0, y1], None, st))]
-        w.config = {"workload": "cfg1: y0=exp(a)*b+c, y1=max(a,b)-tanh(c), f32 [4096,4096]",
-                    "l2": "320 MB per step > 126 MB L2"}
+        w.kernels = [("ew_cfg1", 20 * n, p.bind([a, b, c], [y0, y1], None, st))]
+        w.config = static_config(name, world)
         w.e2e = {"inputs": [a, b, c], "results": [y0, y1]}
     elif name == "cfg2":
         rows, cols = 65536, 1024
@@ -176,8 +195,8 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         p = ask_b200.Plan(R.cfg2_step(rows, cols), rank_device())
         w.plans = [p]
         w.kernels = [("reduce_warp_row_rowstats_f32", 4 * rows * cols + rows * 20,
-                      lambda: p.launch([x], outs, None, st))]
-        w.config = {"workload": "cfg2: row sum/max/min/argmax, f32 [65536,1024]", "l2": "256 MB > L2"}
+                      p.bind([x], outs, None, st))]
+        w.config = static_config(name, world)
         w.e2e = {"inputs": [x], "results": outs}
     elif name in ("cfg3", "cfg3bf"):
         dt = "f16" if name == "cfg3" else "bf16"
@@ -189,10 +208,10 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         ps = [ask_b200.Plan(r, rank_device()) for r in R.cfg3_steps(dt, rows, cols)]
         w.plans = ps
         n = rows * cols
-        w.kernels = [(f"reduce_softmax_max_{dt}", 2 * n + 4 * rows, lambda: ps[0].launch([x], [m], None, st)),
-                     (f"reduce_softmax_sum_{dt}", 2 * n + 8 * rows, lambda: ps[1].launch([x, m], [s], None, st)),
-                     (f"ew_softmax_norm_{dt}", 4 * n + 8 * rows, lambda: ps[2].launch([x, m, s], [y], None, st))]
-        w.config = {"workload": f"cfg3: 3-step softmax plan, {dt} [32768,4096]", "l2": "256 MB input > L2"}
+        w.kernels = [(f"reduce_softmax_max_{dt}", 2 * n + 4 * rows, ps[0].bind([x], [m], None, st)),
+                     (f"reduce_softmax_sum_{dt}", 2 * n + 8 * rows, ps[1].bind([x, m], [s], None, st)),
+                     (f"ew_softmax_norm_{dt}", 4 * n + 8 * rows, ps[2].bind([x, m, s], [y], None, st))]
+        w.config = static_config(name, world)
         w.dtype = dt
         w.e2e = {"inputs": [x], "results": [y]}
     elif name in ("cfg4g", "cfg4s"):
@@ -204,9 +223,8 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
             p = ask_b200.Plan(R.cfg4_gather_step(rows, dim, n), rank_device())
             distinct = int(torch.unique(idx).numel())
             w.kernels = [("gather_rows", 8 * n + 4 * n * dim + 4 * dim * distinct,
-                          lambda: p.launch([table, idx], [out], None, st))]
-            w.config = {"workload": "cfg4 gather: table f32 [2^20,256], idx i64 Zipf(1.1) [2^23]",
-                        "distinct_rows": distinct, "l2": "8 GiB output > L2"}
+                          p.bind([table, idx], [out], None, st))]
+            w.config = dict(static_config(name, world), distinct_rows=distinct)
             w.e2e = {"inputs": [table, idx], "results": [out]}
         else:
             grad = gen(1, SEED["cfg4"], 2, n * dim, 0.0, 1.0, torch.float32)
@@ -215,9 +233,8 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
             p = ask_b200.Plan(R.cfg4_scatter_step(rows, dim, n), rank_device())
             scratch = torch.empty(max(p.scratch_bytes, 16), dtype=torch.uint8, device=dev)
             w.kernels = [("scatter_add_sorted_rows", 8 * n + 4 * n * dim + 8 * rows * dim,
-                          lambda: p.launch([base, idx, grad], [out], scratch, st))]
-            w.config = {"workload": "cfg4 scatter_add: grad f32 [2^23,256] into zeros [2^20,256], idx Zipf(1.1)",
-                        "l2": "8 GiB updates > L2"}
+                          p.bind([base, idx, grad], [out], scratch, st))]
+            w.config = static_config(name, world)
             w.e2e = {"inputs": [base, idx, grad], "results": [out]}
         w.plans = [p]
     else:
@@ -527,10 +544,9 @@ def reference_arm(args, world, rank):
         bps, secs, desc = cpu_sample(args.workload, threads, budget_s=2.0)
         vals.append(bps / 1e9)
     value = statistics.median(vals)
-    w.config["grids"] = grids
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "impl": "reference", "vs_baseline": None,
-            "data": "synthetic (seeded Philox4x32-10)", "config": {"workload": args.workload},
+            "data": "synthetic (seeded Philox4x32-10)", "config": static_config(args.workload, world),
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": desc, "cpu": cpu_model()},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
