@@ -126,6 +126,21 @@ cudaError_t scatter_sorted_launch(const IndexArgs& a, void* scratch, int sms, cu
 
 // ---- input synthesis (Philox4x32-10) -------------------------------------------------
 enum GenKind : int { GEN_UNIFORM_F32 = 0, GEN_NORMAL_F32, GEN_NORMAL_F16, GEN_NORMAL_BF16, GEN_I32, GEN_ZIPF_I64, GEN_ZIPF_I32 };
+// Family S: the three-step softmax plan fused (softmax_kernels.cu).  x and y
+// are [rows, cols] f16/bf16 (16-byte aligned), m and s are [rows] f32.
+struct SoftmaxArgs {
+  const void* x;
+  float* m;
+  float* s;
+  void* y;
+  uint64_t rows, cols;
+  int type;  // kF16 or kBF16
+};
+// 16-byte vectors each thread of a row's CTA holds, or 0 when cols has no
+// fused kernel (cols must be a multiple of 256, at most 32768).
+int softmax_vectors_per_thread(uint64_t cols);
+cudaError_t softmax_rows_launch(const SoftmaxArgs& a, int sms, cudaStream_t stream);
+
 cudaError_t gen_launch(int kind, uint64_t seed, uint32_t stream_id, uint64_t offset, uint64_t count, double p0,
                        double p1, const double* zipf_cdf, uint64_t zipf_n, void* dst, cudaStream_t stream);
 

@@ -393,8 +393,8 @@ void assign_registers(Program& p) {
 }
 
 // ---- plan -------------------------------------------------------------------------
-enum Family { FAM_ELEMENTWISE = 0, FAM_REDUCE, FAM_GATHER, FAM_SCATTER };
-const char* const kFamilyNames[] = {"elementwise", "reduce", "gather", "scatter_add"};
+enum Family { FAM_ELEMENTWISE = 0, FAM_REDUCE, FAM_GATHER, FAM_SCATTER, FAM_SOFTMAX };
+const char* const kFamilyNames[] = {"elementwise", "reduce", "gather", "scatter_add", "softmax"};
 
 struct PortInfo {
   int dtype;
@@ -430,8 +430,10 @@ struct ask_b200_plan {
   uint64_t count = 0, inner = 1;
   RedArgs red{};
   IndexArgs idx{};
+  SoftmaxArgs sm{};
   bool shardable = false;
   std::string kernel;
+  int block = 256;  // threads per CTA where the family fixes it (softmax)
 };
 
 struct ask_b200_comm {
@@ -632,12 +634,34 @@ void build_index(ask_b200_plan& pl, const json::Value& r, bool scatter) {
   pl.grid = pl.num_sms * 8;
 }
 
+// Family S: {"family": "softmax", "dtype": "f16"|"bf16", "rows": R, "cols": C}
+// -- the reference's three softmax steps (row max, row sum of exp(x - max),
+// normalise) as one step with outputs m [R] f32, s [R] f32, y [R, C].
+void build_softmax(ask_b200_plan& pl, const json::Value& r) {
+  SoftmaxArgs& a = pl.sm;
+  a = SoftmaxArgs{};
+  a.type = parse_dtype(r.at("dtype").as_str("dtype"));
+  if (a.type != kF16 && a.type != kBF16) fail(ASK_B200_E_UNSUPPORTED, "the fused softmax reads f16 or bf16 rows");
+  a.rows = checked_count(r.at("rows"), "rows");
+  a.cols = checked_count(r.at("cols"), "cols");
+  const int vpt = softmax_vectors_per_thread(a.cols);
+  if (!vpt) fail(ASK_B200_E_UNSUPPORTED, "the fused softmax needs cols a multiple of 256 and at most 32768");
+  const uint64_t n = mul_checked(a.rows, a.cols);
+  pl.inputs = {{a.type, n, IM_FULL}};
+  pl.outputs = {{kF32, a.rows, IM_FULL}, {kF32, a.rows, IM_FULL}, {a.type, n, IM_FULL}};
+  pl.kernel = a.type == kF16 ? "softmax_rows_f16" : "softmax_rows_bf16";
+  pl.launches = a.rows ? 1 : 0;
+  pl.grid = int(std::min<uint64_t>(a.rows ? a.rows : 1, uint64_t(pl.num_sms) * 4));
+  pl.block = int(a.cols / 8 / uint64_t(vpt));
+}
+
 std::string describe(const ask_b200_plan& pl) {
   std::ostringstream o;
   o << "{\"format\":\"ask-b200-recipe\",\"abi_version\":" << ASK_B200_ABI_VERSION << ",\"family\":\""
     << kFamilyNames[pl.family] << "\",\"kernel\":\"" << pl.kernel << "\",\"device\":" << pl.device
     << ",\"target\":{\"backend\":\"cuda\",\"arch\":100},\"launch\":{\"grid\":[" << pl.grid << ",1,1],\"block\":["
-    << (pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? kRedThreads : 256)
+    << (pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? kRedThreads :
+        pl.family == FAM_SOFTMAX ? pl.block : 256)
     << ",1,1],\"shared_bytes\":0},\"kernels_per_launch\":" << pl.launches << ",\"scratch_bytes\":" << pl.scratch;
   if (pl.family == FAM_REDUCE) {
     const char* strat[] = {"warp_row", "column", "split"};
@@ -742,6 +766,17 @@ void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratc
       if (scratch && !aligned16(scratch)) fail(ASK_B200_E_INVALID, "scratch must be 16-byte aligned");
       check_cuda(scatter_add_launch(a, 1, pl.grid, reinterpret_cast<void*>(scratch), pl.num_sms, st),
                  "scatter_add launch");
+      break;
+    }
+    case FAM_SOFTMAX: {
+      SoftmaxArgs a = pl.sm;
+      a.x = reinterpret_cast<const void*>(ports[0]);
+      a.m = reinterpret_cast<float*>(ports[1]);
+      a.s = reinterpret_cast<float*>(ports[2]);
+      a.y = reinterpret_cast<void*>(ports[3]);
+      if (a.rows && (!aligned16(ports[0]) || !aligned16(ports[3])))
+        fail(ASK_B200_E_INVALID, "the fused softmax needs 16-byte aligned x and y");
+      check_cuda(softmax_rows_launch(a, pl.num_sms, st), "softmax launch");
       break;
     }
     default:
@@ -852,6 +887,7 @@ int ask_b200_plan_create(const char* recipe_json, int device, ask_b200_plan** ou
     else if (fam == "reduce") { pl->family = FAM_REDUCE; build_reduce(*pl, r); }
     else if (fam == "gather") { pl->family = FAM_GATHER; build_index(*pl, r, false); }
     else if (fam == "scatter_add") { pl->family = FAM_SCATTER; build_index(*pl, r, true); }
+    else if (fam == "softmax") { pl->family = FAM_SOFTMAX; build_softmax(*pl, r); }
     else fail(ASK_B200_E_UNSUPPORTED, "unknown family '" + fam + "'");
     if (pl->inputs.size() + pl->outputs.size() > 64)
       fail(ASK_B200_E_UNSUPPORTED, "the pointer ABI supports at most 64 input and output buffers");

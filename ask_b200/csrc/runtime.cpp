@@ -194,6 +194,7 @@ struct Step {
   std::vector<size_t> ports;  // logical buffers bound to the plan's inputs then outputs
   size_t n_inputs = 0;
   size_t scratch = kNone;     // private logical buffer for the plan's scratch
+  size_t scratch_bytes = 0;
   bool copy = false;
   size_t copy_src = 0, copy_dst = 0;
   std::vector<size_t> touches;  // every buffer whose address the step's launch holds
@@ -275,6 +276,41 @@ std::vector<size_t> index_list(const json::Value& v, const char* what) {
   return out;
 }
 
+// The reference partitions a row softmax into three owned steps (row max of
+// cast(x), row sum of exp(cast(x) - max), normalise).  Three consecutive steps
+// that are exactly those, bound as (x)->(m), (x, m)->(s), (x, m, s)->(y),
+// become one fused softmax plan (softmax_kernels.cu) that still writes m, s
+// and y: x is read once instead of three times and exp is computed once per
+// element.  A program can opt out with "fuse": false.
+void fuse_softmax(State& st, Program& p) {
+  for (size_t i = 0; i + 2 < p.steps.size(); ++i) {
+    const Step &a = p.steps[i], &b = p.steps[i + 1], &c = p.steps[i + 2];
+    std::string dt;
+    for (const char* t : {"f16", "bf16"})
+      if (a.kernel == std::string("reduce_warp_row_softmax_max_") + t &&
+          b.kernel == std::string("reduce_warp_row_softmax_sum_") + t && c.kernel == std::string("ew_softmax_norm_") + t)
+        dt = t;
+    if (dt.empty() || a.copy || b.copy || c.copy || a.ports.size() != 2 || b.ports.size() != 3 || c.ports.size() != 4)
+      continue;
+    const size_t x = a.ports[0], m = a.ports[1], s = b.ports[2], y = c.ports[3];
+    if (b.ports[0] != x || b.ports[1] != m || c.ports[0] != x || c.ports[1] != m || c.ports[2] != s) continue;
+    const uint64_t rows = p.sizes[m] / 4, cols = rows ? p.sizes[x] / 2 / rows : 0;
+    if (!rows || rows * cols * 2 != p.sizes[x]) continue;
+    const std::string recipe = "{\"family\":\"softmax\",\"dtype\":\"" + dt + "\",\"rows\":" + std::to_string(rows) +
+                               ",\"cols\":" + std::to_string(cols) + "}";
+    ask_b200_plan* raw = nullptr;
+    if (ask_b200_plan_create(recipe.c_str(), st.device, &raw) != ASK_B200_OK) continue;  // no fused kernel: keep 3 steps
+    Step fused;
+    fused.plan.reset(raw, PlanDeleter());
+    fused.kernel = std::string("softmax_rows_") + dt;
+    fused.ports = {x, m, s, y};
+    fused.n_inputs = 1;
+    p.steps.erase(p.steps.begin() + long(i), p.steps.begin() + long(i) + 3);
+    p.steps.insert(p.steps.begin() + long(i), std::move(fused));
+    ++st.counters["fused_softmax_steps"];
+  }
+}
+
 std::shared_ptr<Program> prepare(const std::shared_ptr<State>& st, const char* text, bool graph) {
   require(text != nullptr, "program JSON is NULL");
   const json::Value root = json::Parser(text).parse();
@@ -350,20 +386,27 @@ std::shared_ptr<Program> prepare(const std::shared_ptr<State>& st, const char* t
       step.copy_src = size_t(src);
       step.copy_dst = size_t(dst);
     }
-    check::StepPorts sp{ins, outs};
     ask_b200_plan_scratch_bytes(raw, &scratch);
-    if (scratch) {  // a private logical buffer with this step's lifetime
-      step.scratch = alloc.buffer_sizes.size();
-      sp.outputs.push_back(step.scratch);
-      alloc.buffer_sizes.push_back(scratch);
-    }
-    step.touches = step.ports;
-    if (step.scratch != kNone) step.touches.push_back(step.scratch);
-    alloc.plan.steps.push_back(sp);
+    step.scratch_bytes = scratch;
     available.insert(outs.begin(), outs.end());
     p->steps.push_back(std::move(step));
   }
   require(available.size() == declared, "program contains an undefined buffer");
+  const json::Value* fuse = root.get("fuse");
+  if (!fuse || fuse->kind != json::Value::Bool || fuse->b) fuse_softmax(*st, *p);
+  for (Step& step : p->steps) {
+    check::StepPorts sp;
+    sp.inputs.assign(step.ports.begin(), step.ports.begin() + long(step.n_inputs));
+    sp.outputs.assign(step.ports.begin() + long(step.n_inputs), step.ports.end());
+    if (step.scratch_bytes) {  // a private logical buffer with this step's lifetime
+      step.scratch = alloc.buffer_sizes.size();
+      sp.outputs.push_back(step.scratch);
+      alloc.buffer_sizes.push_back(step.scratch_bytes);
+    }
+    step.touches = step.ports;
+    if (step.scratch != kNone) step.touches.push_back(step.scratch);
+    alloc.plan.steps.push_back(sp);
+  }
   alloc.plan.buffer_count = alloc.buffer_sizes.size();
   if (graph)
     check::assign_graph_slots(alloc);
@@ -689,7 +732,7 @@ int ask_b200_session_create(int device, ask_b200_session** out) {
     cuda_check(cudaStreamCreateWithFlags(&st->capture, cudaStreamNonBlocking), "cudaStreamCreate");
     for (const char* k : {"allocations", "launches", "program_submissions", "workspace_reuses", "prepared_internal_slots",
                           "prepared_internal_bytes", "graph_instantiations", "graph_launches", "graph_nodes",
-                          "graph_edges", "graph_node_updates"})
+                          "graph_edges", "graph_node_updates", "fused_softmax_steps"})
       st->counters[k] = 0;
     *out = new ask_b200_session{st};
   });

@@ -220,9 +220,12 @@ class Session:
         return self.importBuffer(int(tensor.data_ptr()), tensor.numel() * tensor.element_size(), readonly)
 
     def prepareProgram(self, sizes: Sequence[int], inputs: Sequence[int], outputs: Sequence[int],
-                       steps: Sequence[PlanStep], graph: bool = False) -> PreparedProgram:
+                       steps: Sequence[PlanStep], graph: bool = False, fuse: bool = True) -> PreparedProgram:
+        """``fuse=False`` keeps a three-step softmax as three steps (by default
+        the runtime runs it as one fused step that writes the same buffers)."""
         text = json.dumps({"buffer_sizes": [int(s) for s in sizes], "inputs": [int(i) for i in inputs],
-                           "outputs": [int(o) for o in outputs], "steps": [s.to_json() for s in steps]})
+                           "outputs": [int(o) for o in outputs], "steps": [s.to_json() for s in steps],
+                           "fuse": bool(fuse)})
         h = _p()
         _check(_lib.ask_b200_program_prepare(self._h, text.encode(), 1 if graph else 0, ctypes.byref(h)))
         return PreparedProgram(h, self, len(outputs))

@@ -205,13 +205,29 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         m = torch.empty(rows, dtype=torch.float32, device=dev)
         s = torch.empty(rows, dtype=torch.float32, device=dev)
         y = torch.empty_like(x)
-        ps = [ask_b200.Plan(r, rank_device()) for r in R.cfg3_steps(dt, rows, cols)]
-        w.plans = ps
+        # The reference's plan: three owned steps over x, m, s, y.  The runtime
+        # layer runs them as one fused softmax step (graph mode); the graded bytes
+        # stay the plan's port bytes (x read by all three steps).
+        from ask_b200 import runtime as rt
         n = rows * cols
-        w.kernels = [(f"reduce_softmax_max_{dt}", 2 * n + 4 * rows, ps[0].bind([x], [m], None, st)),
-                     (f"reduce_softmax_sum_{dt}", 2 * n + 8 * rows, ps[1].bind([x, m], [s], None, st)),
-                     (f"ew_softmax_norm_{dt}", 4 * n + 8 * rows, ps[2].bind([x, m, s], [y], None, st))]
-        w.config = static_config(name, world)
+        session = rt.Session.create(rank_device())
+        steps = R.cfg3_steps(dt, rows, cols)
+        prog = session.prepareProgram([2 * n, 4 * rows, 4 * rows, 2 * n], [0], [1, 2, 3],
+                                      [rt.PlanStep(steps[0], [0], [1]), rt.PlanStep(steps[1], [0, 1], [2]),
+                                       rt.PlanStep(steps[2], [0, 1, 2], [3])], graph=True)
+        kernel = prog.describe()["steps"][0]["kernel"]
+        xin = session.importTensor(x, readonly=True)
+        bufs = [session.importTensor(t) for t in (m, s, y)]
+
+        def run():
+            prog.submit([xin], bufs)
+        w.plans = [ask_b200.Plan({"family": "softmax", "dtype": dt, "rows": rows, "cols": cols}, rank_device())]
+        w.kernels = [(kernel, 4 * n + 8 * rows, run)]
+        w.global_bytes = 4 * 2 * n + 6 * 4 * rows
+        w.session, w.program, w.stream_handle = session, prog, session.stream()
+        w.config = dict(static_config(name, world),
+                        plan=f"3 owned steps (max, sum of exp, normalise) run by the runtime as one {kernel} step, "
+                             "CUDA graph", graded_bytes="plan port bytes 4*2n + 6*4*rows")
         w.dtype = dt
         w.e2e = {"inputs": [x], "results": [y]}
     elif name in ("cfg4g", "cfg4s"):
@@ -239,7 +255,8 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         w.plans = [p]
     else:
         raise SystemExit(f"unknown workload {name}")
-    w.global_bytes = w.bytes_per_step()
+    if not hasattr(w, "global_bytes"):
+        w.global_bytes = w.bytes_per_step()
     return w
 
 
@@ -363,8 +380,10 @@ def main():
         torch.cuda.synchronize()
 
     w = make_workload(args.workload, rank, world, torch, ask_b200, R, comm, small=args.small)
-    st = torch.cuda.current_stream()
     torch.cuda.synchronize()
+    if getattr(w, "stream_handle", None):  # a runtime session's stream: time and copy on it
+        torch.cuda.set_stream(torch.cuda.ExternalStream(w.stream_handle))
+    st = torch.cuda.current_stream()
 
     # warm-up
     for _ in range(max(args.warmup, 3)):

@@ -183,6 +183,70 @@ def test_cfg3_softmax_full_size(device, dtype):
     assert np.all(np.abs(rowsum - 1.0) < 0.02)
 
 
+def _softmax_check(dtype, xh, rows, cols, gm, gs, gy):
+    rm, rs, ry = oracle.softmax(dtype, xh, rows, cols, threads=THREADS)
+    assert same_with_nan(gm, rm)  # NaN payloads are the device's canonical NaN
+    fin = np.isfinite(rs)
+    assert np.array_equal(np.isnan(gs), np.isnan(rs))
+    assert np.all(np.abs(gs[fin].astype(np.float64) - rs[fin]) <= 2.0 ** -20 * np.abs(rs[fin]))
+    conv = f16_to_f32 if dtype == "f16" else bf16_to_f32
+    gyv, ryv = conv(gy), conv(ry)
+    nan = np.isnan(ryv)
+    assert np.array_equal(np.isnan(gyv), nan)
+    step = np.spacing(np.abs(ryv[~nan]).astype(np.float16)).astype(np.float32) if dtype == "f16" else \
+        np.abs(bf16_to_f32(ry[~nan] + 1) - ryv[~nan])
+    assert np.all(np.abs(gyv[~nan] - ryv[~nan]) <= step + 1e-45), "softmax output differs by more than 1 ulp"
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("rows,cols", [(1, 256), (37, 1024), (300, 4096), (19, 8192), (5, 32768), (130, 2304)])
+def test_fused_softmax_against_oracle(device, dtype, rows, cols):
+    kind = 2 if dtype == "f16" else 3
+    x = gen_dev(kind, 0xA5C3, 7, rows * cols, 0.0, 3.0, torch.int16)
+    xh = x.cpu().numpy().view(np.uint16).copy()
+    # special rows: a NaN, +inf, -inf everywhere, all -0, a huge spread (exp underflows to 0)
+    nan16, inf16, ninf16 = (0x7E00, 0x7C00, 0xFC00) if dtype == "f16" else (0x7FC0, 0x7F80, 0xFF80)
+    big = 0x7BFF if dtype == "f16" else 0x7F7F
+    specials = [(0, 5, nan16), (min(1, rows - 1), 3, inf16)]
+    for r, c, v in specials:
+        xh[r * cols + c] = v
+    if rows > 4:
+        xh[2 * cols:3 * cols] = ninf16
+        xh[3 * cols:4 * cols] = 0x8000
+        xh[4 * cols] = big
+    x = torch.from_numpy(xh.view(np.int16)).cuda()
+    plan = ask_b200.Plan({"family": "softmax", "dtype": dtype, "rows": rows, "cols": cols}, 0)
+    assert plan.describe()["kernel"] == f"softmax_rows_{dtype}"
+    m = torch.empty(rows, dtype=torch.float32, device="cuda")
+    s = torch.empty(rows, dtype=torch.float32, device="cuda")
+    y = torch.empty_like(x)
+    plan.launch([x], [m, s, y], None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    _softmax_check(dtype, xh, rows, cols, m.cpu().numpy(), s.cpu().numpy(),
+                   y.cpu().numpy().view(np.uint16).reshape(-1))
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_fused_softmax_full_size_matches_three_steps(device, dtype):
+    rows, cols = 32768, 4096
+    x = gen_dev(2 if dtype == "f16" else 3, 0xA5C3, 0, rows * cols, 0.0, 2.0, torch.int16)
+    st = torch.cuda.current_stream()
+    m3, s3 = (torch.empty(rows, dtype=torch.float32, device="cuda") for _ in range(2))
+    y3 = torch.empty_like(x)
+    steps = [ask_b200.Plan(r, 0) for r in R.cfg3_steps(dtype, rows, cols)]
+    steps[0].launch([x], [m3], None, st)
+    steps[1].launch([x, m3], [s3], None, st)
+    steps[2].launch([x, m3, s3], [y3], None, st)
+    m1, s1 = (torch.empty(rows, dtype=torch.float32, device="cuda") for _ in range(2))
+    y1 = torch.empty_like(x)
+    ask_b200.Plan({"family": "softmax", "dtype": dtype, "rows": rows, "cols": cols}, 0).launch([x], [m1, s1, y1], None, st)
+    torch.cuda.synchronize()
+    assert torch.equal(m1.view(torch.int32), m3.view(torch.int32))
+    assert torch.all((s1.double() - s3.double()).abs() <= 2.0 ** -21 * s3.double().abs())
+    d = (y1.view(torch.int16).int() - y3.view(torch.int16).int()).abs()
+    assert int(d.max()) <= 1 and float((d != 0).float().mean()) < 1e-3
+
+
 # ---- cfg4: gather / scatter_add ---------------------------------------------------------
 @pytest.mark.parametrize("itype", ["i64", "i32"])
 @pytest.mark.parametrize("inner,dtype", [(256, "f32"), (3, "f32"), (8, "f16"), (5, "i64"), (64, "bool")])

@@ -160,8 +160,9 @@ def direct(plan_recipe, ins, outs, scratch_bytes=0):
 
 
 @pytest.mark.parametrize("graph", [False, True])
+@pytest.mark.parametrize("fuse", [False, True])
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_softmax_program_matches_direct_steps(device, graph, dtype):
+def test_softmax_program_matches_direct_steps(device, graph, fuse, dtype):
     rows, cols = 512, 4096
     kind = 2 if dtype == "f16" else 3
     x = gen_dev(kind, 0xA5C3, 0, rows * cols, 0.0, 2.0, torch.int16)
@@ -176,21 +177,30 @@ def test_softmax_program_matches_direct_steps(device, graph, dtype):
 
     session = rt.Session.create(0)
     program = session.prepareProgram(
-        [2 * rows * cols, 4 * rows, 4 * rows, 2 * rows * cols], [0], [3],
+        [2 * rows * cols, 4 * rows, 4 * rows, 2 * rows * cols], [0], [1, 2, 3],
         [rt.PlanStep(steps[0], [0], [1]), rt.PlanStep(steps[1], [0, 1], [2]), rt.PlanStep(steps[2], [0, 1, 2], [3])],
-        graph)
+        graph, fuse=fuse)
     d = program.describe()
-    assert [k["kernel"] for k in d["steps"]] == [f"reduce_warp_row_softmax_max_{dtype}",
-                                                 f"reduce_warp_row_softmax_sum_{dtype}", f"ew_softmax_norm_{dtype}"]
-    assert len(d["slot_capacity_bytes"]) == 2  # m and s live in workspace slots
+    if fuse:  # the runtime runs the three steps as one fused softmax step
+        assert [k["kernel"] for k in d["steps"]] == [f"softmax_rows_{dtype}"]
+        assert session.stats()["fused_softmax_steps"] == 1
+    else:
+        assert [k["kernel"] for k in d["steps"]] == [f"reduce_warp_row_softmax_max_{dtype}",
+                                                     f"reduce_warp_row_softmax_sum_{dtype}", f"ew_softmax_norm_{dtype}"]
     xin = session.importTensor(x, readonly=True)
-    y = torch.empty_like(y_ref)
-    yout = session.importTensor(y)
+    outs = [torch.empty_like(m), torch.empty_like(s), torch.empty_like(y_ref)]
+    bufs = [session.importTensor(t) for t in outs]
     session.waitForExternalStream(torch.cuda.current_stream())
     for _ in range(3):
-        program.submit([xin], [yout]).wait()
-        assert torch.equal(y, y_ref)
-        y.zero_()
+        program.submit([xin], bufs).wait()
+        assert torch.equal(outs[0].view(torch.int32), m.view(torch.int32))
+        if fuse:  # the fused sum may round differently in the last place; y then by at most one unit
+            assert torch.all((outs[1].double() - s.double()).abs() <= 2.0 ** -21 * s.double().abs())
+            assert int((outs[2].int() - y_ref.int()).abs().max()) <= 1
+        else:
+            assert torch.equal(outs[1].view(torch.int32), s.view(torch.int32)) and torch.equal(outs[2], y_ref)
+        for t in outs:
+            t.zero_()
         torch.cuda.synchronize()
 
 
