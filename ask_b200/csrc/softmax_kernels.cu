@@ -12,9 +12,9 @@
 // writes y (and m, s) -- 2 bytes read and 2 written per element instead of 8.
 // The next row's vectors are loaded before this row's reductions.
 //
-// Semantics per element are those of the three steps: max folds with fmaxf
-// (which orders -0 < +0) and becomes the canonical NaN when the row holds a
-// NaN (llvm.maximum); exp(x + m*(-1)) with CUDA's expf; the division is the
+// Semantics per element are those of the three steps: max folds with
+// max.NaN.f32 (llvm.maximum: the canonical NaN when the row holds a NaN,
+// -0 < +0); exp(x + m*(-1)) with CUDA's expf; the division is the
 // correctly rounded f32 quotient (one reciprocal per row and Markstein's
 // correction, with the IEEE division for any unit outside its conditions, as
 // in the softmax normalise kernel); f16/bf16 rounding to nearest even.  The sum
@@ -59,6 +59,14 @@ __device__ __forceinline__ uint32_t narrow_two(float lo, float hi) {
   return r;
 }
 
+// llvm.maximum on f32 in one instruction: NaN if either operand is NaN (the
+// canonical NaN), otherwise the larger, with -0 < +0.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
 constexpr int kMaxWarps = 16;
 #ifndef ASKB_SOFTMAX_THREADS
 #define ASKB_SOFTMAX_THREADS 128
@@ -94,21 +102,20 @@ __global__ void __launch_bounds__(kMaxWarps * 32) softmax_rows_kernel(const uint
 #pragma unroll
       for (int q = 0; q < VPT; ++q) v[q] = ld_stream_v4(x + next * vecs + q * blockDim.x + threadIdx.x);
     }
-    // m = max over the row
-    float mx = e[0];
-    bool nan = e[0] != e[0];
+    // m = max over the row (NaN-propagating); the thread's smallest value
+    // bounds its exp results from below for the division's check
+    float mx = e[0], mn = e[0];
 #pragma unroll
     for (int k = 1; k < VPT * 8; ++k) {
-      mx = fmaxf(mx, e[k]);
-      nan |= e[k] != e[k];
+      mx = max_nan(mx, e[k]);
+      mn = fminf(mn, e[k]);
     }
 #pragma unroll
-    for (int d = 16; d; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+    for (int d = 16; d; d >>= 1) mx = max_nan(mx, __shfl_xor_sync(0xffffffffu, mx, d));
     if (lane == 0) red_max[parity][warp] = mx;
-    const bool any_nan = __syncthreads_or(nan) != 0;  // also publishes red_max
+    __syncthreads();
     float m = red_max[parity][0];
-    for (uint32_t k = 1; k < nwarps; ++k) m = fmaxf(m, red_max[parity][k]);
-    if (any_nan) m = __uint_as_float(0x7fffffffu);
+    for (uint32_t k = 1; k < nwarps; ++k) m = max_nan(m, red_max[parity][k]);
     const float nm = __fmul_rn(m, -1.0f);
     // e = exp(x + m*(-1)), s = sum of e
     float part = 0.0f;
@@ -129,13 +136,16 @@ __global__ void __launch_bounds__(kMaxWarps * 32) softmax_rows_kernel(const uint
       m_out[row] = m;
       s_out[row] = s;
     }
-    // y = cast(e / s): correctly rounded quotient from one reciprocal
+    // y = cast(e / s): the correctly rounded quotient from one reciprocal
+    // (Markstein's two corrections).  Its conditions hold for the whole thread
+    // when s and 1/s are normal and every e >= exp(-69) > 2^-100: then
+    // 2^-100 / s <= e / s <= 1 (e <= 1 because m is the row's maximum and
+    // s >= 1), so every quotient is normal.  Otherwise the IEEE division runs.
     const float r = __frcp_rn(s);
-    const bool row_ok = s >= 0x1p-100f && s <= 0x1p100f;
+    const bool ok = s >= 1.0f && s <= 0x1p100f && __fadd_rn(mn, nm) >= -69.0f;
 #pragma unroll
     for (int qv = 0; qv < VPT; ++qv) {
       float q[8];
-      bool ok = row_ok;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const float ek = e[qv * 8 + k];
@@ -143,7 +153,6 @@ __global__ void __launch_bounds__(kMaxWarps * 32) softmax_rows_kernel(const uint
         t = __fmaf_rn(__fmaf_rn(-t, s, ek), r, t);
         t = __fmaf_rn(__fmaf_rn(-t, s, ek), r, t);
         q[k] = t;
-        ok &= (t >= 0x1p-124f && t <= 0x1p126f) || ek == 0.0f;
       }
       uint32_t o[4];
       if (ok) {
