@@ -39,6 +39,7 @@ enum Op : uint8_t {
   OP_FLOOR, OP_CEIL, OP_ROUND,
   OP_CMP,         // aux = predicate, result bool; src_type = operand type
   OP_SELECT,      // a = bool condition, b = yes, c = no
+  OP_COORD,       // i64 coordinate of the element along axis aux of the iteration shape
   kNumOps
 };
 
@@ -61,6 +62,24 @@ enum IndexMap : uint8_t {
   IM_SCALAR = 1,  // 0-D buffer: element 0
   IM_OUTER = 2,   // elementwise: i / inner      reduce: indexed by the output (o*inner + n)
   IM_INNER = 3,   // elementwise: i % inner
+  IM_VIEW = 4,    // elementwise: a strided, windowed view of the port (PortView)
+};
+
+// A general index map for one port of an elementwise step over an iteration
+// shape of `rank` axes (the reference's broadcast_in_dim, transpose, slice,
+// pad and concatenate operand maps, ScalarEmitter.h:626-730).  For output
+// coordinate c_d the port coordinate is i_d = (c_d - lo[d]) / step[d]; the
+// element is valid when every c_d - lo[d] >= 0 is a multiple of step[d] and
+// i_d < extent[d], and is then read at offset + sum(i_d * stride[d]);
+// otherwise the port yields `pad` (a value word of the port's type).
+constexpr int kMaxRank = 6;
+struct PortView {
+  int64_t lo[kMaxRank];
+  int64_t step[kMaxRank];
+  int64_t extent[kMaxRank];
+  int64_t stride[kMaxRank];
+  int64_t offset;
+  uint64_t pad;
 };
 
 constexpr int kMaxInsn = 48;

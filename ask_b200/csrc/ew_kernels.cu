@@ -111,6 +111,59 @@ __global__ void __launch_bounds__(kEwThreads)
   }
 }
 
+// ---- general index maps ------------------------------------------------------------
+// One element per thread iteration: the element's coordinates in the iteration
+// shape are computed once, every IM_VIEW port maps them through its view, and
+// OP_COORD reads them.  Scalar loads and stores; this path serves the index
+// maps the fused kernels above have no vector form for.
+__global__ void __launch_bounds__(kEwThreads) ew_view_kernel(const __grid_constant__ Program prog,
+                                                             const __grid_constant__ EwArgs args,
+                                                             const __grid_constant__ ViewSet views) {
+  const uint64_t n = args.count;
+  const uint64_t nthreads = uint64_t(gridDim.x) * kEwThreads;
+  uint64_t r[kMaxRegs];
+  for (uint64_t i = uint64_t(blockIdx.x) * kEwThreads + threadIdx.x; i < n; i += nthreads) {
+    int64_t c[kMaxRank];
+    uint64_t rest = i;
+    for (int d = views.rank - 1; d >= 0; --d) {
+      const uint64_t e = views.shape[d];
+      c[d] = int64_t(rest % e);
+      rest /= e;
+    }
+    for (int k = 0; k < prog.n_insn; ++k) {
+      const Insn& ins = prog.insn[k];
+      if (ins.op == OP_INPUT) {
+        const int port = ins.a, t = prog.in_type[port];
+        const void* p = args.in[port];
+        switch (prog.in_map[port]) {
+          case IM_SCALAR: r[ins.dst] = word_from_storage(t, p, 0); break;
+          case IM_OUTER: r[ins.dst] = word_from_storage(t, p, i / args.inner.d); break;
+          case IM_INNER: r[ins.dst] = word_from_storage(t, p, i % args.inner.d); break;
+          case IM_VIEW: {
+            const PortView& v = views.port[port];
+            int64_t off = v.offset;
+            bool ok = true;
+            for (int d = 0; d < views.rank; ++d) {
+              const int64_t s = c[d] - v.lo[d];
+              const int64_t q = s / v.step[d];
+              ok = ok && s >= 0 && q * v.step[d] == s && q < v.extent[d];
+              off += q * v.stride[d];
+            }
+            r[ins.dst] = ok ? word_from_storage(t, p, uint64_t(off)) : v.pad;
+            break;
+          }
+          default: r[ins.dst] = word_from_storage(t, p, i); break;
+        }
+      } else if (ins.op == OP_COORD) {
+        r[ins.dst] = uint64_t(c[ins.aux]);
+      } else {
+        r[ins.dst] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a], r[ins.b], r[ins.c]);
+      }
+    }
+    for (int k = 0; k < prog.n_out; ++k) word_to_storage(prog.out_type[k], args.out[k], i, r[prog.out_reg[k]]);
+  }
+}
+
 // ---- hand-written functor kernels for the hottest programs ------------------------
 // Software-pipelined grid-stride loop over whole 16-byte units: the loads of the
 // next unit are in flight while the current unit is computed, so latency is
@@ -270,6 +323,18 @@ bool ew_spec_program(int spec, Program* out) {
 }
 
 int ew_num_specs() { return EW_NUM_SPECS; }
+
+cudaError_t ew_view_launch(const Program& prog, const EwArgs& args, const ViewSet& views, int grid, cudaStream_t stream) {
+  if (args.count == 0) return cudaSuccess;
+  ew_view_kernel<<<dim3(grid), dim3(kEwThreads), 0, stream>>>(prog, args, views);
+  return cudaGetLastError();
+}
+
+int ew_view_occupancy() {
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, ew_view_kernel, kEwThreads, 0) != cudaSuccess) return 1;
+  return blocks > 0 ? blocks : 1;
+}
 
 cudaError_t ew_occupancy(int spec, int* blocks_per_sm) {
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, ew_kernel_ptr(spec), kEwThreads, 0);

@@ -126,6 +126,17 @@ cudaError_t scatter_sorted_launch(const IndexArgs& a, void* scratch, int sms, cu
 
 // ---- input synthesis (Philox4x32-10) -------------------------------------------------
 enum GenKind : int { GEN_UNIFORM_F32 = 0, GEN_NORMAL_F32, GEN_NORMAL_F16, GEN_NORMAL_BF16, GEN_I32, GEN_ZIPF_I64, GEN_ZIPF_I32 };
+// Elementwise steps with general index maps (IM_VIEW ports) or coordinate
+// instructions: the runtime-program interpreter with per-element coordinates.
+struct ViewSet {
+  int rank;
+  uint64_t shape[kMaxRank];
+  PortView port[kMaxIn];
+};
+cudaError_t ew_view_launch(const Program& prog, const EwArgs& args, const ViewSet& views, int grid,
+                           cudaStream_t stream);
+int ew_view_occupancy();
+
 // Family S: the three-step softmax plan fused (softmax_kernels.cu).  x and y
 // are [rows, cols] f16/bf16 (16-byte aligned), m and s are [rows] f32.
 struct SoftmaxArgs {

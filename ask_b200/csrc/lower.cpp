@@ -18,12 +18,15 @@
 //   - any other step of elementwise ops becomes an "elementwise" recipe.
 // Arguments enter the op program with an index map: the full output shape,
 // a scalar, a prefix of the output axes ("outer": broadcast_in_dim with
-// dimensions 0..k-1) or a suffix ("inner").  ask.constant/ask.splat become
+// dimensions 0..k-1), a suffix ("inner"), or -- for transpose, slice, pad,
+// general broadcasts and reshapes of an argument -- a strided, windowed view
+// (IM_VIEW; pad's elements outside the window read its constant pad value).
+// concatenate becomes views of its operands selected by the coordinate along
+// its axis, iota a cast of that coordinate.  ask.constant/ask.splat become
 // constants (MLIR prints each float literal so that it re-parses exactly, or
-// as its bit pattern in hex; either is carried over without double rounding),
-// ask.reshape of an argument is the argument itself.  Ops this library has no
-// index map for (transpose, slice, pad, concatenate, iota) and matmul or
-// external steps are reported as unsupported.
+// as its bit pattern in hex; either is carried over without double rounding).
+// An index map of a computed value (the reference re-evaluates the value at
+// the mapped index) and matmul or external steps are reported as unsupported.
 #include <algorithm>
 #include <cctype>
 #include <cstdio>
@@ -457,6 +460,18 @@ struct Lowered {
   std::vector<size_t> input_args;  // recipe input k reads function argument input_args[k]
 };
 
+// A value that is only an index map of a step argument: for each axis of the
+// value's shape the argument coordinate (c - lo) / step (valid while
+// non-negative, divisible and below extent) and its element stride, plus a
+// base offset and the value outside the window (ScalarEmitter.h:626-730).
+struct ArgView {
+  size_t arg = 0;
+  std::vector<int64_t> lo, step, extent, stride;
+  int64_t offset = 0;
+  std::string pad = "0";  // JSON constant for elements outside the window
+  bool windowed(size_t d) const { return lo[d] != 0 || step[d] != 1; }
+};
+
 class Lowering {
  public:
   explicit Lowering(const Func& f) : f_(f) {
@@ -483,18 +498,25 @@ class Lowering {
   }
 
  private:
+  struct Port {
+    size_t arg;
+    std::string map;   // full, scalar, outer, inner, view
+    std::string view;  // the view's JSON for map == view
+  };
   const Func& f_;
   std::map<std::string, size_t> arg_, def_;
-  // op program under construction
+  // op program under construction; insn_port_[i] >= 0 marks an input instruction
   std::vector<std::string> insns_;
+  std::vector<int> insn_port_;
   std::vector<std::string> types_;
   std::map<std::string, int> memo_;
-  std::vector<std::string> arg_map_;   // per argument: "", full, scalar, outer, inner
-  std::vector<int> arg_insn_;
+  std::vector<Port> ports_;
+  std::vector<int> port_insn_;
   std::vector<int64_t> out_shape_;
-  size_t lead_ = 0;                    // reduce: number of leading (outer) axes
-  uint64_t map_inner_ = 0;             // elementwise: the 'inner' every outer/inner map shares
+  size_t lead_ = 0;            // reduce: number of leading (outer) axes
+  uint64_t map_inner_ = 0;     // elementwise: the 'inner' every outer/inner map shares
   bool is_reduce_ = false;
+  bool uses_shape_ = false;    // a view or a coordinate needs the iteration shape
 
   static bool is_reduction(const std::string& n) { return n.rfind("reduce_", 0) == 0 || n == "argmax" || n == "argmin"; }
 
@@ -509,19 +531,27 @@ class Lowering {
     if (!p) invalid("value " + v + " is not defined");
     return p->type;
   }
-  int emit(const std::string& insn, const std::string& dtype) {
+  static std::vector<int64_t> arr(const Op& p, const char* key) {
+    auto it = p.attrs.find(key);
+    if (it == p.attrs.end()) invalid("ask." + strip(p.name) + " needs '" + key + "'");
+    return it->second.arr;
+  }
+  int emit(const std::string& insn, const std::string& dtype, int port = -1) {
     insns_.push_back(insn);
+    insn_port_.push_back(port);
     types_.push_back(dtype);
     return int(insns_.size()) - 1;
   }
-  // Argument `a` read with index map `map`: one recipe input per argument.
-  int use_arg(size_t a, const std::string& map) {
-    if (arg_map_[a].empty()) arg_map_[a] = map;
-    if (arg_map_[a] != map)
-      unsupported("argument " + std::to_string(a) + " is read through two index maps (" + arg_map_[a] + ", " + map + ")");
-    return arg_insn_[a];
+  // One recipe input per distinct (argument, index map, view).
+  int use_port(size_t arg, const std::string& map, const std::string& view = "") {
+    for (size_t k = 0; k < ports_.size(); ++k)
+      if (ports_[k].arg == arg && ports_[k].map == map && ports_[k].view == view) return port_insn_[k];
+    ports_.push_back({arg, map, view});
+    port_insn_.push_back(emit("", f_.arg_types[arg].dtype, int(ports_.size()) - 1));
+    if (map == "view") uses_shape_ = true;
+    return port_insn_.back();
   }
-  std::string constant(const Op& op) {
+  std::string constant_text(const Op& op) const {
     auto it = op.attrs.find("value");
     if (it == op.attrs.end()) invalid("ask.constant without a value");
     const Attr& v = it->second;
@@ -534,13 +564,10 @@ class Lowering {
     if (v.kind == Attr::Int || (v.kind == Attr::Float && (v.text.find("0x") != std::string::npos ||
                                                           v.text.find("0X") != std::string::npos)))
       return json_str("bits:" + v.text);  // MLIR prints an inexact float literal as its bit pattern
-    if (v.kind == Attr::Float) {
-      if (v.text == "nan" || v.text == "inf" || v.text == "-inf") return json_str(v.text);
-      return json_str(v.text);  // decimal text: rounded once to the constant's type
-    }
+    if (v.kind == Attr::Float) return json_str(v.text);  // decimal text: rounded once to the constant's type
     invalid("unsupported constant value");
   }
-  // The scalar value behind a splat / broadcast of a constant, if any.
+  // The scalar constant behind a splat / broadcast / reshape chain, if any.
   const Op* scalar_source(const std::string& v) const {
     const Op* p = producer(v);
     while (p) {
@@ -555,36 +582,169 @@ class Lowering {
     }
     return nullptr;
   }
-  // Index map of an argument broadcast to the output shape.
-  std::string broadcast_map(const Type& from, const std::vector<int64_t>& dims) {
+
+  // ---- views ---------------------------------------------------------------------------
+  static std::vector<int64_t> row_major(const std::vector<int64_t>& shape) {
+    std::vector<int64_t> s(shape.size(), 1);
+    for (size_t d = shape.size(); d-- > 1;) s[d - 1] = s[d] * shape[d];
+    return s;
+  }
+  bool view_of(const std::string& v, ArgView* out) const {
+    auto a = arg_.find(v);
+    const Type& t = type_of(v);
+    if (a != arg_.end()) {
+      out->arg = a->second;
+      out->lo.assign(t.shape.size(), 0);
+      out->step.assign(t.shape.size(), 1);
+      out->extent = t.shape;
+      out->stride = row_major(t.shape);
+      out->offset = 0;
+      return true;
+    }
+    const Op* p = producer(v);
+    if (!p) return false;
+    const std::string n = strip(p->name);
+    ArgView in;
+    if (n == "transpose") {
+      if (!view_of(p->operands.at(0), &in)) return false;
+      const auto perm = arr(*p, "permutation");
+      *out = in;
+      for (size_t d = 0; d < perm.size(); ++d) {
+        const size_t s = size_t(perm[d]);
+        out->lo[d] = in.lo[s];
+        out->step[d] = in.step[s];
+        out->extent[d] = in.extent[s];
+        out->stride[d] = in.stride[s];
+      }
+      return true;
+    }
+    if (n == "broadcast_in_dim") {
+      if (!view_of(p->operands.at(0), &in)) return false;
+      const auto dims = arr(*p, "dimensions");
+      const Type& it = type_of(p->operands.at(0));
+      const size_t r = t.shape.size();
+      *out = in;
+      out->lo.assign(r, 0);
+      out->step.assign(r, 1);
+      out->extent = t.shape;
+      out->stride.assign(r, 0);
+      for (size_t k = 0; k < dims.size(); ++k) {
+        const size_t d = size_t(dims[k]);
+        if (it.shape[k] == 1) {  // a broadcast axis: stays at the argument's coordinate 0
+          if (in.windowed(k)) return false;
+          continue;
+        }
+        out->lo[d] = in.lo[k];
+        out->step[d] = in.step[k];
+        out->extent[d] = in.extent[k];
+        out->stride[d] = in.stride[k];
+      }
+      return true;
+    }
+    if (n == "slice") {
+      if (!view_of(p->operands.at(0), &in)) return false;
+      const auto starts = arr(*p, "starts");
+      const auto steps = arr(*p, "steps");
+      *out = in;
+      for (size_t d = 0; d < t.shape.size(); ++d) {
+        if (in.windowed(d)) return false;
+        out->offset += starts[d] * in.stride[d];
+        out->stride[d] = in.stride[d] * steps[d];
+        out->extent[d] = t.shape[d];
+      }
+      return true;
+    }
+    if (n == "pad") {
+      if (!view_of(p->operands.at(0), &in)) return false;
+      const Op* c = scalar_source(p->operands.at(1));
+      if (!c) return false;  // a computed pad value needs a select, not a view
+      const auto low = arr(*p, "pad_low");
+      const auto interior = arr(*p, "interior");
+      *out = in;
+      for (size_t d = 0; d < t.shape.size(); ++d) {
+        if (in.windowed(d)) return false;
+        out->lo[d] = low[d];
+        out->step[d] = interior[d] + 1;
+      }
+      out->pad = constant_text(*c);
+      return true;
+    }
+    if (n == "reshape") {
+      if (!view_of(p->operands.at(0), &in)) return false;
+      const Type& it = type_of(p->operands.at(0));
+      if (in.offset != 0 || in.stride != row_major(it.shape) || in.extent != it.shape) return false;
+      for (size_t d = 0; d < in.lo.size(); ++d)
+        if (in.windowed(d)) return false;
+      out->arg = in.arg;
+      out->lo.assign(t.shape.size(), 0);
+      out->step.assign(t.shape.size(), 1);
+      out->extent = t.shape;
+      out->stride = row_major(t.shape);
+      out->offset = 0;
+      return true;
+    }
+    return false;
+  }
+  static bool is_identity(const ArgView& w, const Type& arg, const std::vector<int64_t>& shape) {
+    if (arg.numel() != product(shape, 0, shape.size()) || w.offset != 0) return false;
+    return w.stride == row_major(shape) && w.extent == shape &&
+           std::all_of(w.lo.begin(), w.lo.end(), [](int64_t x) { return x == 0; }) &&
+           std::all_of(w.step.begin(), w.step.end(), [](int64_t x) { return x == 1; });
+  }
+  std::string view_json(const ArgView& w) const {
+    auto list = [](const std::vector<int64_t>& v) {
+      std::string o = "[";
+      for (size_t i = 0; i < v.size(); ++i) o += (i ? "," : "") + std::to_string(v[i]);
+      return o + "]";
+    };
+    return "{\"elements\":" + std::to_string(f_.arg_types[w.arg].numel()) + ",\"offset\":" + std::to_string(w.offset) +
+           ",\"lo\":" + list(w.lo) + ",\"step\":" + list(w.step) + ",\"extent\":" + list(w.extent) +
+           ",\"stride\":" + list(w.stride) + ",\"pad\":" + w.pad + "}";
+  }
+  int use_view(const ArgView& w) {
+    if (is_reduce_) unsupported("reductions read no strided or windowed views");
+    return use_port(w.arg, "view", view_json(w));
+  }
+
+  // Index map of an argument broadcast to the output shape (the fast maps).
+  bool simple_broadcast(const Type& from, const std::vector<int64_t>& dims, std::string* map) {
     const size_t r = out_shape_.size(), k = dims.size();
-    if (from.numel() == 1) return "scalar";
+    if (from.numel() == 1) { *map = "scalar"; return true; }
     bool prefix = true, suffix = true;
     for (size_t i = 0; i < k; ++i) {
-      prefix = prefix && dims[i] == int64_t(i);
-      suffix = suffix && dims[i] == int64_t(r - k + i);
+      prefix = prefix && dims[i] == int64_t(i) && from.shape[i] == out_shape_[i];
+      suffix = suffix && dims[i] == int64_t(r - k + i) && from.shape[i] == out_shape_[r - k + i];
     }
     if (is_reduce_) {
-      if (prefix && k == lead_) return "outer";
-      unsupported("a broadcast operand of a reduction must be indexed by exactly the kept leading axes");
+      if (prefix && k == lead_) { *map = "outer"; return true; }
+      return false;
     }
+    if (!prefix && !suffix) return false;
     const uint64_t inner = prefix ? product(out_shape_, k, r) : product(out_shape_, r - k, r);
-    if (!prefix && !suffix) unsupported("broadcast_in_dim over non-leading, non-trailing axes needs a general index map");
-    if (map_inner_ && map_inner_ != inner)
-      unsupported("outer/inner broadcasts of different extents in one step");
+    if (map_inner_ && map_inner_ != inner) return false;
     map_inner_ = inner;
-    return prefix ? "outer" : "inner";
+    *map = prefix ? "outer" : "inner";
+    return true;
+  }
+  int coord(int64_t axis) {
+    uses_shape_ = true;
+    if (is_reduce_) unsupported("iota and concatenate inside a reduction");
+    return emit("[\"coord\"," + std::to_string(axis) + "]", "i64");
   }
   int value(const std::string& v) {
     auto m = memo_.find(v);
     if (m != memo_.end()) return m->second;
-    int id;
+    int id = -1;
+    const Type& vt = type_of(v);
     auto a = arg_.find(v);
     if (a != arg_.end()) {
-      const Type& t = f_.arg_types[a->second];
-      if (t.shape != out_shape_ && t.numel() != product(out_shape_, 0, out_shape_.size()))
+      if (vt.numel() == 1 && product(out_shape_, 0, out_shape_.size()) != 1) {
+        id = use_port(a->second, "scalar");
+      } else if (vt.numel() == product(out_shape_, 0, out_shape_.size())) {
+        id = use_port(a->second, "full");
+      } else {
         unsupported("argument " + v + " does not have the step's iteration shape; broadcast it explicitly");
-      id = use_arg(a->second, t.numel() == 1 && product(out_shape_, 0, out_shape_.size()) != 1 ? "scalar" : "full");
+      }
       memo_[v] = id;
       return id;
     }
@@ -596,27 +756,68 @@ class Lowering {
       if (k >= p->operands.size()) invalid("ask." + n + " is missing an operand");
       return value(p->operands[k]);
     };
+    ArgView w;
     if (n == "constant") {
-      id = emit("[\"const\"," + json_str(dt) + "," + constant(*p) + "]", dt);
-    } else if (n == "splat" || n == "broadcast_in_dim" || n == "reshape") {
-      if (const Op* c = scalar_source(v)) {
-        id = value(c->result);
-      } else if (n == "reshape") {
-        const std::string& src = p->operands.at(0);
-        if (!arg_.count(src) || type_of(src).numel() != p->type.numel())
-          unsupported("reshape of a computed value inside a step");
-        id = use_arg(arg_.at(src), "full");
-      } else if (n == "broadcast_in_dim") {
-        const std::string& src = p->operands.at(0);
-        if (!arg_.count(src)) unsupported("broadcast_in_dim of a computed value inside a step");
-        if (p->type.shape != out_shape_) unsupported("broadcast to a shape other than the step's iteration shape");
-        auto d = p->attrs.find("dimensions");
-        id = use_arg(arg_.at(src), broadcast_map(type_of(src), d == p->attrs.end() ? std::vector<int64_t>{} : d->second.arr));
-      } else {  // splat of a non-constant scalar argument
-        const std::string& src = p->operands.at(0);
-        if (!arg_.count(src)) unsupported("splat of a computed scalar inside a step");
-        id = use_arg(arg_.at(src), "scalar");
+      id = emit("[\"const\"," + json_str(dt) + "," + constant_text(*p) + "]", dt);
+    } else if (const Op* c = (n == "splat" || n == "broadcast_in_dim" || n == "reshape") ? scalar_source(v) : nullptr) {
+      id = value(c->result);
+    } else if (n == "splat") {
+      const std::string& src = p->operands.at(0);
+      if (!arg_.count(src)) unsupported("splat of a computed scalar inside a step");
+      id = use_port(arg_.at(src), "scalar");
+    } else if ((n == "broadcast_in_dim" || n == "transpose" || n == "slice" || n == "pad" || n == "reshape") &&
+               view_of(v, &w)) {
+      if (p->type.shape != out_shape_) unsupported("an index map to a shape other than the step's iteration shape");
+      const Type& at = f_.arg_types[w.arg];
+      std::string map;
+      if (is_identity(w, at, out_shape_)) {
+        id = use_port(w.arg, "full");
+      } else if (n == "broadcast_in_dim" && arg_.count(p->operands.at(0)) &&
+                 simple_broadcast(at, arr(*p, "dimensions"), &map)) {
+        id = use_port(w.arg, map);
+      } else {
+        id = use_view(w);
       }
+    } else if (n == "iota") {
+      auto d = p->attrs.find("dimension");
+      if (d == p->attrs.end()) invalid("ask.iota without a dimension");
+      if (p->type.shape != out_shape_) unsupported("iota of a shape other than the step's iteration shape");
+      const int c = coord(d->second.i);
+      id = dt == "i64" ? c : emit("[\"cast\"," + std::to_string(c) + "," + json_str(dt) + "]", dt);
+    } else if (n == "concatenate") {
+      auto ax = p->attrs.find("axis");
+      if (ax == p->attrs.end()) invalid("ask.concatenate without an axis");
+      if (p->type.shape != out_shape_) unsupported("concatenate to a shape other than the step's iteration shape");
+      const size_t axis = size_t(ax->second.i);
+      std::vector<std::pair<int, int64_t>> parts;  // (value, end coordinate along axis)
+      int64_t at = 0;
+      for (const std::string& o : p->operands) {
+        const int64_t e = type_of(o).shape.at(axis);
+        if (e == 0) continue;
+        ArgView ow;
+        if (!view_of(o, &ow)) unsupported("concatenate operands must be index maps of step arguments");
+        if (ow.windowed(axis)) unsupported("concatenate of a padded operand along the same axis");
+        ow.lo[axis] = at;
+        ow.extent.resize(out_shape_.size());
+        for (size_t d = 0; d < out_shape_.size(); ++d)
+          if (d != axis) ow.extent[d] = std::min<int64_t>(ow.extent[d], out_shape_[d]);
+        parts.emplace_back(use_view(ow), at + e);
+        at += e;
+      }
+      if (parts.empty()) {
+        id = emit("[\"const\"," + json_str(dt) + ",0]", dt);
+      } else {
+        const int c = parts.size() > 1 ? coord(int64_t(axis)) : -1;
+        id = parts.back().first;
+        for (size_t k = parts.size() - 1; k-- > 0;) {
+          const int bound = emit("[\"const\",\"i64\"," + std::to_string(parts[k].second) + "]", "i64");
+          const int lt = emit("[\"compare\",\"lt\"," + std::to_string(c) + "," + std::to_string(bound) + "]", "bool");
+          id = emit("[\"select\"," + std::to_string(lt) + "," + std::to_string(parts[k].first) + "," +
+                        std::to_string(id) + "]", dt);
+        }
+      }
+    } else if (n == "broadcast_in_dim" || n == "reshape" || n == "transpose" || n == "slice" || n == "pad") {
+      unsupported("ask." + n + " of a computed value: only index maps of step arguments are supported");
     } else if (n == "cast") {
       const int x = operand(0);
       id = emit("[\"cast\"," + std::to_string(x) + "," + json_str(dt) + "]", dt);
@@ -634,43 +835,60 @@ class Lowering {
     } else if (kBinary.count(n)) {
       const int x = operand(0), y = operand(1);
       id = emit("[" + json_str(n) + "," + std::to_string(x) + "," + std::to_string(y) + "]", dt);
-    } else if (n == "transpose" || n == "slice" || n == "pad" || n == "concatenate" || n == "iota") {
-      unsupported("ask." + n + " needs a general index map, which this library's kernels do not have");
     } else {
       unsupported("ask." + n + " inside an elementwise step");
     }
-    if (p->type.shape != out_shape_ && p->type.numel() != 1 && n != "reshape")
+    if (p->type.shape != out_shape_ && p->type.numel() != 1)
       unsupported("ask." + n + " changes the iteration shape inside the step");
     memo_[v] = id;
     return id;
   }
   void start_program() {
     insns_.clear();
+    insn_port_.clear();
     types_.clear();
     memo_.clear();
-    arg_map_.assign(f_.args.size(), "");
-    arg_insn_.clear();
-    for (size_t k = 0; k < f_.args.size(); ++k)
-      arg_insn_.push_back(emit("[\"input\"," + std::to_string(k) + "]", f_.arg_types[k].dtype));
+    ports_.clear();
+    port_insn_.clear();
+    uses_shape_ = false;
   }
-  std::string inputs_json() const {
+  // Ports in argument order (then first use); input instructions name them.
+  std::vector<size_t> port_order() const {
+    std::vector<size_t> order(ports_.size());
+    for (size_t k = 0; k < order.size(); ++k) order[k] = k;
+    std::stable_sort(order.begin(), order.end(), [&](size_t x, size_t y) { return ports_[x].arg < ports_[y].arg; });
+    return order;
+  }
+  std::string inputs_json(const std::vector<size_t>& order) const {
     std::string o = "[";
-    for (size_t k = 0; k < f_.args.size(); ++k) {
+    for (size_t k = 0; k < order.size(); ++k) {
+      const Port& pt = ports_[order[k]];
       o += (k ? "," : "");
-      o += "{\"dtype\":" + json_str(f_.arg_types[k].dtype) + ",\"map\":" +
-           json_str(arg_map_[k].empty() ? "full" : arg_map_[k]) + "}";
+      o += "{\"dtype\":" + json_str(f_.arg_types[pt.arg].dtype) + ",\"map\":" + json_str(pt.map);
+      if (pt.map == "view") o += ",\"view\":" + pt.view;
+      o += "}";
     }
     return o + "]";
   }
-  std::string program_json() const {
+  std::string program_json(const std::vector<size_t>& order) const {
+    std::vector<size_t> rank(order.size());
+    for (size_t k = 0; k < order.size(); ++k) rank[order[k]] = k;
     std::string o = "[";
-    for (size_t k = 0; k < insns_.size(); ++k) o += (k ? "," : "") + insns_[k];
+    for (size_t k = 0; k < insns_.size(); ++k) {
+      o += (k ? "," : "");
+      o += insn_port_[k] >= 0 ? "[\"input\"," + std::to_string(rank[size_t(insn_port_[k])]) + "]" : insns_[k];
+    }
     return o + "]";
   }
-  std::vector<size_t> identity_args() const {
-    std::vector<size_t> v(f_.args.size());
-    for (size_t k = 0; k < v.size(); ++k) v[k] = k;
+  std::vector<size_t> port_args(const std::vector<size_t>& order) const {
+    std::vector<size_t> v;
+    for (size_t k : order) v.push_back(ports_[k].arg);
     return v;
+  }
+  std::string shape_json() const {
+    std::string o = "[";
+    for (size_t i = 0; i < out_shape_.size(); ++i) o += (i ? "," : "") + std::to_string(out_shape_[i]);
+    return o + "]";
   }
 
   Lowered elementwise() {
@@ -685,13 +903,18 @@ class Lowering {
       outs += (k ? "," : "") + std::string("{\"dtype\":") + json_str(type_of(f_.returns[k]).dtype) + "}";
     }
     outs += "]";
+    if (uses_shape_ && (out_shape_.empty() || out_shape_.size() > 6))
+      unsupported("views and coordinates need an iteration shape of 1..6 axes");
+    const std::vector<size_t> order = port_order();
     std::ostringstream o;
     o << "{\"family\":\"elementwise\",\"count\":" << product(out_shape_, 0, out_shape_.size())
-      << ",\"inner\":" << (map_inner_ ? map_inner_ : 1) << ",\"inputs\":" << inputs_json() << ",\"outputs\":" << outs
-      << ",\"program\":" << program_json() << ",\"results\":[";
+      << ",\"inner\":" << (map_inner_ ? map_inner_ : 1);
+    if (uses_shape_) o << ",\"shape\":" << shape_json();
+    o << ",\"inputs\":" << inputs_json(order) << ",\"outputs\":" << outs << ",\"program\":" << program_json(order)
+      << ",\"results\":[";
     for (size_t k = 0; k < results.size(); ++k) o << (k ? "," : "") << results[k];
     o << "]}";
-    return {o.str(), identity_args()};
+    return {o.str(), port_args(order)};
   }
 
   Lowered reduction() {
@@ -745,14 +968,15 @@ class Lowering {
                     std::to_string(slot) + "}";
     }
     reductions += "]";
-    for (size_t k = 0; k < f_.args.size(); ++k)
-      if (arg_map_[k] == "inner") unsupported("reductions read no per-column operands");
+    for (const Port& pt : ports_)
+      if (pt.map == "inner" || pt.map == "view") unsupported("reductions read no per-column or strided operands");
+    const std::vector<size_t> order = port_order();
     std::ostringstream o;
     o << "{\"family\":\"reduce\",\"outer\":" << outer << ",\"extent\":" << extent << ",\"inner\":" << inner
-      << ",\"inputs\":" << inputs_json() << ",\"program\":" << program_json() << ",\"results\":[";
+      << ",\"inputs\":" << inputs_json(order) << ",\"program\":" << program_json(order) << ",\"results\":[";
     for (size_t k = 0; k < results.size(); ++k) o << (k ? "," : "") << results[k];
     o << "],\"reductions\":" << reductions << "}";
-    return {o.str(), identity_args()};
+    return {o.str(), port_args(order)};
   }
 
   Lowered indexed(const Op& op, bool scatter) {

@@ -101,10 +101,11 @@ int parse_map(const std::string& s) {
   if (s == "scalar") return IM_SCALAR;
   if (s == "outer") return IM_OUTER;
   if (s == "inner") return IM_INNER;
+  if (s == "view") return IM_VIEW;
   fail(ASK_B200_E_INVALID, "unknown index map '" + s + "'");
 }
 const char* map_name(int m) {
-  return m == IM_FULL ? "full" : m == IM_SCALAR ? "scalar" : m == IM_OUTER ? "outer" : "inner";
+  return m == IM_FULL ? "full" : m == IM_SCALAR ? "scalar" : m == IM_OUTER ? "outer" : m == IM_INNER ? "inner" : "view";
 }
 
 // ---- constants ---------------------------------------------------------------------
@@ -236,6 +237,11 @@ Program parse_program(const json::Value& prog_json, const json::Value& results_j
       x.op = OP_CMP; x.aux = uint8_t(pi); x.a = operand(ins[2], i); x.b = operand(ins[3], i);
       need(vt[x.a] == vt[x.b], "compare operands must have identical types");
       x.src_type = uint8_t(vt[x.a]); type = kBool;
+    } else if (name == "coord") {
+      need(ins.size() == 2, "coord takes an axis of the iteration shape");
+      const int64_t axis = ins[1].as_int("coord axis");
+      need(axis >= 0 && axis < kMaxRank, "coord axis out of range");
+      x.op = OP_COORD; x.aux = uint8_t(axis); type = kI64;
     } else if (name == "select") {
       need(ins.size() == 4, "select takes a condition and two operands");
       x.op = OP_SELECT; x.a = operand(ins[1], i); x.b = operand(ins[2], i); x.c = operand(ins[3], i);
@@ -305,7 +311,7 @@ bool same_program(const Program& a, const Program& b) {
 // Linear-scan register assignment for the runtime interpreter: a value's
 // register is freed after its last use (results live to the end).
 int operand_count(int op) {
-  if (op == OP_INPUT || op == OP_CONST) return 0;
+  if (op == OP_INPUT || op == OP_CONST || op == OP_COORD) return 0;
   if (op == OP_SELECT) return 3;
   if (op == OP_CMP || (op >= OP_ADD && op <= OP_SHR)) return 2;
   return 1;  // cast and the unary ops
@@ -431,6 +437,8 @@ struct ask_b200_plan {
   RedArgs red{};
   IndexArgs idx{};
   SoftmaxArgs sm{};
+  bool views = false;  // elementwise step with IM_VIEW ports or coordinate instructions
+  ViewSet vs{};
   bool shardable = false;
   std::string kernel;
   int block = 256;  // threads per CTA where the family fixes it (softmax)
@@ -450,9 +458,17 @@ int blocks_per_sm_default(int) { return 8; }
 void finish_elementwise(ask_b200_plan& pl) {
   // Specialisation lookup on the canonical SSA form.
   pl.spec = EW_GENERIC;
-  for (int s = 1; s < EW_NUM_SPECS; ++s) {
+  for (int s = 1; s < EW_NUM_SPECS && !pl.views; ++s) {
     Program sp{};
     if (ew_spec_program(s, &sp) && same_program(sp, pl.prog)) { pl.spec = s; break; }
+  }
+  if (pl.views) {
+    pl.kernel = "ew_view";
+    int occ = pl.device >= 0 ? ew_view_occupancy() : 8;
+    const uint64_t needed = (pl.count + kEwThreads - 1) / kEwThreads;
+    pl.grid = int(std::max<uint64_t>(1, std::min(needed, uint64_t(std::max(occ, 1)) * uint64_t(pl.num_sms))));
+    pl.launches = pl.count ? 1 : 0;
+    return;
   }
   if (pl.spec == EW_GENERIC) assign_registers(pl.prog);
   const char* names[] = {"ew_generic", "ew_cfg1", "ew_cfg5b", "ew_softmax_norm_f16", "ew_softmax_norm_bf16"};
@@ -475,6 +491,37 @@ void parse_ports(const json::Value& r, const char* key, bool with_map, std::vect
   }
 }
 
+// An IM_VIEW port's view (PortView) from {"elements", "offset", "lo", "step",
+// "extent", "stride", "pad"}; every element it can read must lie inside the
+// port's `elements`.
+PortView parse_view(const json::Value& v, int rank, int type, uint64_t* elements) {
+  PortView pv{};
+  *elements = checked_count(v.at("elements"), "view elements");
+  pv.offset = v.at("offset").as_int("view offset");
+  const char* keys[] = {"lo", "step", "extent", "stride"};
+  int64_t* dst[] = {pv.lo, pv.step, pv.extent, pv.stride};
+  for (int k = 0; k < 4; ++k) {
+    const auto& a = v.at(keys[k]).as_array(keys[k]);
+    if (int(a.size()) != rank) fail(ASK_B200_E_INVALID, std::string("view ") + keys[k] + " must have one entry per axis");
+    for (int d = 0; d < rank; ++d) dst[k][d] = a[size_t(d)].as_int(keys[k]);
+  }
+  bool empty = false;
+  int64_t lo = pv.offset, hi = pv.offset;
+  for (int d = 0; d < rank; ++d) {
+    if (pv.step[d] < 1) fail(ASK_B200_E_INVALID, "view steps must be positive");
+    if (pv.extent[d] < 0) fail(ASK_B200_E_INVALID, "view extents must be non-negative");
+    if (pv.extent[d] == 0) empty = true;
+    const int64_t span = (pv.extent[d] ? pv.extent[d] - 1 : 0) * pv.stride[d];
+    lo += span < 0 ? span : 0;
+    hi += span > 0 ? span : 0;
+  }
+  if (!empty && (lo < 0 || uint64_t(hi) >= *elements))
+    fail(ASK_B200_E_INVALID, "a view reads outside its port's elements");
+  const json::Value* pad = v.get("pad");
+  pv.pad = pad ? constant_word(*pad, type) : 0;
+  return pv;
+}
+
 void build_elementwise(ask_b200_plan& pl, const json::Value& r) {
   pl.count = checked_count(r.at("count"), "count");
   const json::Value* in = r.get("inner");
@@ -483,14 +530,40 @@ void build_elementwise(ask_b200_plan& pl, const json::Value& r) {
   parse_ports(r, "inputs", true, ports.type, ports.map);
   pl.prog = canonical(parse_program(r.at("program"), r.at("results"), ports, true));
   bool uses_div = false;
+  bool coords = false;
+  for (int i = 0; i < pl.prog.n_insn; ++i) coords = coords || pl.prog.insn[i].op == OP_COORD;
+  const json::Value* shape = r.get("shape");
+  int rank = 1;
+  pl.vs = ViewSet{};
+  if (shape) {
+    const auto& a = shape->as_array("shape");
+    if (a.empty() || a.size() > size_t(kMaxRank)) fail(ASK_B200_E_UNSUPPORTED, "iteration shape must have 1..6 axes");
+    rank = int(a.size());
+    uint64_t n = 1;
+    for (int d = 0; d < rank; ++d) n = mul_checked(n, pl.vs.shape[d] = checked_count(a[size_t(d)], "shape"));
+    if (n != pl.count) fail(ASK_B200_E_INVALID, "the iteration shape's element count differs from count");
+  } else {
+    pl.vs.shape[0] = pl.count;
+  }
+  pl.vs.rank = rank;
+  for (int i = 0; i < pl.prog.n_insn; ++i)
+    if (pl.prog.insn[i].op == OP_COORD && int(pl.prog.insn[i].aux) >= rank)
+      fail(ASK_B200_E_INVALID, "coord axis beyond the iteration shape");
+  const auto& in_json = r.at("inputs").as_array("inputs");
   for (size_t k = 0; k < ports.type.size(); ++k) {
     uint64_t elems = pl.count;
     if (ports.map[k] == IM_SCALAR) elems = 1;
     if (ports.map[k] == IM_OUTER || ports.map[k] == IM_INNER) uses_div = true;
     if (ports.map[k] == IM_OUTER) elems = pl.inner ? pl.count / pl.inner : 0;
     if (ports.map[k] == IM_INNER) elems = pl.inner;
+    if (ports.map[k] == IM_VIEW) {
+      if (!shape) fail(ASK_B200_E_INVALID, "a view port needs the step's iteration \"shape\"");
+      pl.vs.port[k] = parse_view(in_json[k].at("view"), rank, ports.type[k], &elems);
+      pl.views = true;
+    }
     pl.inputs.push_back({ports.type[k], elems, ports.map[k]});
   }
+  pl.views = pl.views || coords;
   if (uses_div && (pl.inner == 0 || pl.count % pl.inner != 0))
     fail(ASK_B200_E_INVALID, "inner must divide count when an outer/inner index map is used");
   std::vector<int> otypes, omaps;
@@ -522,6 +595,10 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   Ports ports;
   parse_ports(r, "inputs", true, ports.type, ports.map);
   pl.prog = canonical(parse_program(r.at("program"), r.at("results"), ports, false));
+  for (int m : ports.map)
+    if (m == IM_VIEW) fail(ASK_B200_E_UNSUPPORTED, "reduction prologues read full, outer or scalar ports, not views");
+  for (int i = 0; i < pl.prog.n_insn; ++i)
+    if (pl.prog.insn[i].op == OP_COORD) fail(ASK_B200_E_UNSUPPORTED, "coord is an elementwise-step instruction");
   const auto& reds = r.at("reductions").as_array("reductions");
   if (reds.empty() || reds.size() > size_t(kMaxReductions))
     fail(ASK_B200_E_UNSUPPORTED, "1.." + std::to_string(kMaxReductions) + " reductions per step");
@@ -715,6 +792,15 @@ void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratc
   const size_t ni = pl.inputs.size();
   switch (pl.family) {
     case FAM_ELEMENTWISE: {
+      if (pl.views) {
+        EwArgs a{};
+        for (size_t k = 0; k < ni; ++k) a.in[k] = reinterpret_cast<const void*>(ports[k]);
+        for (size_t k = 0; k < pl.outputs.size(); ++k) a.out[k] = reinterpret_cast<void*>(ports[ni + k]);
+        a.count = pl.count;
+        a.inner = make_u32div(pl.inner ? pl.inner : 1, pl.count);
+        check_cuda(ew_view_launch(pl.prog, a, pl.vs, pl.grid, st), "elementwise launch");
+        break;
+      }
       EwArgs a{};
       bool aligned = true;
       for (size_t k = 0; k < ni; ++k) {

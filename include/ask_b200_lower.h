@@ -7,12 +7,13 @@
  * Input is what the reference's partitioner emits (lib/Frontend/Partition.cpp):
  * each owned step's module printed as MLIR text ("step_sources") and the
  * execution plan that binds steps to buffers.  The supported subset is the hot
- * path: elementwise ops over the step's iteration shape with scalar and
- * leading/trailing-axis broadcasts, reductions (sum, prod, max, min, any, all,
- * argmax, argmin) over one contiguous block of axes, gather and scatter_add.
- * Steps outside it fail with ASK_B200_E_UNSUPPORTED and a message naming the
- * op (transpose, slice, pad, concatenate and iota need index maps these
- * kernels do not have; matmul and external steps are not recipe steps).
+ * path: elementwise ops over the step's iteration shape, whose arguments may
+ * be read through broadcast_in_dim, transpose, slice, pad, reshape and
+ * concatenate (as strided, windowed views of the argument) and iota;
+ * reductions (sum, prod, max, min, any, all, argmax, argmin) over one
+ * contiguous block of axes; gather and scatter_add.  Steps outside it fail
+ * with ASK_B200_E_UNSUPPORTED and a message naming the op (an index map of a
+ * computed value rather than of an argument, matmul and external steps).
  */
 #ifndef ASK_B200_LOWER_H
 #define ASK_B200_LOWER_H

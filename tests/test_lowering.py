@@ -192,17 +192,88 @@ def test_index_maps():
     ask_b200.Plan(r, -1)
 
 
-@pytest.mark.parametrize("op,attrs,shape", [
-    ("transpose", "permutation = array<i64: 1, 0>", [8, 4]),
-    ("slice", "start_indices = array<i64: 0, 0>, limit_indices = array<i64: 4, 4>, strides = array<i64: 1, 1>", [4, 4]),
-])
-def test_general_index_maps_are_unsupported(op, attrs, shape):
+def arr(v):
+    return f"array<i64: {', '.join(str(int(x)) for x in v)}>" if len(v) else "array<i64>"
+
+
+def view_steps():
+    """(name, step source, input arrays, numpy expectation) of index-map steps."""
+    rng = np.random.default_rng(5)
+    cases = []
+    # transpose of an argument plus a full-shape argument
+    s = Step()
+    x, b = s.arg([3, 5], "i32"), s.arg([5, 3], "i32")
+    y = s.op("add", [s.op("transpose", [x], [5, 3], "i32", "permutation = " + arr([1, 0])), b], [5, 3], "i32")
+    xv, bv = rng.integers(-99, 99, (3, 5)).astype(np.int32), rng.integers(-99, 99, (5, 3)).astype(np.int32)
+    cases.append(("transpose", s.text([y]), [xv, bv], xv.T + bv))
+    # slice with a negative step and a positive one
+    s = Step()
+    x = s.arg([7, 9], "i32")
+    sl = s.op("slice", [x], [4, 3], "i32", f"starts = {arr([6, 1])}, stops = {arr([-1, 8])}, steps = {arr([-2, 3])}")
+    y = s.op("mul", [sl, s.splat(s.const(3, "i32"), [4, 3])], [4, 3], "i32")
+    xv = rng.integers(-99, 99, (7, 9)).astype(np.int32)
+    cases.append(("slice", s.text([y]), [xv], xv[6::-2, 1:8:3] * 3))
+    # pad with low, high and interior padding, f32 (exact adds of small integers)
+    s = Step()
+    x = s.arg([2, 3], "f32")
+    pv = s.splat(s.const("5.000000e-01", "f32"), [])
+    pd = s.op("pad", [x, pv], [6, 8], "f32",
+              f"pad_low = {arr([1, 0])}, pad_high = {arr([2, 1])}, interior = {arr([1, 2])}")
+    y = s.op("add", [pd, s.splat(s.const("1.000000e+00", "f32"), [6, 8])], [6, 8], "f32")
+    xv = rng.integers(-9, 9, (2, 3)).astype(np.float32)
+    want = np.full((6, 8), 0.5, np.float32)
+    want[1:1 + 2 * 2:2, 0:0 + 3 * 3:3] = xv
+    cases.append(("pad", s.text([y]), [xv], want + 1))
+    # concatenate of three arguments along axis 1, one of them transposed
+    s = Step()
+    a1, a2, a3 = s.arg([4, 2], "i32"), s.arg([4, 3], "i32"), s.arg([1, 4], "i32")
+    t3 = s.op("transpose", [a3], [4, 1], "i32", "permutation = " + arr([1, 0]))
+    y = s.op("concatenate", [a1, a2, t3], [4, 6], "i32", "axis = 1 : i64")
+    v1, v2, v3 = (rng.integers(-99, 99, sh).astype(np.int32) for sh in ([4, 2], [4, 3], [1, 4]))
+    cases.append(("concatenate", s.text([y]), [v1, v2, v3], np.concatenate([v1, v2, v3.T], axis=1)))
+    # iota along axis 1 cast to f32, plus a general broadcast of a [3,1] column
+    s = Step()
+    col = s.arg([3, 1], "f32")
+    io = s.op("iota", [], [3, 4], "f32", "dimension = 1 : i64")
+    bc = s.op("broadcast_in_dim", [col], [3, 4], "f32", f"dimensions = {arr([0, 1])}, shape = {arr([3, 4])}")
+    y = s.op("add", [io, bc], [3, 4], "f32")
+    cv = rng.integers(-9, 9, (3, 1)).astype(np.float32)
+    cases.append(("iota_broadcast", s.text([y]), [cv], np.arange(4, dtype=np.float32)[None, :] + cv))
+    return cases
+
+
+@pytest.mark.parametrize("case", view_steps(), ids=lambda c: c[0])
+def test_index_maps_lower_to_views(case):
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    r = out["recipe"]
+    assert r["shape"] == list(want.shape)
+    assert ask_b200.Plan(r, -1).describe()["kernel"] == "ew_view"
+    assert len(out["input_arguments"]) == len(r["inputs"])
+
+
+def test_index_map_of_a_computed_value_is_unsupported():
     s = Step()
     x = s.arg([4, 8], "f32")
-    y = s.op(op, [x], shape, "f32", attrs)
+    e = s.op("exp", [x], [4, 8], "f32")
+    y = s.op("transpose", [e], [8, 4], "f32", "permutation = " + arr([1, 0]))
     with pytest.raises(rt.CUDAError) as err:
         rt.lower_step(s.text([y]))
-    assert err.value.status == ask_b200.E_UNSUPPORTED and op in str(err.value)
+    assert err.value.status == ask_b200.E_UNSUPPORTED and "computed value" in str(err.value)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", view_steps(), ids=lambda c: c[0])
+def test_index_map_steps_on_gpu(device, case):
+    import torch
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    plan = ask_b200.Plan(out["recipe"], 0)
+    dev_in = [torch.from_numpy(np.ascontiguousarray(ins[a])).cuda() for a in out["input_arguments"]]
+    y = torch.empty(want.size, dtype=torch.from_numpy(want).dtype, device="cuda")
+    plan.launch(dev_in, [y], None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy().reshape(want.shape), want)
 
 
 def test_malformed_sources_are_invalid():
