@@ -356,14 +356,6 @@ __device__ __forceinline__ void apply(uint4* out, uint64_t pos, uint4 acc, bool 
   }
 }
 
-__device__ __forceinline__ void copy_async16(void* smem, const void* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
-               "l"(gmem)
-               : "memory");
-}
-__device__ __forceinline__ void copy_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void copy_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // K5: a warp per chunk of kChunk sorted entries.  The chunk becomes a list of
 // items in shared memory -- the update rows in sorted order, with the base row
