@@ -162,15 +162,27 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         z = torch.empty_like(xi)
         scratch = torch.empty(max(pa.scratch_bytes, 16), dtype=torch.uint8, device=dev)
 
-        if world > 1:
-            def run_a():
-                pa.launch_sharded(comm, [x], outs, scratch, st)
-        else:
-            run_a = pa.bind([x], outs, scratch, st)
-
         w.plans = [pa, pb]
-        w.kernels = [("reduce_split_global_f32", 4 * (a1 - a0), run_a),
-                     ("ew_cfg5b", 12 * (b1 - b0), pb.bind([xi, yi], [z], None, st))]
+        run_b = pb.bind([xi, yi], [z], None, st)
+        if world > 1:
+            # The sharded reduction ends in an all-gather that waits for every
+            # rank; it runs on a side stream beside the i32 chain so that wait
+            # (and the exchange) hides behind the chain's streaming.  The two
+            # plans share no data; the step joins both streams.
+            side = torch.cuda.Stream()
+            fork, join = torch.cuda.Event(), torch.cuda.Event()
+
+            def run_step():
+                fork.record(st)
+                side.wait_event(fork)
+                pa.launch_sharded(comm, [x], outs, scratch, side)
+                join.record(side)
+                run_b()
+                st.wait_event(join)
+            w.kernels = [("reduce_split_global_f32+ew_cfg5b", 4 * (a1 - a0) + 12 * (b1 - b0), run_step)]
+        else:
+            w.kernels = [("reduce_split_global_f32", 4 * (a1 - a0), pa.bind([x], outs, scratch, st)),
+                         ("ew_cfg5b", 12 * (b1 - b0), run_b)]
         w.global_bytes = 4 * na + 12 * nb
         w.config = static_config(name, world, small)
         w.tensors = {"x": x, "xi": xi, "yi": yi, "z": z, "outs": outs, "scratch": scratch}
