@@ -335,7 +335,8 @@ def cpu_sample(name: str, threads: int, budget_s: float = 12.0):
         idx = oracle.generate(5, SEED["cfg4"], 1, 0, n, 1.1, rows, threads=8)
         if name == "cfg4g":
             table = np.zeros(rows * dim, np.float32)
-            bytes_one = 8 * n + 8 * n * dim
+            # the GPU arm's compulsory bytes: indices, output rows, each distinct table row once
+            bytes_one = 8 * n + 4 * n * dim + 4 * dim * int(np.unique(idx).size)
 
             def run():
                 oracle.gather(table, idx, 1, rows, dim, threads=threads)
