@@ -31,6 +31,7 @@
 
 #include "json.h"
 #include "kernels.h"
+#include "plan_internal.h"
 
 using namespace askb;
 
@@ -399,14 +400,7 @@ void assign_registers(Program& p) {
 }
 
 // ---- plan -------------------------------------------------------------------------
-enum Family { FAM_ELEMENTWISE = 0, FAM_REDUCE, FAM_GATHER, FAM_SCATTER, FAM_SOFTMAX };
 const char* const kFamilyNames[] = {"elementwise", "reduce", "gather", "scatter_add", "softmax"};
-
-struct PortInfo {
-  int dtype;
-  uint64_t elements;
-  int map;
-};
 
 uint64_t checked_count(const json::Value& v, const char* what) {
   const int64_t x = v.as_int(what);
@@ -420,29 +414,6 @@ uint64_t mul_checked(uint64_t a, uint64_t b) {
 }
 
 }  // namespace
-
-struct ask_b200_plan {
-  int family = FAM_ELEMENTWISE;
-  int device = -1;
-  int num_sms = 148;
-  std::vector<PortInfo> inputs, outputs;
-  Program prog{};
-  int spec = 0;
-  int strategy = 0;
-  int grid = 1;
-  int launches = 1;
-  size_t scratch = 0;
-  size_t record_offset = 0;  // sharded reduce: where the per-rank records live in scratch
-  uint64_t count = 0, inner = 1;
-  RedArgs red{};
-  IndexArgs idx{};
-  SoftmaxArgs sm{};
-  bool views = false;  // elementwise step with IM_VIEW ports or coordinate instructions
-  ViewSet vs{};
-  bool shardable = false;
-  std::string kernel;
-  int block = 256;  // threads per CTA where the family fixes it (softmax)
-};
 
 struct ask_b200_comm {
   ncclComm_t comm = nullptr;
@@ -529,6 +500,7 @@ void build_elementwise(ask_b200_plan& pl, const json::Value& r) {
   Ports ports;
   parse_ports(r, "inputs", true, ports.type, ports.map);
   pl.prog = canonical(parse_program(r.at("program"), r.at("results"), ports, true));
+  pl.ssa = pl.prog;
   bool uses_div = false;
   bool coords = false;
   for (int i = 0; i < pl.prog.n_insn; ++i) coords = coords || pl.prog.insn[i].op == OP_COORD;
@@ -595,6 +567,7 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   Ports ports;
   parse_ports(r, "inputs", true, ports.type, ports.map);
   pl.prog = canonical(parse_program(r.at("program"), r.at("results"), ports, false));
+  pl.ssa = pl.prog;
   for (int m : ports.map)
     if (m == IM_VIEW) fail(ASK_B200_E_UNSUPPORTED, "reduction prologues read full, outer or scalar ports, not views");
   for (int i = 0; i < pl.prog.n_insn; ++i)

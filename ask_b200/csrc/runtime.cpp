@@ -13,8 +13,10 @@
 //   - counters: allocations, launches (steps enqueued), program_submissions,
 //     workspace_reuses, prepared_internal_slots/bytes, graph_instantiations,
 //     graph_launches, graph_nodes, graph_edges, graph_node_updates.
-// The step kind is an ask_b200 plan instead of a cubin kernel; graph mode
-// records each step (all of its kernels, and its pre-copy) as a child graph.
+// A step is an ask_b200 plan (a recipe) or a loaded kernel (Session::load,
+// CUDA.cpp:499-541: a cubin or PTX entry with declared parameter widths, such
+// as the kernel artifacts of ask_b200_artifact.h); graph mode records each step
+// (all of its kernels, and its pre-copy) as a child graph.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -104,6 +106,29 @@ class DeviceScope {
 };
 
 struct EventImpl;
+struct State;
+
+// A loaded kernel (Session::load): a CUDA library holding the image and the
+// entry's handle, with the parameter ABI it was checked against.
+struct KernelImpl {
+  const State* owner = nullptr;
+  int device = 0;
+  cudaLibrary_t lib = nullptr;
+  cudaKernel_t fn = nullptr;
+  std::string entry;
+  std::vector<unsigned> widths;  // 0 = device pointer, else scalar bytes
+  int max_threads = 0;
+  int max_dynamic_shared = 0;
+  ~KernelImpl() {
+    if (lib) {
+      int prev = 0;
+      cudaGetDevice(&prev);
+      cudaSetDevice(device);
+      cudaLibraryUnload(lib);
+      cudaSetDevice(prev);
+    }
+  }
+};
 
 struct State {
   int device = 0;
@@ -113,7 +138,11 @@ struct State {
   bool closed = false;
   std::map<std::string, uint64_t> counters;
   std::vector<std::shared_ptr<EventImpl>> pending;
+  std::map<std::pair<std::string, std::string>, std::shared_ptr<KernelImpl>> kernels;  // (image, entry)
+  int major = 0, minor = 0;
+  unsigned max_grid[3] = {0, 0, 0}, max_block[3] = {0, 0, 0}, max_threads = 0;
   ~State() {
+    kernels.clear();
     if (stream || capture) {
       int prev = 0;
       cudaGetDevice(&prev);
@@ -198,6 +227,12 @@ struct Step {
   bool copy = false;
   size_t copy_src = 0, copy_dst = 0;
   std::vector<size_t> touches;  // every buffer whose address the step's launch holds
+  // A loaded-kernel step: one argument per parameter (a logical buffer, -1 for
+  // null, or scalar ABI bytes) and a fixed launch.
+  std::shared_ptr<KernelImpl> kern;
+  std::vector<int64_t> arg_buffer;
+  std::vector<std::string> arg_scalar;
+  unsigned grid[3] = {1, 1, 1}, block[3] = {1, 1, 1}, shared = 0;
 };
 
 struct Program {
@@ -223,11 +258,13 @@ struct EventImpl {
   std::vector<std::shared_ptr<Buffer>> hold;
   std::shared_ptr<Workspace> ws;
   std::shared_ptr<Program> program;
+  std::shared_ptr<KernelImpl> kernel;
   void finish() {
     if (ws) ws->busy = false;
     ws.reset();
     hold.clear();
     program.reset();
+    kernel.reset();
     finished = true;
   }
   ~EventImpl() {
@@ -262,6 +299,172 @@ void synchronize(State& s) {
   cuda_check(cudaStreamSynchronize(s.stream), "cudaStreamSynchronize");
   for (auto& e : s.pending) e->finish();
   s.pending.clear();
+}
+
+// ---- loaded kernels (Session::load / validateLaunch / submit) -------------------
+void check_types(const State& st, const std::vector<std::string>& types) {
+  static const std::set<std::string> supported = {"bool", "i32", "i64", "f32", "f16", "bf16"};
+  for (const std::string& t : types) {
+    require(supported.count(t) != 0, "unsupported runtime element type: " + t);
+    if (t == "bf16")
+      require(st.major >= 8, "bf16 requires hardware support (CUDA compute capability >= 8.0); selected device has " +
+                                 std::to_string(st.major) + "." + std::to_string(st.minor));
+  }
+}
+
+// CUDA.cpp:499-541: validate the image, target and ABI, load the image once per
+// (image, entry) and check the entry's parameter layout against the widths.
+std::shared_ptr<KernelImpl> load_kernel(State& st, const std::string& image, const std::string& entry,
+                                        const std::vector<std::string>& types, int arch,
+                                        const std::vector<unsigned>& widths) {
+  check_types(st, types);
+  const bool ptx = image.compare(0, 4, "\x7f" "ELF") != 0;
+  require(arch >= 10 && (ptx ? st.major * 10 + st.minor >= arch : st.major == arch / 10 && st.minor >= arch % 10),
+          "CUDA code target is incompatible with the selected device");
+  require(ptx ? image.find('\0') == std::string::npos && image.find(".version") != std::string::npos
+              : image.size() >= 64,
+          "runtime load requires a CUDA cubin ELF image or PTX text");
+  require(!image.empty() && !entry.empty() && entry.find('\0') == std::string::npos,
+          "kernel binary and entry must be nonempty");
+  require(!widths.empty() && widths.size() <= 64, "unsupported kernel parameter count");
+  for (unsigned w : widths) require(w == 0 || w == 1 || w == 2 || w == 4 || w == 8, "unsupported kernel parameter width");
+  const auto key = std::make_pair(image, entry);
+  const auto found = st.kernels.find(key);
+  if (found != st.kernels.end()) {
+    require(found->second->widths == widths, "cached kernel parameter contract differs");
+    ++st.counters["module_hits"];
+    return found->second;
+  }
+  auto k = std::make_shared<KernelImpl>();
+  k->owner = &st;
+  k->device = st.device;
+  k->entry = entry;
+  k->widths = widths;
+  std::string data = image;
+  if (ptx) data.push_back('\0');  // PTX is NUL-terminated driver input
+  cuda_check(cudaLibraryLoadData(&k->lib, data.data(), nullptr, nullptr, 0, nullptr, nullptr, 0), "cudaLibraryLoadData");
+  cuda_check(cudaLibraryGetKernel(&k->fn, k->lib, entry.c_str()), "cudaLibraryGetKernel");
+  const void* f = reinterpret_cast<const void*>(k->fn);
+  size_t expected = 0;
+  for (size_t i = 0; i < widths.size(); ++i) {
+    const size_t width = widths[i] ? widths[i] : sizeof(uint64_t);
+    expected = (expected + width - 1) / width * width;
+    size_t offset = 0, size = 0;
+    cuda_check(cudaFuncGetParamInfo(f, i, &offset, &size), "cudaFuncGetParamInfo");
+    require(offset == expected && size == width, "kernel parameter layout differs from the declared ABI");
+    expected += width;
+  }
+  size_t offset = 0, size = 0;
+  const cudaError_t extra = cudaFuncGetParamInfo(f, widths.size(), &offset, &size);
+  cudaGetLastError();  // the expected failure must not linger as the last error
+  require(extra != cudaSuccess, "kernel parameter count differs from the declared ABI");
+  cudaFuncAttributes attr{};
+  cuda_check(cudaFuncGetAttributes(&attr, f), "cudaFuncGetAttributes");
+  require(attr.maxThreadsPerBlock > 0 && attr.maxDynamicSharedSizeBytes >= 0, "invalid CUDA kernel resource limits");
+  k->max_threads = attr.maxThreadsPerBlock;
+  k->max_dynamic_shared = attr.maxDynamicSharedSizeBytes;
+  st.kernels.emplace(key, k);
+  ++st.counters["module_loads"];
+  return k;
+}
+
+// CUDA.cpp:543-552.
+void validate_launch(const State& st, const std::shared_ptr<KernelImpl>& k, const unsigned grid[3],
+                     const unsigned block[3], unsigned shared) {
+  require(k && k->owner == &st, "kernel belongs to a different CUDA execution session");
+  require(shared <= unsigned(k->max_dynamic_shared), "dynamic shared memory exceeds the compiled kernel configured limit");
+  uint64_t threads = 1;
+  for (int i = 0; i < 3; ++i) {
+    require(grid[i] && grid[i] <= st.max_grid[i], "launch grid exceeds device limits");
+    require(block[i] && block[i] <= st.max_block[i], "launch block exceeds device limits");
+    threads *= block[i];
+  }
+  require(threads <= st.max_threads && threads <= uint64_t(k->max_threads),
+          "launch thread count exceeds kernel/device limits");
+}
+
+// Launch parameters: one 8-byte word per parameter holding the pointer or the
+// scalar's little-endian ABI bytes.
+void launch_kernel(const KernelImpl& k, std::vector<uint64_t>& words, const unsigned grid[3], const unsigned block[3],
+                   unsigned shared, cudaStream_t stream) {
+  std::vector<void*> params(words.size());
+  for (size_t i = 0; i < words.size(); ++i) params[i] = &words[i];
+  cuda_check(cudaLaunchKernel(reinterpret_cast<const void*>(k.fn), dim3(grid[0], grid[1], grid[2]),
+                              dim3(block[0], block[1], block[2]), params.data(), shared, stream),
+             "cudaLaunchKernel");
+}
+
+uint64_t scalar_word(const std::string& bytes) {
+  uint64_t w = 0;
+  std::memcpy(&w, bytes.data(), std::min(bytes.size(), sizeof w));
+  return w;
+}
+
+std::string hex_bytes(const std::string& hex, const char* what) {
+  require(hex.size() % 2 == 0, std::string(what) + " must be an even number of hex digits");
+  std::string out;
+  for (size_t i = 0; i < hex.size(); i += 2) {
+    auto nib = [&](char c) -> int {
+      if (c >= '0' && c <= '9') return c - '0';
+      if (c >= 'a' && c <= 'f') return c - 'a' + 10;
+      if (c >= 'A' && c <= 'F') return c - 'A' + 10;
+      fail(ASK_B200_E_INVALID, std::string(what) + " must be hex digits");
+    };
+    out.push_back(char(nib(hex[i]) * 16 + nib(hex[i + 1])));
+  }
+  return out;
+}
+
+void dims3(const json::Value* v, unsigned out[3], const char* what) {
+  require(v != nullptr, std::string("kernel step needs ") + what);
+  const auto& a = v->as_array(what);
+  require(a.size() == 3, std::string(what) + " must have three entries");
+  for (int i = 0; i < 3; ++i) {
+    const int64_t x = a[size_t(i)].as_int(what);
+    require(x >= 1 && x <= 0xffffffffll, std::string(what) + " entries must be in [1, 2^32-1]");
+    out[i] = unsigned(x);
+  }
+}
+
+// A program step that launches a loaded kernel (PlanStep with `kernel`,
+// CUDA.cpp:765-781): {"kernel": k, "inputs", "outputs", "grid", "block",
+// "shared_bytes", "arguments": [{"buffer": b} | {"buffer": -1} | {"scalar": "hex"}]}.
+void prepare_kernel_step(const State& st, const json::Value& sv, const json::Value& kv,
+                         const std::vector<std::shared_ptr<KernelImpl>>& kernels, const std::set<size_t>& ports,
+                         Step& step) {
+  const int64_t ki = kv.as_int("step kernel");
+  require(ki >= 0 && size_t(ki) < kernels.size() && kernels[size_t(ki)], "program step kernel index is out of range");
+  step.kern = kernels[size_t(ki)];
+  step.kernel = step.kern->entry;
+  dims3(sv.get("grid"), step.grid, "grid");
+  dims3(sv.get("block"), step.block, "block");
+  const json::Value* sh = sv.get("shared_bytes");
+  const int64_t shared = sh ? sh->as_int("shared_bytes") : 0;
+  require(shared >= 0 && shared <= 0xffffffffll, "shared_bytes must be in [0, 2^32-1]");
+  step.shared = unsigned(shared);
+  validate_launch(st, step.kern, step.grid, step.block, step.shared);
+  const auto& args = sv.at("arguments").as_array("arguments");
+  require(args.size() == step.kern->widths.size(), "program kernel argument count differs from its ABI");
+  std::set<size_t> bound;
+  for (size_t i = 0; i < args.size(); ++i) {
+    const unsigned width = step.kern->widths[i];
+    const json::Value* b = args[i].get("buffer");
+    const json::Value* sc = args[i].get("scalar");
+    const int64_t buffer = b ? b->as_int("argument buffer") : -1;
+    const std::string bytes = sc ? hex_bytes(sc->as_str("argument scalar"), "argument scalar") : std::string();
+    if (width) {
+      require(buffer == -1 && sc && bytes.size() == width, "program scalar argument differs from its ABI");
+    } else {
+      require(!sc && buffer >= -1, "program pointer argument differs from its ABI");
+      if (buffer >= 0) {
+        require(ports.count(size_t(buffer)) != 0, "program argument is not a step port");
+        bound.insert(size_t(buffer));
+      }
+    }
+    step.arg_buffer.push_back(buffer);
+    step.arg_scalar.push_back(bytes);
+  }
+  require(bound == ports, "program step port is not bound to a kernel parameter");
 }
 
 // ---- program preparation --------------------------------------------------------
@@ -311,7 +514,8 @@ void fuse_softmax(State& st, Program& p) {
   }
 }
 
-std::shared_ptr<Program> prepare(const std::shared_ptr<State>& st, const char* text, bool graph) {
+std::shared_ptr<Program> prepare(const std::shared_ptr<State>& st, const char* text, bool graph,
+                                 const std::vector<std::shared_ptr<KernelImpl>>& kernels) {
   require(text != nullptr, "program JSON is NULL");
   const json::Value root = json::Parser(text).parse();
   auto p = std::make_shared<Program>();
@@ -349,32 +553,40 @@ std::shared_ptr<Program> prepare(const std::shared_ptr<State>& st, const char* t
       require(!available.count(b), "program step overwrites an existing logical buffer");
       require(ports.insert(b).second, "program step repeats or aliases an output");
     }
-    ask_b200_plan* raw = nullptr;
-    const std::string& recipe = sv.at("recipe").as_str("step recipe");
-    const int rc = ask_b200_plan_create(recipe.c_str(), st->device, &raw);
-    if (rc != ASK_B200_OK) fail(rc, std::string("step recipe: ") + ask_b200_last_error());
-    step.plan.reset(raw, PlanDeleter());
-    size_t n_in = 0, n_out = 0, scratch = 0;
-    ask_b200_plan_ports(raw, &n_in, &n_out);
-    require(n_in == ins.size() && n_out == outs.size(),
-            "step binds " + std::to_string(ins.size()) + " inputs and " + std::to_string(outs.size()) +
-                " outputs; its recipe has " + std::to_string(n_in) + " and " + std::to_string(n_out));
-    size_t needed = 0;
-    ask_b200_plan_describe(raw, nullptr, 0, &needed);
-    std::string desc(needed, '\0');
-    ask_b200_plan_describe(raw, &desc[0], needed, &needed);
-    const json::Value d = json::Parser(desc.c_str()).parse();
-    step.kernel = d.at("kernel").as_str("kernel");
-    const auto& pm = d.at("port_map").as_array("port_map");
     step.ports = ins;
     step.ports.insert(step.ports.end(), outs.begin(), outs.end());
     step.n_inputs = ins.size();
-    for (size_t k = 0; k < pm.size(); ++k) {
-      const uint64_t bytes = uint64_t(pm[k].at("elements").as_int("elements")) *
-                             uint64_t(pm[k].at("storage_bytes").as_int("storage_bytes"));
-      require(p->sizes[step.ports[k]] == bytes,
-              "step port " + std::to_string(k) + " needs " + std::to_string(bytes) + " bytes; logical buffer " +
-                  std::to_string(step.ports[k]) + " has " + std::to_string(p->sizes[step.ports[k]]));
+    const json::Value* kv = sv.get("kernel");
+    require(bool(kv) != bool(sv.get("recipe")), "program step requires one recipe or kernel");
+    if (kv) {
+      prepare_kernel_step(*st, sv, *kv, kernels, ports, step);
+    } else {
+      ask_b200_plan* raw = nullptr;
+      const std::string& recipe = sv.at("recipe").as_str("step recipe");
+      const int rc = ask_b200_plan_create(recipe.c_str(), st->device, &raw);
+      if (rc != ASK_B200_OK) fail(rc, std::string("step recipe: ") + ask_b200_last_error());
+      step.plan.reset(raw, PlanDeleter());
+      size_t n_in = 0, n_out = 0, scratch = 0;
+      ask_b200_plan_ports(raw, &n_in, &n_out);
+      require(n_in == ins.size() && n_out == outs.size(),
+              "step binds " + std::to_string(ins.size()) + " inputs and " + std::to_string(outs.size()) +
+                  " outputs; its recipe has " + std::to_string(n_in) + " and " + std::to_string(n_out));
+      size_t needed = 0;
+      ask_b200_plan_describe(raw, nullptr, 0, &needed);
+      std::string desc(needed, '\0');
+      ask_b200_plan_describe(raw, &desc[0], needed, &needed);
+      const json::Value d = json::Parser(desc.c_str()).parse();
+      step.kernel = d.at("kernel").as_str("kernel");
+      const auto& pm = d.at("port_map").as_array("port_map");
+      for (size_t k = 0; k < pm.size(); ++k) {
+        const uint64_t bytes = uint64_t(pm[k].at("elements").as_int("elements")) *
+                               uint64_t(pm[k].at("storage_bytes").as_int("storage_bytes"));
+        require(p->sizes[step.ports[k]] == bytes,
+                "step port " + std::to_string(k) + " needs " + std::to_string(bytes) + " bytes; logical buffer " +
+                    std::to_string(step.ports[k]) + " has " + std::to_string(p->sizes[step.ports[k]]));
+      }
+      ask_b200_plan_scratch_bytes(raw, &scratch);
+      step.scratch_bytes = scratch;
     }
     if (const json::Value* pc = sv.get("pre_copy")) {
       const int64_t src = pc->at("source").as_int("pre_copy source"), dst = pc->at("destination").as_int("pre_copy destination");
@@ -386,8 +598,6 @@ std::shared_ptr<Program> prepare(const std::shared_ptr<State>& st, const char* t
       step.copy_src = size_t(src);
       step.copy_dst = size_t(dst);
     }
-    ask_b200_plan_scratch_bytes(raw, &scratch);
-    step.scratch_bytes = scratch;
     available.insert(outs.begin(), outs.end());
     p->steps.push_back(std::move(step));
   }
@@ -486,6 +696,13 @@ void enqueue_step(const Program& p, const Step& s, const std::vector<uint64_t>& 
     cuda_check(cudaMemcpyAsync(reinterpret_cast<void*>(addr[s.copy_dst]), reinterpret_cast<const void*>(addr[s.copy_src]),
                                p.sizes[s.copy_dst], cudaMemcpyDeviceToDevice, stream),
                "pre-copy");
+  if (s.kern) {
+    std::vector<uint64_t> words(s.arg_buffer.size());
+    for (size_t i = 0; i < words.size(); ++i)
+      words[i] = s.kern->widths[i] ? scalar_word(s.arg_scalar[i]) : s.arg_buffer[i] >= 0 ? addr[size_t(s.arg_buffer[i])] : 0;
+    launch_kernel(*s.kern, words, s.grid, s.block, s.shared, stream);
+    return;
+  }
   std::vector<uint64_t> ports(s.ports.size());
   for (size_t k = 0; k < ports.size(); ++k) ports[k] = addr[s.ports[k]];
   const uint64_t scratch = s.scratch == kNone ? 0 : addr[s.scratch];
@@ -689,6 +906,9 @@ struct ask_b200_program {
 struct ask_b200_event {
   std::shared_ptr<EventImpl> e;
 };
+struct ask_b200_kernel {
+  std::shared_ptr<KernelImpl> k;
+};
 
 namespace {
 
@@ -728,11 +948,20 @@ int ask_b200_session_create(int device, ask_b200_session** out) {
     auto st = std::make_shared<State>();
     st->device = device;
     DeviceScope scope(device);
+    cudaDeviceProp prop{};
+    cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    st->major = prop.major;
+    st->minor = prop.minor;
+    for (int i = 0; i < 3; ++i) {
+      st->max_grid[i] = unsigned(prop.maxGridSize[i]);
+      st->max_block[i] = unsigned(prop.maxThreadsDim[i]);
+    }
+    st->max_threads = unsigned(prop.maxThreadsPerBlock);
     cuda_check(cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking), "cudaStreamCreate");
     cuda_check(cudaStreamCreateWithFlags(&st->capture, cudaStreamNonBlocking), "cudaStreamCreate");
     for (const char* k : {"allocations", "launches", "program_submissions", "workspace_reuses", "prepared_internal_slots",
                           "prepared_internal_bytes", "graph_instantiations", "graph_launches", "graph_nodes",
-                          "graph_edges", "graph_node_updates", "fused_softmax_steps"})
+                          "graph_edges", "graph_node_updates", "fused_softmax_steps", "module_loads", "module_hits"})
       st->counters[k] = 0;
     *out = new ask_b200_session{st};
   });
@@ -894,7 +1123,107 @@ int ask_b200_program_prepare(ask_b200_session* s, const char* program_json, int 
     std::lock_guard<std::recursive_mutex> lock(st.mu);
     st.check_open();
     DeviceScope scope(st.device);
-    *out = new ask_b200_program{prepare(s->st, program_json, graph != 0)};
+    *out = new ask_b200_program{prepare(s->st, program_json, graph != 0, {})};
+  });
+}
+
+int ask_b200_program_prepare_kernels(ask_b200_session* s, const char* program_json, ask_b200_kernel* const* kernels,
+                                     size_t n_kernels, int graph, ask_b200_program** out) {
+  return guarded([&] {
+    require(out != nullptr, "out is NULL");
+    *out = nullptr;
+    require(n_kernels == 0 || kernels, "kernel list is NULL");
+    State& st = session_state(s);
+    std::lock_guard<std::recursive_mutex> lock(st.mu);
+    st.check_open();
+    DeviceScope scope(st.device);
+    std::vector<std::shared_ptr<KernelImpl>> ks(n_kernels);
+    for (size_t i = 0; i < n_kernels; ++i) ks[i] = kernels[i] ? kernels[i]->k : nullptr;
+    *out = new ask_b200_program{prepare(s->st, program_json, graph != 0, ks)};
+  });
+}
+
+int ask_b200_kernel_load(ask_b200_session* s, const void* image, size_t bytes, const char* entry,
+                         const char* const* required_types, size_t n_types, int arch, const unsigned* widths,
+                         size_t n_widths, ask_b200_kernel** out) {
+  return guarded([&] {
+    require(out != nullptr, "out is NULL");
+    *out = nullptr;
+    require(image || !bytes, "kernel image is NULL");
+    require(entry != nullptr, "kernel entry is NULL");
+    require(n_types == 0 || required_types, "required type list is NULL");
+    require(n_widths == 0 || widths, "parameter width list is NULL");
+    State& st = session_state(s);
+    std::lock_guard<std::recursive_mutex> lock(st.mu);
+    st.check_open();
+    DeviceScope scope(st.device);
+    std::vector<std::string> types;
+    for (size_t i = 0; i < n_types; ++i) {
+      require(required_types[i] != nullptr, "required type is NULL");
+      types.emplace_back(required_types[i]);
+    }
+    const std::string img(static_cast<const char*>(image), bytes);
+    *out = new ask_b200_kernel{load_kernel(st, img, entry, types, arch, std::vector<unsigned>(widths, widths + n_widths))};
+  });
+}
+
+int ask_b200_kernel_info(const ask_b200_kernel* k, char* entry, size_t cap, size_t* needed, unsigned* max_threads) {
+  return guarded([&] {
+    require(k && k->k, "kernel is NULL");
+    if (max_threads) *max_threads = unsigned(k->k->max_threads);
+    write_text(k->k->entry, entry, cap, needed);
+  });
+}
+
+int ask_b200_kernel_release(ask_b200_kernel* k) {
+  delete k;
+  return ASK_B200_OK;
+}
+
+int ask_b200_kernel_submit(ask_b200_session* s, ask_b200_kernel* k, const ask_b200_kernel_arg* args, size_t n_args,
+                           const unsigned grid[3], const unsigned block[3], unsigned shared_bytes, ask_b200_event** event) {
+  return guarded([&] {
+    require(event != nullptr, "event is NULL");
+    *event = nullptr;
+    require(k && k->k, "kernel is NULL");
+    require(grid && block, "grid or block is NULL");
+    require(n_args == 0 || args, "argument list is NULL");
+    State& st = session_state(s);
+    std::lock_guard<std::recursive_mutex> lock(st.mu);
+    st.check_open();
+    DeviceScope scope(st.device);
+    const KernelImpl& kern = *k->k;
+    validate_launch(st, k->k, grid, block, shared_bytes);
+    require(n_args == kern.widths.size(), "kernel argument count differs from its ABI");
+    std::vector<uint64_t> words(n_args, 0);
+    std::vector<std::shared_ptr<Buffer>> hold;
+    for (size_t i = 0; i < n_args; ++i) {
+      const unsigned width = kern.widths[i];
+      if (width) {
+        require(!args[i].buffer && args[i].scalar && args[i].scalar_bytes == width,
+                "scalar argument byte width differs from its ABI");
+        std::memcpy(&words[i], args[i].scalar, width);
+      } else {
+        require(!args[i].scalar && !args[i].scalar_bytes, "pointer argument requires a device buffer or null");
+        if (args[i].buffer) {
+          require(args[i].buffer->b && args[i].buffer->b->st == s->st,
+                  "device tensor belongs to a different CUDA execution session");
+          words[i] = args[i].buffer->b->ptr;
+          hold.push_back(args[i].buffer->b);
+        }
+      }
+    }
+    reap(st);
+    auto ev = std::make_shared<EventImpl>();
+    ev->st = s->st;
+    cuda_check(cudaEventCreateWithFlags(&ev->ev, cudaEventDisableTiming), "cudaEventCreate");
+    launch_kernel(kern, words, grid, block, shared_bytes, st.stream);
+    ++st.counters["launches"];
+    cuda_check(cudaEventRecord(ev->ev, st.stream), "cudaEventRecord");
+    ev->hold = std::move(hold);
+    ev->kernel = k->k;
+    st.pending.push_back(ev);
+    *event = new ask_b200_event{ev};
   });
 }
 

@@ -5,9 +5,11 @@ Runtime's C++ API (include/ask/Runtime/CUDA.h:66-175) so code written against
 ``ask::runtime`` reads the same: ``Session.create``, ``allocate``,
 ``importBuffer``, ``prepareProgram(sizes, inputs, outputs, steps, graph)``,
 ``PreparedProgram.submit/run``, ``DeviceBuffer.pointer/size/readonly/
-copyFromHost/copyToHost``, ``Event.query/wait`` and ``Session.stats``.  A
-:class:`PlanStep` holds an ask_b200 recipe (one owned step, see
-:mod:`ask_b200.recipes`) in place of the reference's loaded cubin kernel.
+copyFromHost/copyToHost``, ``Event.query/wait``, ``Session.load/submit`` and
+``Session.stats``.  A :class:`PlanStep` holds an ask_b200 recipe (one owned
+step, see :mod:`ask_b200.recipes`) or, as in the reference, a loaded
+:class:`Kernel` with its arguments and launch (kernel artifacts:
+:mod:`ask_b200.artifact`).
 
 ``check_allocation`` and ``assign_slots`` expose the plan verifier and the
 slot assigners on the host (no GPU needed).
@@ -50,6 +52,14 @@ RUNTIME_SIGNATURES = {
     "ask_b200_event_query": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_int)]),
     "ask_b200_event_wait": (ctypes.c_int, [_p]),
     "ask_b200_event_release": (ctypes.c_int, [_p]),
+    "ask_b200_program_prepare_kernels": (ctypes.c_int, [_p, ctypes.c_char_p, ctypes.POINTER(_p), _sz, ctypes.c_int,
+                                                        ctypes.POINTER(_p)]),
+    "ask_b200_kernel_load": (ctypes.c_int, [_p, ctypes.c_void_p, _sz, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p),
+                                            _sz, ctypes.c_int, ctypes.POINTER(ctypes.c_uint), _sz, ctypes.POINTER(_p)]),
+    "ask_b200_kernel_info": (ctypes.c_int, [_p] + _TEXT + [ctypes.POINTER(ctypes.c_uint)]),
+    "ask_b200_kernel_release": (ctypes.c_int, [_p]),
+    "ask_b200_kernel_submit": (ctypes.c_int, [_p, _p, ctypes.c_void_p, _sz, ctypes.POINTER(ctypes.c_uint),
+                                              ctypes.POINTER(ctypes.c_uint), ctypes.c_uint, ctypes.POINTER(_p)]),
     "ask_b200_allocation_check": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)] + _TEXT),
     "ask_b200_allocation_assign": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int] + _TEXT),
 }
@@ -78,23 +88,72 @@ def _text(fn, *args) -> str:
 
 
 @dataclass
-class PlanStep:
-    """One program step: an ask_b200 recipe bound to logical buffers.
-
-    ``inputs``/``outputs`` bind the recipe's ports in port-map order;
-    ``preCopy`` = (source, destination) is the reference's PlanStep::preCopy.
-    """
-    recipe: dict
-    inputs: Sequence[int]
-    outputs: Sequence[int]
-    preCopy: Optional[tuple] = None
+class PlanArgument:
+    """One kernel-step argument (the reference's PlanArgument): a logical
+    buffer for a pointer parameter (-1 = null) or the scalar's ABI bytes."""
+    buffer: int = -1
+    scalar: bytes = b""
 
     def to_json(self) -> dict:
-        d = {"recipe": self.recipe if isinstance(self.recipe, str) else json.dumps(self.recipe),
-             "inputs": [int(i) for i in self.inputs], "outputs": [int(o) for o in self.outputs]}
+        return {"scalar": self.scalar.hex()} if self.scalar else {"buffer": int(self.buffer)}
+
+
+@dataclass
+class PlanStep:
+    """One program step bound to logical buffers: an ask_b200 recipe, or a
+    loaded :class:`Kernel` with ``arguments`` (PlanArgument or int buffer
+    indices), ``grid``, ``block`` and ``sharedBytes``.
+
+    A recipe's ``inputs``/``outputs`` bind its ports in port-map order;
+    ``preCopy`` = (source, destination) is the reference's PlanStep::preCopy.
+    """
+    recipe: Optional[dict] = None
+    inputs: Sequence[int] = ()
+    outputs: Sequence[int] = ()
+    preCopy: Optional[tuple] = None
+    kernel: Optional["Kernel"] = None
+    arguments: Sequence = ()
+    grid: Sequence[int] = (1, 1, 1)
+    block: Sequence[int] = (1, 1, 1)
+    sharedBytes: int = 0
+
+    def to_json(self, kernel_index: Optional[int] = None) -> dict:
+        d = {"inputs": [int(i) for i in self.inputs], "outputs": [int(o) for o in self.outputs]}
+        if self.kernel is not None:
+            d.update({"kernel": kernel_index, "grid": [int(x) for x in self.grid], "block": [int(x) for x in self.block],
+                      "shared_bytes": int(self.sharedBytes),
+                      "arguments": [(a if isinstance(a, PlanArgument) else PlanArgument(buffer=int(a))).to_json()
+                                    for a in self.arguments]})
+        else:
+            d["recipe"] = self.recipe if isinstance(self.recipe, str) else json.dumps(self.recipe)
         if self.preCopy is not None:
             d["pre_copy"] = {"source": int(self.preCopy[0]), "destination": int(self.preCopy[1])}
         return d
+
+
+class Kernel:
+    """A loaded kernel entry (ask::runtime::Kernel)."""
+
+    def __init__(self, handle: _p, session: "Session"):
+        self._h = handle
+        self.session = session
+
+    def entry(self) -> str:
+        need = _sz()
+        _check(_lib.ask_b200_kernel_info(self._h, None, 0, ctypes.byref(need), None))
+        buf = ctypes.create_string_buffer(need.value)
+        _check(_lib.ask_b200_kernel_info(self._h, buf, need.value, ctypes.byref(need), None))
+        return buf.value.decode()
+
+    def maxThreads(self) -> int:
+        n = ctypes.c_uint()
+        _check(_lib.ask_b200_kernel_info(self._h, None, 0, None, ctypes.byref(n)))
+        return n.value
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            _lib.ask_b200_kernel_release(self._h)
+            self._h = None
 
 
 class DeviceBuffer:
@@ -152,6 +211,10 @@ class Event:
         if getattr(self, "_h", None):
             _lib.ask_b200_event_release(self._h)
             self._h = None
+
+
+class _KernelArg(ctypes.Structure):
+    _fields_ = [("buffer", _p), ("scalar", ctypes.c_void_p), ("scalar_bytes", _sz)]
 
 
 def _handles(buffers) -> ctypes.Array:
@@ -223,12 +286,61 @@ class Session:
                        steps: Sequence[PlanStep], graph: bool = False, fuse: bool = True) -> PreparedProgram:
         """``fuse=False`` keeps a three-step softmax as three steps (by default
         the runtime runs it as one fused step that writes the same buffers)."""
+        kernels = []
+        step_json = []
+        for s in steps:
+            index = None
+            if s.kernel is not None:
+                index = next((i for i, k in enumerate(kernels) if k is s.kernel), None)
+                if index is None:
+                    kernels.append(s.kernel)
+                    index = len(kernels) - 1
+            step_json.append(s.to_json(index))
         text = json.dumps({"buffer_sizes": [int(s) for s in sizes], "inputs": [int(i) for i in inputs],
-                           "outputs": [int(o) for o in outputs], "steps": [s.to_json() for s in steps],
-                           "fuse": bool(fuse)})
+                           "outputs": [int(o) for o in outputs], "steps": step_json, "fuse": bool(fuse)})
         h = _p()
-        _check(_lib.ask_b200_program_prepare(self._h, text.encode(), 1 if graph else 0, ctypes.byref(h)))
-        return PreparedProgram(h, self, len(outputs))
+        if kernels:
+            arr = (_p * len(kernels))(*[k._h for k in kernels])
+            _check(_lib.ask_b200_program_prepare_kernels(self._h, text.encode(), arr, len(kernels), 1 if graph else 0,
+                                                         ctypes.byref(h)))
+        else:
+            _check(_lib.ask_b200_program_prepare(self._h, text.encode(), 1 if graph else 0, ctypes.byref(h)))
+        program = PreparedProgram(h, self, len(outputs))
+        program._kernels = kernels
+        return program
+
+    def load(self, image: bytes, entry: str, requiredTypes: Sequence[str], arch: int,
+             parameterWidths: Sequence[int]) -> Kernel:
+        """Session::load: a cubin (or PTX text) entry with its declared ABI
+        (0 = device pointer, 1/2/4/8 = scalar bytes)."""
+        data = image.encode() if isinstance(image, str) else bytes(image)
+        types = (ctypes.c_char_p * max(len(requiredTypes), 1))(*[t.encode() for t in requiredTypes])
+        widths = (ctypes.c_uint * max(len(parameterWidths), 1))(*[int(w) for w in parameterWidths])
+        h = _p()
+        _check(_lib.ask_b200_kernel_load(self._h, data, len(data), entry.encode(), types, len(requiredTypes), int(arch),
+                                         widths, len(parameterWidths), ctypes.byref(h)))
+        return Kernel(h, self)
+
+    def submit(self, kernel: Kernel, arguments: Sequence, grid: Sequence[int], block: Sequence[int],
+               sharedBytes: int = 0) -> Event:
+        """Session::submit: arguments are DeviceBuffer, None (null pointer) or
+        bytes (a scalar's ABI bytes)."""
+        n = len(arguments)
+        args = (_KernelArg * max(n, 1))()
+        keep = []
+        for i, a in enumerate(arguments):
+            if isinstance(a, (bytes, bytearray)):
+                buf = ctypes.create_string_buffer(bytes(a), len(a))
+                keep.append(buf)
+                args[i].scalar = ctypes.cast(buf, ctypes.c_void_p)
+                args[i].scalar_bytes = len(a)
+            elif a is not None:
+                args[i].buffer = a._h
+        g = (ctypes.c_uint * 3)(*[int(x) for x in grid])
+        b = (ctypes.c_uint * 3)(*[int(x) for x in block])
+        ev = _p()
+        _check(_lib.ask_b200_kernel_submit(self._h, kernel._h, args, n, g, b, int(sharedBytes), ctypes.byref(ev)))
+        return Event(ev)
 
     def stream(self) -> int:
         s = _p()

@@ -2,9 +2,10 @@
  * ask_b200_runtime.h -- the runtime layer that hosts ask_b200 plans as the
  * steps of an execution plan: sessions, device buffers, prepared programs and
  * completion events.  It mirrors the reference Runtime's C++ surface
- * (include/ask/Runtime/CUDA.h:66-175; lib/Runtime/CUDA.cpp:679-1005) with a
- * "recipe step" kind in place of a loaded cubin kernel: each step is an
- * ask_b200 plan whose ports are bound to logical buffers of the program.
+ * (include/ask/Runtime/CUDA.h:66-175; lib/Runtime/CUDA.cpp:418-1005).  A step
+ * is either an ask_b200 plan (a "recipe step") whose ports are bound to
+ * logical buffers of the program, or a loaded kernel (Session::load, e.g. a
+ * kernel artifact from ask_b200_artifact.h) with its arguments and launch.
  *
  *   Session            one device, one non-blocking stream, usage counters
  *                      (Session::create / allocate / importBuffer /
@@ -15,6 +16,8 @@
  *                      lib/Pass/Pass.cpp:12-208) with internal buffers mapped
  *                      to reusable workspace slots; submit() binds the public
  *                      ports, run() also allocates the outputs
+ *   Kernel             a loaded cubin/PTX entry whose parameter layout was
+ *                      checked against declared widths (Session::load)
  *   Event              completion of one submission; it keeps the submission's
  *                      buffers and workspace alive until the GPU is done
  *
@@ -35,6 +38,14 @@
  * copy enqueued before the step.  A scatter_add recipe already performs its own
  * pre-copy (out = base) inside its launch and needs none.
  *
+ * A kernel step (ask_b200_program_prepare_kernels) replaces "recipe" with
+ *   "kernel": k (index into the kernels passed), "grid": [x, y, z],
+ *   "block": [x, y, z], "shared_bytes": n,
+ *   "arguments": [{"buffer": b} | {"buffer": -1} | {"scalar": "<hex ABI bytes>"}, ...]
+ * with one argument per kernel parameter: pointer parameters bind step ports
+ * (every port exactly once) or null, scalar parameters carry exactly their
+ * width in little-endian bytes (the reference's PlanArgument).
+ *
  * All entry points return 0 or a negative ASK_B200_E_* status with the
  * message in ask_b200_last_error() (ask_b200.h).  Handles are reference
  * counted: *_release drops the caller's handle, and an object lives on while
@@ -53,6 +64,15 @@ typedef struct ask_b200_session ask_b200_session;
 typedef struct ask_b200_buffer ask_b200_buffer;
 typedef struct ask_b200_program ask_b200_program;
 typedef struct ask_b200_event ask_b200_event;
+typedef struct ask_b200_kernel ask_b200_kernel;
+
+/* One argument of Session::submit: a buffer (NULL for a null pointer) for a
+ * pointer parameter, or scalar_bytes bytes at scalar for a scalar one. */
+typedef struct ask_b200_kernel_arg {
+  ask_b200_buffer *buffer;
+  const void *scalar;
+  size_t scalar_bytes;
+} ask_b200_kernel_arg;
 
 /* Session::create(device) (lib/Runtime/CUDA.cpp:418-441). */
 ASK_B200_API int ask_b200_session_create(int device, ask_b200_session **out);
@@ -90,6 +110,31 @@ ASK_B200_API int ask_b200_program_submit(ask_b200_program *program, ask_b200_buf
 ASK_B200_API int ask_b200_program_run(ask_b200_program *program, ask_b200_buffer *const *inputs, size_t n_inputs,
                                       ask_b200_buffer **outputs, size_t n_outputs, ask_b200_event **event);
 ASK_B200_API int ask_b200_program_release(ask_b200_program *program);
+
+/* Session::prepareProgram with kernel steps: "kernel": k in a step indexes kernels[]. */
+ASK_B200_API int ask_b200_program_prepare_kernels(ask_b200_session *session, const char *program_json,
+                                                  ask_b200_kernel *const *kernels, size_t n_kernels, int graph,
+                                                  ask_b200_program **out);
+
+/*
+ * Session::load(image, entry, requiredTypes, arch, parameterWidths)
+ * (lib/Runtime/CUDA.cpp:499-541): a cubin ELF image for compute capability
+ * arch/10.arch%10 (or PTX text for at least arch), the entry's parameter widths
+ * (0 = device pointer, 1/2/4/8 = scalar bytes) checked against its layout,
+ * and the element types the session must support.  Loaded once per
+ * (image, entry) per session; a second load returns the cached kernel.
+ */
+ASK_B200_API int ask_b200_kernel_load(ask_b200_session *session, const void *image, size_t bytes, const char *entry,
+                                      const char *const *required_types, size_t n_types, int arch,
+                                      const unsigned *widths, size_t n_widths, ask_b200_kernel **out);
+/* Kernel::entry / Kernel::maxThreads. */
+ASK_B200_API int ask_b200_kernel_info(const ask_b200_kernel *kernel, char *entry, size_t cap, size_t *needed,
+                                      unsigned *max_threads);
+ASK_B200_API int ask_b200_kernel_release(ask_b200_kernel *kernel);
+/* Session::submit(kernel, arguments, grid, block, sharedBytes) (lib/Runtime/CUDA.cpp:568-600). */
+ASK_B200_API int ask_b200_kernel_submit(ask_b200_session *session, ask_b200_kernel *kernel,
+                                        const ask_b200_kernel_arg *args, size_t n_args, const unsigned grid[3],
+                                        const unsigned block[3], unsigned shared_bytes, ask_b200_event **event);
 
 /* Event::query / Event::wait. */
 ASK_B200_API int ask_b200_event_query(ask_b200_event *event, int *done);
