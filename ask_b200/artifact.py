@@ -313,18 +313,49 @@ def parameter_widths(artifact: dict):
     return [0 if isinstance(a, str) else len(scalar_bytes(a["type"], a["value"])) for a in artifact["arguments"]]
 
 
-def load_artifact(session, artifact: dict, port_types: Optional[Sequence[str]] = None):
+def submit_arguments(artifact: dict, inputs: Sequence, outputs: Sequence, types: Optional[dict] = None):
+    """(arguments, alignments) for Session.submit: DeviceBuffers for ports,
+    ABI bytes for scalars, and each pointer's element size as its alignment."""
+    args, aligns = [], []
+    for a in artifact["arguments"]:
+        if isinstance(a, str):
+            if a == "null":
+                args.append(None)
+                aligns.append(1)
+            else:
+                kind, n = a.split(":")
+                args.append((inputs if kind == "input" else outputs)[int(n)])
+                aligns.append(ELEMENT_BYTES[types[a]] if types and a in types else 1)
+        else:
+            args.append(scalar_bytes(a["type"], a["value"]))
+            aligns.append(1)
+    return args, aligns
+
+
+def load_artifact(session, artifact: dict, element_types: Optional[Sequence[str]] = None):
     """Load an artifact on a runtime Session (Session::load with its declared
     widths and required element types merged with the port types)."""
     validate_artifact(artifact)
     payload = base64.b64decode(artifact["payload"]) if artifact["format"] == "cubin" else artifact["payload"].encode()
-    types = list(dict.fromkeys(list(artifact["required_element_types"]) + list(port_types or [])))
+    types = list(dict.fromkeys(list(artifact["required_element_types"]) + list(element_types or [])))
     return session.load(payload, artifact["entry"], types, artifact["target"]["arch"], parameter_widths(artifact))
 
 
-def artifact_step(artifact: dict, kernel, inputs: Sequence[int], outputs: Sequence[int]):
+ELEMENT_BYTES = {"bool": 1, "i32": 4, "i64": 8, "f32": 4, "f16": 2, "bf16": 2}
+
+
+def port_types(request: dict) -> dict:
+    """{"input:N" / "output:N": element type} from a request's pointer signature."""
+    return {request["source_bindings"][k]: POINTER_TYPES[t] for k, t in request["signature"].items()
+            if t in POINTER_TYPES}
+
+
+def artifact_step(artifact: dict, kernel, inputs: Sequence[int], outputs: Sequence[int],
+                  types: Optional[dict] = None):
     """A program step launching a loaded artifact: input:N / output:N bind the
-    logical buffers inputs[N] / outputs[N]; scalars carry their ABI bytes."""
+    logical buffers inputs[N] / outputs[N]; scalars carry their ABI bytes.
+    With ``types`` (port -> element type, :func:`port_types`) each pointer
+    carries its element size as the alignment the runtime checks."""
     from .runtime import PlanArgument, PlanStep
     args = []
     for a in artifact["arguments"]:
@@ -333,7 +364,8 @@ def artifact_step(artifact: dict, kernel, inputs: Sequence[int], outputs: Sequen
                 args.append(PlanArgument(buffer=-1))
             else:
                 kind, n = a.split(":")
-                args.append(PlanArgument(buffer=int((inputs if kind == "input" else outputs)[int(n)])))
+                align = ELEMENT_BYTES[types[a]] if types and a in types else 1
+                args.append(PlanArgument(buffer=int((inputs if kind == "input" else outputs)[int(n)]), align=align))
         else:
             args.append(PlanArgument(scalar=scalar_bytes(a["type"], a["value"])))
     launch = artifact["launch"]

@@ -232,6 +232,7 @@ struct Step {
   std::shared_ptr<KernelImpl> kern;
   std::vector<int64_t> arg_buffer;
   std::vector<std::string> arg_scalar;
+  std::vector<uint64_t> arg_align;  // required address alignment of a pointer argument (1 = none)
   unsigned grid[3] = {1, 1, 1}, block[3] = {1, 1, 1}, shared = 0;
 };
 
@@ -428,7 +429,10 @@ void dims3(const json::Value* v, unsigned out[3], const char* what) {
 
 // A program step that launches a loaded kernel (PlanStep with `kernel`,
 // CUDA.cpp:765-781): {"kernel": k, "inputs", "outputs", "grid", "block",
-// "shared_bytes", "arguments": [{"buffer": b} | {"buffer": -1} | {"scalar": "hex"}]}.
+// "shared_bytes", "arguments": [{"buffer": b, "align": a} | {"buffer": -1} | {"scalar": "hex"}]}.
+// "align" (optional, a power of two) is the address alignment the kernel
+// needs for that pointer -- its element size; submissions binding a public
+// buffer at another address are refused before anything is enqueued.
 void prepare_kernel_step(const State& st, const json::Value& sv, const json::Value& kv,
                          const std::vector<std::shared_ptr<KernelImpl>>& kernels, const std::set<size_t>& ports,
                          Step& step) {
@@ -451,6 +455,10 @@ void prepare_kernel_step(const State& st, const json::Value& sv, const json::Val
     const json::Value* b = args[i].get("buffer");
     const json::Value* sc = args[i].get("scalar");
     const int64_t buffer = b ? b->as_int("argument buffer") : -1;
+    const json::Value* al = args[i].get("align");
+    const int64_t align = al ? al->as_int("argument align") : 1;
+    require(align >= 1 && align <= 256 && (align & (align - 1)) == 0, "argument align must be a power of two up to 256");
+    require(!al || !width, "scalar arguments take no alignment");
     const std::string bytes = sc ? hex_bytes(sc->as_str("argument scalar"), "argument scalar") : std::string();
     if (width) {
       require(buffer == -1 && sc && bytes.size() == width, "program scalar argument differs from its ABI");
@@ -463,6 +471,7 @@ void prepare_kernel_step(const State& st, const json::Value& sv, const json::Val
     }
     step.arg_buffer.push_back(buffer);
     step.arg_scalar.push_back(bytes);
+    step.arg_align.push_back(uint64_t(align));
   }
   require(bound == ports, "program step port is not bound to a kernel parameter");
 }
@@ -863,6 +872,13 @@ std::shared_ptr<EventImpl> submit(const std::shared_ptr<Program>& pp, const std:
     require(!a.size || !b.size || a.ptr + a.size <= b.ptr || b.ptr + b.size <= a.ptr,
             "distinct program output buffers must not overlap other ports");
   }
+  for (const Step& s : p.steps)
+    for (size_t i = 0; i < s.arg_align.size(); ++i) {
+      const int64_t b = s.arg_buffer[i];
+      if (b >= 0 && bound[size_t(b)] && bound[size_t(b)]->ptr % s.arg_align[i])
+        fail(ASK_B200_E_INVALID, "kernel step " + s.kernel + " argument " + std::to_string(i) +
+                                     " is not aligned to " + std::to_string(s.arg_align[i]) + " bytes");
+    }
   return enqueue(st, pp, std::move(bound));
 }
 
@@ -1208,6 +1224,9 @@ int ask_b200_kernel_submit(ask_b200_session* s, ask_b200_kernel* k, const ask_b2
         if (args[i].buffer) {
           require(args[i].buffer->b && args[i].buffer->b->st == s->st,
                   "device tensor belongs to a different CUDA execution session");
+          require(args[i].align <= 1 || args[i].buffer->b->ptr % args[i].align == 0,
+                  "kernel argument " + std::to_string(i) + " is not aligned to " + std::to_string(args[i].align) +
+                      " bytes");
           words[i] = args[i].buffer->b->ptr;
           hold.push_back(args[i].buffer->b);
         }

@@ -93,9 +93,15 @@ class PlanArgument:
     buffer for a pointer parameter (-1 = null) or the scalar's ABI bytes."""
     buffer: int = -1
     scalar: bytes = b""
+    align: int = 1  # address alignment the kernel needs for this pointer (its element size)
 
     def to_json(self) -> dict:
-        return {"scalar": self.scalar.hex()} if self.scalar else {"buffer": int(self.buffer)}
+        if self.scalar:
+            return {"scalar": self.scalar.hex()}
+        d = {"buffer": int(self.buffer)}
+        if self.align > 1:
+            d["align"] = int(self.align)
+        return d
 
 
 @dataclass
@@ -214,7 +220,7 @@ class Event:
 
 
 class _KernelArg(ctypes.Structure):
-    _fields_ = [("buffer", _p), ("scalar", ctypes.c_void_p), ("scalar_bytes", _sz)]
+    _fields_ = [("buffer", _p), ("scalar", ctypes.c_void_p), ("scalar_bytes", _sz), ("align", _sz)]
 
 
 def _handles(buffers) -> ctypes.Array:
@@ -322,9 +328,10 @@ class Session:
         return Kernel(h, self)
 
     def submit(self, kernel: Kernel, arguments: Sequence, grid: Sequence[int], block: Sequence[int],
-               sharedBytes: int = 0) -> Event:
+               sharedBytes: int = 0, alignments: Optional[Sequence[int]] = None) -> Event:
         """Session::submit: arguments are DeviceBuffer, None (null pointer) or
-        bytes (a scalar's ABI bytes)."""
+        bytes (a scalar's ABI bytes); ``alignments[i]`` (optional) is the
+        address alignment pointer argument i needs."""
         n = len(arguments)
         args = (_KernelArg * max(n, 1))()
         keep = []
@@ -336,6 +343,8 @@ class Session:
                 args[i].scalar_bytes = len(a)
             elif a is not None:
                 args[i].buffer = a._h
+            if alignments is not None:
+                args[i].align = int(alignments[i])
         g = (ctypes.c_uint * 3)(*[int(x) for x in grid])
         b = (ctypes.c_uint * 3)(*[int(x) for x in block])
         ev = _p()

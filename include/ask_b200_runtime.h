@@ -41,10 +41,13 @@
  * A kernel step (ask_b200_program_prepare_kernels) replaces "recipe" with
  *   "kernel": k (index into the kernels passed), "grid": [x, y, z],
  *   "block": [x, y, z], "shared_bytes": n,
- *   "arguments": [{"buffer": b} | {"buffer": -1} | {"scalar": "<hex ABI bytes>"}, ...]
+ *   "arguments": [{"buffer": b, "align": a} | {"buffer": -1} | {"scalar": "<hex ABI bytes>"}, ...]
  * with one argument per kernel parameter: pointer parameters bind step ports
  * (every port exactly once) or null, scalar parameters carry exactly their
- * width in little-endian bytes (the reference's PlanArgument).
+ * width in little-endian bytes (the reference's PlanArgument).  The optional
+ * "align" is the address alignment the kernel needs for that pointer (its
+ * element size): a submission binding a public buffer at another address is
+ * refused before anything is enqueued.
  *
  * All entry points return 0 or a negative ASK_B200_E_* status with the
  * message in ask_b200_last_error() (ask_b200.h).  Handles are reference
@@ -67,11 +70,14 @@ typedef struct ask_b200_event ask_b200_event;
 typedef struct ask_b200_kernel ask_b200_kernel;
 
 /* One argument of Session::submit: a buffer (NULL for a null pointer) for a
- * pointer parameter, or scalar_bytes bytes at scalar for a scalar one. */
+ * pointer parameter, or scalar_bytes bytes at scalar for a scalar one.  align
+ * (0 or 1 = none) is the address alignment the kernel needs for a pointer --
+ * its element size; a buffer at another address is refused before launch. */
 typedef struct ask_b200_kernel_arg {
   ask_b200_buffer *buffer;
   const void *scalar;
   size_t scalar_bytes;
+  size_t align;
 } ask_b200_kernel_arg;
 
 /* Session::create(device) (lib/Runtime/CUDA.cpp:418-441). */

@@ -26,11 +26,12 @@ _CUBINS = {}
 
 
 def artifact_for(recipe, grid=592, scalars=(("n", "i32", 7),), source=None):
+    """(artifact, port -> element type) of the recipe's step."""
     req = request_for(recipe, grid=(grid, 1, 1), scalars=scalars, source=source)
     key = json.dumps(req, sort_keys=True)
     if key not in _CUBINS:
         _CUBINS[key] = A.build_artifact(req)
-    return _CUBINS[key]
+    return _CUBINS[key], A.port_types(req)
 
 
 @pytest.fixture(scope="module")
@@ -42,10 +43,12 @@ def session(device):
 
 def run_artifact(session, recipe, inputs, out_dtypes, grid=592, mode="submit", offset_bytes=0,
                  scalars=(("n", "i32", 7),)):
-    """Build, load and launch the recipe's artifact; returns the outputs."""
-    art = artifact_for(recipe, grid, scalars)
+    """Build, load and launch the recipe's artifact; returns the outputs.
+    offset_bytes must keep every port aligned to its element size."""
+    art, types = artifact_for(recipe, grid, scalars)
     ports = ask_b200.Plan(recipe, -1).describe()["port_map"]
     kernel = A.load_artifact(session, art, [p["element_type"] for p in ports])
+    assert all(offset_bytes % A.ELEMENT_BYTES[p["element_type"]] == 0 for p in ports)
     dev_in = [to_dev(a, offset_bytes) for a in inputs]
     n_out = [p["elements"] for p in ports[len(inputs):]]
     dev_out = [torch.zeros(n * np.dtype(NUMPY[dt]).itemsize + offset_bytes, dtype=torch.uint8,
@@ -54,18 +57,12 @@ def run_artifact(session, recipe, inputs, out_dtypes, grid=592, mode="submit", o
     bin_ = [session.importTensor(t, readonly=True) for t in dev_in]
     bout = [session.importTensor(t) for t in dev_out]
     if mode == "submit":
-        args = []
-        for a in art["arguments"]:
-            if isinstance(a, str):
-                kind, k = a.split(":")
-                args.append((bin_ if kind == "input" else bout)[int(k)])
-            else:
-                args.append(A.scalar_bytes(a["type"], a["value"]))
+        args, aligns = A.submit_arguments(art, bin_, bout, types)
         session.submit(kernel, args, art["launch"]["grid"], art["launch"]["block"],
-                       art["launch"]["shared_bytes"]).wait()
+                       art["launch"]["shared_bytes"], aligns).wait()
     else:
         ni, no = len(bin_), len(bout)
-        step = A.artifact_step(art, kernel, list(range(ni)), list(range(ni, ni + no)))
+        step = A.artifact_step(art, kernel, list(range(ni)), list(range(ni, ni + no)), types)
         prog = session.prepareProgram([b.size() for b in bin_ + bout], list(range(ni)), list(range(ni, ni + no)),
                                       [step], graph=(mode == "graph"))
         prog.submit(bin_, bout).wait()
@@ -91,7 +88,8 @@ def test_random_programs_match_oracle(session, dtype, seed):
     n = 1031
     rec = R.elementwise(p, outs, n)
     ins = [random_inputs(rng, dtype, n), random_inputs(rng, dtype, n), random_inputs(rng, dtype, 1)]
-    got = run_artifact(session, rec, ins, [o.dtype for o in outs], offset_bytes=4 * (seed % 2))
+    # an offset of one element: aligned ports, but not 16-byte aligned (the scalar path)
+    got = run_artifact(session, rec, ins, [o.dtype for o in outs], offset_bytes=(seed % 2) * (8 if dtype == "i64" else 4))
     want = oracle.elementwise(rec, ins)
     for k, (g, w) in enumerate(zip(got, want)):
         assert_same(g, w, outs[k].dtype)
@@ -224,7 +222,7 @@ def test_gather_with_out_of_bounds(session, dtype, inner, itype):
 
 # ---- the loader's ABI checks --------------------------------------------------------------
 def test_load_checks_the_declared_abi(session):
-    art = artifact_for(R.cfg5b_step(1000))
+    art, _ = artifact_for(R.cfg5b_step(1000))
     image = base64.b64decode(art["payload"])
     widths = A.parameter_widths(art)  # [0, 0, 0, 4]
     k1 = session.load(image, art["entry"], ["i32"], 100, widths)
@@ -261,7 +259,7 @@ def _fresh(session):
 
 
 def test_launch_and_argument_validation(session):
-    art = artifact_for(R.cfg5b_step(1000))
+    art, types = artifact_for(R.cfg5b_step(1000))
     kernel = A.load_artifact(session, art)
     x = session.allocate(4000)
     y = session.allocate(4000)
@@ -278,6 +276,18 @@ def test_launch_and_argument_validation(session):
     with pytest.raises(rt.CUDAError) as err:
         session.submit(kernel, [x, y, out, b"\0\0\0\0"], [4, 1, 1], [256, 1, 1], 1 << 20)
     assert "dynamic shared memory" in str(err.value)
+    # an i32 port bound at an address that is not 4-byte aligned is refused on the host
+    raw = session.allocate(4004)
+    odd = session.importBuffer(raw.pointer() + 2, 4000)
+    args, aligns = A.submit_arguments(art, [odd, y], [out], types)
+    with pytest.raises(rt.CUDAError) as err:
+        session.submit(kernel, args, [4, 1, 1], [256, 1, 1], 0, aligns)
+    assert "not aligned to 4 bytes" in str(err.value)
+    step = A.artifact_step(art, kernel, [0, 1], [2], types)
+    prog = session.prepareProgram([4000] * 3, [0, 1], [2], [step])
+    with pytest.raises(rt.CUDAError) as err:
+        prog.submit([odd, y], [out])
+    assert "not aligned to 4 bytes" in str(err.value)
     other = _fresh(session)
     with pytest.raises(rt.CUDAError) as err:
         other.submit(kernel, [None, None, None, b"\0\0\0\0"], [4, 1, 1], [256, 1, 1])
@@ -296,9 +306,9 @@ def test_graph_program_rebinds_ports(session):
     address changes."""
     n = 1 << 16
     rec = R.cfg5b_step(n)
-    art = artifact_for(rec)
+    art, types = artifact_for(rec)
     kernel = A.load_artifact(session, art)
-    step = A.artifact_step(art, kernel, [0, 1], [2])
+    step = A.artifact_step(art, kernel, [0, 1], [2], types)
     prog = session.prepareProgram([4 * n] * 3, [0, 1], [2], [step], graph=True)
     rng = np.random.default_rng(9)
     for _ in range(3):
