@@ -257,6 +257,27 @@ def build_artifact(request: dict, compile_fn=compile_source) -> dict:
             "launch": gen["launch"], "arguments": arguments, "required_element_types": gen["required_element_types"]}
 
 
+def request_for(recipe, entry: str = "step_kernel", grid: Sequence[int] = (592, 1, 1), scalars=(),
+                source: Optional[str] = None) -> dict:
+    """A protocol-v2 request for a recipe step: one pointer parameter per port
+    in port-map order (named input_N / output_N), then the given
+    (name, type, value) scalars."""
+    from . import Plan
+    ptype = {v: k for k, v in POINTER_TYPES.items()}
+    sig, bind, shapes = {}, {}, {}
+    for p in Plan(recipe, -1).describe()["port_map"]:
+        name = p["logical_port"].replace(":", "_")
+        sig[name] = ptype[p["element_type"]]
+        bind[name] = p["logical_port"]
+        shapes[p["logical_port"]] = [p["elements"]]
+    for name, t, v in scalars:
+        sig[name] = t
+        bind[name] = v
+    return {"protocol_version": 2, "source": source if source is not None else json.dumps(recipe), "entry": entry,
+            "signature": sig, "source_bindings": bind, "constants": {}, "fixed_options": {},
+            "target": {"backend": "cuda", "arch": ARCH}, "grid": [int(g) for g in grid], "port_shapes": shapes}
+
+
 ARTIFACT_FIELDS = ("protocol_version", "format", "payload", "entry", "target", "producer", "launch", "arguments",
                    "required_element_types")
 
@@ -339,6 +360,12 @@ def load_artifact(session, artifact: dict, element_types: Optional[Sequence[str]
     payload = base64.b64decode(artifact["payload"]) if artifact["format"] == "cubin" else artifact["payload"].encode()
     types = list(dict.fromkeys(list(artifact["required_element_types"]) + list(element_types or [])))
     return session.load(payload, artifact["entry"], types, artifact["target"]["arch"], parameter_widths(artifact))
+
+
+def request_parameters(request: dict) -> list:
+    """The generator's parameter list of a request whose source is a recipe:
+    each signature entry's port binding, or its scalar type."""
+    return [request["source_bindings"][k] if t in POINTER_TYPES else t for k, t in request["signature"].items()]
 
 
 ELEMENT_BYTES = {"bool": 1, "i32": 4, "i64": 8, "f32": 4, "f16": 2, "bf16": 2}

@@ -351,7 +351,12 @@ std::shared_ptr<KernelImpl> load_kernel(State& st, const std::string& image, con
     const size_t width = widths[i] ? widths[i] : sizeof(uint64_t);
     expected = (expected + width - 1) / width * width;
     size_t offset = 0, size = 0;
-    cuda_check(cudaFuncGetParamInfo(f, i, &offset, &size), "cudaFuncGetParamInfo");
+    const cudaError_t e = cudaFuncGetParamInfo(f, i, &offset, &size);
+    if (e == cudaErrorInvalidValue) {  // fewer parameters than declared
+      cudaGetLastError();
+      fail(ASK_B200_E_INVALID, "kernel parameter count differs from the declared ABI");
+    }
+    cuda_check(e, "cudaFuncGetParamInfo");
     require(offset == expected && size == width, "kernel parameter layout differs from the declared ABI");
     expected += width;
   }

@@ -132,7 +132,47 @@ def static_config(name, world, small=False):
     if name == "cfg4s":
         return {"workload": "cfg4 scatter_add: grad f32 [2^23,256] into zeros [2^20,256], idx Zipf(1.1)",
                 "l2": "8 GiB updates > L2"}
+    if name in ARTIFACT_WORKLOADS:
+        base = static_config(ARTIFACT_WORKLOADS[name], world, small)
+        return dict(base, workload=base["workload"] + ", as an external-kernel artifact v2 (cubin) run by the "
+                                                      "runtime's Session::load kernel step, CUDA graph")
     raise SystemExit(f"unknown workload {name}")
+
+
+# Kernel-artifact variants of single-GPU workloads: the same step compiled by
+# the artifact worker into a flat-parameter cubin and run as a loaded-kernel
+# program step (ask_b200.artifact).
+ARTIFACT_WORKLOADS = {"cfg1a": "cfg1", "cfg2a": "cfg2"}
+
+
+class _ArtifactLaunches:
+    """Launch accounting of an artifact step (one kernel per step)."""
+    kernel_launches = 1
+
+    def __init__(self, grid):
+        self._grid = grid
+
+    def describe(self):
+        return {"launch": {"grid": [self._grid, 1, 1]}}
+
+
+def artifact_step_runner(recipe, ins, outs, grid):
+    """Compile the recipe's artifact, load it on a runtime session and return
+    (session, submit function, kernel name)."""
+    from ask_b200 import artifact as A
+    from ask_b200 import runtime as rt
+    req = A.request_for(recipe, entry="bench_step", grid=(grid, 1, 1))
+    art = A.build_artifact(req)
+    session = rt.Session.create(rank_device())
+    kernel = A.load_artifact(session, art)
+    ni, no = len(ins), len(outs)
+    step = A.artifact_step(art, kernel, list(range(ni)), list(range(ni, ni + no)), A.port_types(req))
+    sizes = [t.numel() * t.element_size() for t in ins + outs]
+    prog = session.prepareProgram(sizes, list(range(ni)), list(range(ni, ni + no)), [step], graph=True)
+    bin_ = [session.importTensor(t, readonly=True) for t in ins]
+    bout = [session.importTensor(t) for t in outs]
+    body = A.artifact_source(recipe, "bench_step", [grid, 1, 1], A.request_parameters(req))["body"]
+    return session, prog, (lambda: prog.submit(bin_, bout)), f"artifact_{body}"
 
 
 def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
@@ -200,6 +240,19 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         return w
     if world > 1:
         raise SystemExit(f"workload {name} is single-GPU (replicas only)")
+    if name in ARTIFACT_WORKLOADS:
+        w = make_workload(ARTIFACT_WORKLOADS[name], rank, world, torch, ask_b200, R, comm, small)
+        w.name = name
+        recipe = R.cfg1_step(4096 * 4096) if name == "cfg1a" else R.cfg2_step(65536, 1024)
+        ins, outs = w.e2e["inputs"], w.e2e["results"]
+        grid = 148 * 8
+        session, prog, run, kname = artifact_step_runner(recipe, ins, outs, grid)
+        (_, nbytes, _), = w.kernels
+        w.kernels = [(kname, nbytes, run)]
+        w.plans = [_ArtifactLaunches(grid)]
+        w.session, w.program, w.stream_handle = session, prog, session.stream()
+        w.config = static_config(name, world)
+        return w
     if name == "cfg1":
         n = 4096 * 4096
         a, b, c = (gen(0, SEED["cfg1"], s, n, -4.0, 4.0, torch.float32) for s in range(3))
@@ -293,6 +346,7 @@ def cpu_sample(name: str, threads: int, budget_s: float = 12.0):
     workload.  Returns (bytes_per_second, seconds, description)."""
     import numpy as np
     import oracle
+    name = ARTIFACT_WORKLOADS.get(name, name)
     if name == "cfg5":
         na = 1 << 26
         nb = 1 << 25

@@ -26,21 +26,7 @@ def ports_of(recipe):
 
 
 def request_for(recipe, entry="step_kernel", grid=(296, 1, 1), scalars=(("n", "i32", 7),), source=None):
-    """A protocol-v2 request binding every port of the recipe, in port order,
-    with the given scalars appended."""
-    sig, bind, shapes = {}, {}, {}
-    ptype = {"bool": "*i1", "i32": "*i32", "i64": "*i64", "f32": "*fp32", "f16": "*fp16", "bf16": "*bf16"}
-    for p in ports_of(recipe):
-        name = p["logical_port"].replace(":", "_")
-        sig[name] = ptype[p["element_type"]]
-        bind[name] = p["logical_port"]
-        shapes[p["logical_port"]] = [p["elements"]]
-    for name, t, v in scalars:
-        sig[name] = t
-        bind[name] = v
-    return {"protocol_version": 2, "source": source if source is not None else json.dumps(recipe), "entry": entry,
-            "signature": sig, "source_bindings": bind, "constants": {}, "fixed_options": {},
-            "target": {"backend": "cuda", "arch": 100}, "grid": list(grid), "port_shapes": shapes}
+    return A.request_for(recipe, entry, grid, scalars, source)
 
 
 def fake_cubin(source):

@@ -231,7 +231,7 @@ def test_load_checks_the_declared_abi(session):
     assert session.stats()["module_hits"] == before["module_hits"] + 1 and k2.entry() == art["entry"]
     assert k1.maxThreads() >= 256
     for bad_widths, msg in [([0, 0, 0, 8], "parameter layout differs"), ([0, 0, 0], "count differs"),
-                            ([0, 0, 0, 4, 4], "parameter layout differs"), ([0, 0, 3, 4], "unsupported kernel parameter width")]:
+                            ([0, 0, 0, 4, 4], "count differs"), ([0, 0, 3, 4], "unsupported kernel parameter width")]:
         with pytest.raises(rt.CUDAError) as err:
             _fresh(session).load(image, art["entry"], ["i32"], 100, bad_widths)
         assert msg in str(err.value), (bad_widths, str(err.value))
