@@ -201,6 +201,24 @@ std::string reductions_struct(const RedArgs& a) {
   return o.str();
 }
 
+// The library's specialised reductions as artifact template arguments: value
+// source, reduction set and 16-byte loads in flight (reduce_kernels.cu's
+// with_spec table).
+struct FastReduction {
+  int spec;
+  const char* source;
+  const char* set;
+  int unroll;
+};
+constexpr FastReduction kFastReductions[] = {
+    {RED_ROWSTATS_F32, "askb::red::SrcF32", "askb::red::RedSet<askb::RED_SUM, askb::RED_MAX, askb::RED_MIN, askb::RED_ARGMAX>", 8},
+    {RED_GLOBAL_F32, "askb::red::SrcF32", "askb::red::RedSet<askb::RED_SUM, askb::RED_MIN, askb::RED_ARGMIN>", 8},
+    {RED_SOFTMAX_MAX_F16, "askb::red::SrcCast<askb::kF16>", "askb::red::RedSet<askb::RED_MAX>", 4},
+    {RED_SOFTMAX_MAX_BF16, "askb::red::SrcCast<askb::kBF16>", "askb::red::RedSet<askb::RED_MAX>", 4},
+    {RED_SOFTMAX_SUM_F16, "askb::red::SrcExpShift<askb::kF16>", "askb::red::RedSet<askb::RED_SUM>", 4},
+    {RED_SOFTMAX_SUM_BF16, "askb::red::SrcExpShift<askb::kBF16>", "askb::red::RedSet<askb::RED_SUM>", 4},
+};
+
 struct Generated {
   std::string source, body;
   std::vector<unsigned> widths;
@@ -251,8 +269,19 @@ Generated generate(const ask_b200_plan& pl, const std::string& entry, const uint
         for (size_t k = 0; k < ni; ++k)
           if (pl.inputs[k].map == IM_FULL || pl.inputs[k].map == IM_INNER) body << " && askb::art::aligned16(" << ins(k) << ")";
         for (size_t k = 0; k < no; ++k) body << " && askb::art::aligned16(" << outs(k) << ")";
-        body << ";\n  askb::ew::ew_spec_loop<Program, 4, 2>(args, aligned ? 1 : 0);\n";
-        g.body = "elementwise";
+        body << ";\n";
+        // The library's hand-written loops for its specialised programs
+        // (ew_kernels.cu: ew_launch), when every unit is whole and aligned.
+        const char* functor = pl.spec == EW_CFG1 ? "askb::ew::FnCfg1"
+                              : pl.spec == EW_SOFTMAX_NORM_F16 ? "askb::ew::FnSoftmaxNorm<askb::kF16>"
+                              : pl.spec == EW_SOFTMAX_NORM_BF16 ? "askb::ew::FnSoftmaxNorm<askb::kBF16>" : nullptr;
+        if (functor) {
+          body << "  using F = " << functor << ";\n  if (aligned && " << u64(pl.count) << " % F::V == 0 && (!F::kRowMapped || "
+               << u64(d.d) << " % F::V == 0))\n    askb::ew::ew_functor_loop<F>(args, " << u64(pl.count)
+               << " / F::V);\n  else\n  ";
+        }
+        body << "  askb::ew::ew_spec_loop<Program, 4, 2>(args, aligned ? 1 : 0);\n";
+        g.body = functor ? "elementwise_functor" : "elementwise";
       }
       break;
     }
@@ -262,6 +291,9 @@ Generated generate(const ask_b200_plan& pl, const std::string& entry, const uint
       decls = program_struct(pl.ssa, "Program") + reductions_struct(a);
       pointer_arrays();
       const uint64_t warps = grid[0] * 256 / 32;
+      const FastReduction* fast = nullptr;
+      for (const FastReduction& f : kFastReductions)
+        if (a.inner == 1 && pl.spec == f.spec) fast = &f;
       if (a.inner != 1) {
         body << "  askb::art::reduce_columns<Program, Reductions, " << u64(a.outer) << ", " << u64(a.extent) << ", "
              << u64(a.inner) << ", " << u64(a.index_base) << ">(in, out);\n";
@@ -275,9 +307,21 @@ Generated generate(const ask_b200_plan& pl, const std::string& entry, const uint
           }
         body << ";\n";
         const bool cta = a.outer * 2 <= warps && a.extent >= 1024;
-        body << "  askb::art::" << (cta ? "reduce_rows_cta" : "reduce_rows_warp") << "<Program, Reductions, "
-             << u64(a.outer) << ", " << u64(a.extent) << ", " << u64(a.index_base) << ">(in, out, aligned);\n";
-        g.body = cta ? "reduce_rows_cta" : "reduce_rows_warp";
+        if (fast) {
+          body << "  askb::RedArgs a;\n";
+          for (size_t k = 0; k < ni; ++k) body << "  a.in[" << k << "] = " << ins(k) << ";\n";
+          for (size_t k = 0; k < no; ++k) body << "  a.out[" << k << "] = " << outs(k) << ";\n";
+          body << "  a.outer = " << u64(a.outer) << ";\n  a.extent = " << u64(a.extent) << ";\n  a.inner = 1;\n"
+               << "  a.index_base = " << u64(a.index_base) << ";\n  a.n_red = " << int(a.n_red) << ";\n";
+          const std::string targs = std::string("<") + fast->source + ", " + fast->set + ", " + std::to_string(fast->unroll) + ">";
+          body << (cta ? "  askb::art::reduce_rows_cta_fast" : "  askb::red::red_warp_row_loop") << targs
+               << "(a, aligned ? 1 : 0);\n";
+          g.body = cta ? "reduce_rows_cta_fast" : "reduce_rows_warp_fast";
+        } else {
+          body << "  askb::art::" << (cta ? "reduce_rows_cta" : "reduce_rows_warp") << "<Program, Reductions, "
+               << u64(a.outer) << ", " << u64(a.extent) << ", " << u64(a.index_base) << ">(in, out, aligned);\n";
+          g.body = cta ? "reduce_rows_cta" : "reduce_rows_warp";
+        }
       }
       break;
     }

@@ -18,6 +18,7 @@
 
 #include "ew_body.cuh"
 #include "reduce_acc.cuh"
+#include "reduce_fast.cuh"
 
 namespace askb {
 namespace art {
@@ -161,6 +162,21 @@ __device__ __forceinline__ void reduce_rows_cta(const void* const* in, void* con
     fold_row<P, RL, 4, EXTENT, BASE>(in, o * EXTENT, o, threadIdx.x, kThreads, aligned, s);
     acc_block_reduce<RL>(s);
     if (threadIdx.x == 0) acc_write<RL>(out, s, o);
+  }
+}
+
+// The library's specialised reductions (compile-time source S and set R, the
+// exact f32 fast fold) with a CTA per output row; the warp-per-row form is
+// red::red_warp_row_loop itself.
+template <class S, class R, int U>
+__device__ __forceinline__ void reduce_rows_cta_fast(const RedArgs& a, int aligned) {
+  for (uint64_t o = blockIdx.x; o < a.outer; o += gridDim.x) {
+    red::FastAcc s;
+    red::fast_init(s);
+    const typename S::Row rw = S::row(a, o);
+    red::span_src<S, R, U>(a, rw, o * a.extent, 0, a.extent, threadIdx.x, kThreads, aligned != 0, s);
+    red::fast_block_reduce<R>(s);
+    if (threadIdx.x == 0) red::fast_write<R, 0>(a, s, o);
   }
 }
 

@@ -116,5 +116,135 @@ __device__ __forceinline__ void ew_view_loop(const Program& prog, const EwArgs& 
   }
 }
 
+// ---- hand-written functor kernels for the hottest programs ------------------------
+// Software-pipelined grid-stride loop over whole 16-byte units: the loads of the
+// next unit are in flight while the current unit is computed, so latency is
+// hidden without depending on other warps.  Used only when every port is
+// 16-byte aligned and the element count is a multiple of the unit; the
+// interpreter kernels above serve every other case.
+template <class F>
+__device__ __forceinline__ void ew_functor_loop(const EwArgs& a, uint64_t units) {
+  const uint64_t stride = uint64_t(gridDim.x) * kEwThreads;
+  uint64_t u = uint64_t(blockIdx.x) * kEwThreads + threadIdx.x;
+  if (u >= units) return;
+  typename F::In cur = F::load(a, u), nxt;
+  for (; u < units; u += stride) {
+    const uint64_t un = u + stride;
+    if (un < units) nxt = F::load(a, un);
+    F::store(a, u, F::compute(a, cur));
+    cur = nxt;
+  }
+}
+
+// ProgCfg1: y0 = exp(a)*b + c ; y1 = maximum(a, b) + tanh(c)*(-1), 4 elements per unit.
+struct FnCfg1 {
+  static constexpr int V = 4;
+  static constexpr bool kRowMapped = false;
+  struct In { uint4 a, b, c; };
+  struct Out { float y0[4], y1[4]; };
+  __device__ static In load(const EwArgs& e, uint64_t u) {
+    return In{ld_stream_v4(static_cast<const uint4*>(e.in[0]) + u), ld_stream_v4(static_cast<const uint4*>(e.in[1]) + u),
+              ld_stream_v4(static_cast<const uint4*>(e.in[2]) + u)};
+  }
+  __device__ static Out compute(const EwArgs&, const In& x) {
+    const float a[4] = {__uint_as_float(x.a.x), __uint_as_float(x.a.y), __uint_as_float(x.a.z), __uint_as_float(x.a.w)};
+    const float b[4] = {__uint_as_float(x.b.x), __uint_as_float(x.b.y), __uint_as_float(x.b.z), __uint_as_float(x.b.w)};
+    const float c[4] = {__uint_as_float(x.c.x), __uint_as_float(x.c.y), __uint_as_float(x.c.z), __uint_as_float(x.c.w)};
+    Out o;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      o.y0[v] = __fadd_rn(__fmul_rn(expf(a[v]), b[v]), c[v]);
+      o.y1[v] = __fadd_rn(ask_maximum(a[v], b[v]), __fmul_rn(tanhf(c[v]), -1.0f));
+    }
+    return o;
+  }
+  __device__ static void store(const EwArgs& e, uint64_t u, const Out& o) {
+    st_stream_v4(static_cast<uint4*>(e.out[0]) + u, make_uint4(__float_as_uint(o.y0[0]), __float_as_uint(o.y0[1]),
+                                                                __float_as_uint(o.y0[2]), __float_as_uint(o.y0[3])));
+    st_stream_v4(static_cast<uint4*>(e.out[1]) + u, make_uint4(__float_as_uint(o.y1[0]), __float_as_uint(o.y1[1]),
+                                                                __float_as_uint(o.y1[2]), __float_as_uint(o.y1[3])));
+  }
+};
+
+// ProgSoftmaxNorm<T>: y = cast(exp(cast(x, f32) + m*(-1)) / s, T), 8 elements per
+// unit; m and s are indexed by the row (unit*8 / inner).
+//
+// The division is the correctly rounded f32 quotient, computed from the row's
+// correctly rounded reciprocal y = RN(1/s) by Markstein's correction: with
+// q0 = RN(e*y) and two steps r = fma(-q, s, e) (exact when q is within an ulp
+// of e/s and no value is subnormal), q' = fma(r, y, q), the last q equals
+// RN(e/s) (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990).  The
+// theorem's conditions -- s and y normal, a normal quotient -- are checked;
+// a unit that fails them (a zero, subnormal, infinite or NaN operand or
+// result, which softmax rows reach only at their extremes) is recomputed with
+// the IEEE division.  One reciprocal per row replaces one per element, and
+// the division no longer occupies the special-function unit per element.
+template <int T>
+struct FnSoftmaxNorm {
+  static constexpr int V = 8;
+  static constexpr bool kRowMapped = true;  // m, s are indexed by unit*8 / inner
+  struct In { uint4 x; float nm, s, y; };
+  using Out = uint4;
+  __device__ static float widen(uint32_t h) {
+    if constexpr (T == kF16) return __half2float(__ushort_as_half(uint16_t(h)));
+    else return __uint_as_float(h << 16);
+  }
+  __device__ static uint32_t narrow(float f) {
+    if constexpr (T == kF16) return __half_as_ushort(__float2half_rn(f));
+    else return bf16_bits_rne(f);
+  }
+  // Two non-NaN values rounded to nearest-even and packed (lo in bits 0..15):
+  // one cvt.rn.{f16,bf16}x2.f32.  For bf16 this equals bf16_bits_rne on every
+  // non-NaN input; NaN inputs take narrow() (the payload-preserving rule).
+  __device__ static uint32_t narrow2(float lo, float hi) {
+    uint32_t r;
+    if constexpr (T == kF16)
+      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    else
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  }
+  __device__ static In load(const EwArgs& e, uint64_t u) {
+    const uint64_t row = udiv(u * V, e.inner);
+    const float s = __ldg(static_cast<const float*>(e.in[2]) + row);
+    return In{ld_stream_v4(static_cast<const uint4*>(e.in[0]) + u),
+              __fmul_rn(__ldg(static_cast<const float*>(e.in[1]) + row), -1.0f), s, __frcp_rn(s)};
+  }
+  __device__ static Out compute(const EwArgs&, const In& x) {
+    const uint32_t w[4] = {x.x.x, x.x.y, x.x.z, x.x.w};
+    float e[8], q[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      e[2 * j] = expf(__fadd_rn(widen(w[j] & 0xffffu), x.nm));
+      e[2 * j + 1] = expf(__fadd_rn(widen(w[j] >> 16), x.nm));
+    }
+    const float s = x.s, y = x.y;
+    bool ok = s >= 0x1p-100f && s <= 0x1p100f;  // s and y = RN(1/s) normal (false for NaN)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float t = __fmul_rn(e[k], y);
+      t = __fmaf_rn(__fmaf_rn(-t, s, e[k]), y, t);
+      t = __fmaf_rn(__fmaf_rn(-t, s, e[k]), y, t);
+      q[k] = t;
+      ok &= (t >= 0x1p-124f && t <= 0x1p126f) || e[k] == 0.0f;
+    }
+    uint32_t r[4];
+    if (ok) {  // every q is finite
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = narrow2(q[2 * j], q[2 * j + 1]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[k] = __fdiv_rn(e[k], s);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = narrow(q[2 * j]) | (narrow(q[2 * j + 1]) << 16);
+    }
+    return make_uint4(r[0], r[1], r[2], r[3]);
+  }
+  __device__ static void store(const EwArgs& e, uint64_t u, const Out& o) {
+    st_stream_v4(static_cast<uint4*>(e.out[0]) + u, o);
+  }
+};
+
 }  // namespace ew
 }  // namespace askb

@@ -44,11 +44,14 @@ def cases():
     v = p.input("f32")
     col_rec = R.reduce(p, v, ["sum", "argmax"], 3, 50, 7)
     return {
-        "cfg1": (R.cfg1_step(4099), "elementwise"),
+        "cfg1": (R.cfg1_step(4099), "elementwise_functor"),
+        "softmax_norm": (R.cfg3_steps("bf16", 64, 1024)[2], "elementwise_functor"),
         "cfg5b": (R.cfg5b_step(1 << 20), "elementwise"),
         "i64_scalar": (i64_rec, "elementwise"),
-        "cfg2_rows": (R.cfg2_step(65536, 1024), "reduce_rows_warp"),
-        "cfg5a_global": (R.cfg5a_step(1 << 24), "reduce_rows_cta"),
+        "cfg2_rows": (R.cfg2_step(65536, 1024), "reduce_rows_warp_fast"),
+        "softmax_max": (R.cfg3_steps("f16", 64, 4096)[0], "reduce_rows_cta_fast"),
+        "softmax_sum": (R.cfg3_steps("bf16", 4096, 512)[1], "reduce_rows_warp_fast"),
+        "cfg5a_global": (R.cfg5a_step(1 << 24), "reduce_rows_cta_fast"),
         "bool_any_all": (any_rec, "reduce_rows_cta"),
         "columns": (col_rec, "reduce_columns"),
         "gather_rows": (R.cfg4_gather_step(1000, 64, 4096), "gather_rows"),

@@ -194,16 +194,22 @@ def test_integer_and_bool_reductions(session, dtype, cols):
         assert np.array_equal(got[k], want[k]), ops[k]
 
 
-def test_prologue_reads_outer_and_scalar_ports(session):
-    """Softmax step 1 as an artifact: exp(cast(x) - m[row]) summed per row."""
-    rows, cols = 64, 4096
+@pytest.mark.parametrize("dt,rows,cols", [("f16", 64, 4096), ("bf16", 4096, 512)])
+def test_softmax_steps(session, dt, rows, cols):
+    """The three softmax steps as artifacts (row max; sum of exp(cast(x) - m[row])
+    with an outer-indexed port; normalise) against the oracle."""
     rng = np.random.default_rng(2)
-    x = (rng.standard_normal(rows * cols) * 3).astype(np.float16).view(np.uint16)
-    m = f16_to_f32(x).reshape(rows, cols).max(axis=1).astype(np.float32)
-    rec = R.cfg3_steps("f16", rows, cols)[1]
-    (got,) = run_artifact(session, rec, [x, m], ["f32"])
-    (want,) = oracle.reduce(rec, [x, m])
-    assert np.all(np.abs(got.astype(np.float64) - want) <= 2.0 ** -20 * np.abs(want))
+    xf = (rng.standard_normal(rows * cols) * 3).astype(np.float32)
+    x = xf.astype(np.float16).view(np.uint16) if dt == "f16" else (xf.view(np.uint32) >> 16).astype(np.uint16)
+    steps = R.cfg3_steps(dt, rows, cols)
+    (m,) = run_artifact(session, steps[0], [x], ["f32"])
+    assert np.array_equal(m, oracle.reduce(steps[0], [x])[0])
+    (s,) = run_artifact(session, steps[1], [x, m], ["f32"])
+    (want,) = oracle.reduce(steps[1], [x, m])
+    assert np.all(np.abs(s.astype(np.float64) - want) <= 2.0 ** -20 * np.abs(want))
+    (y,) = run_artifact(session, steps[2], [x, m, s], [dt])
+    (wy,) = oracle.elementwise(steps[2], [x, m, s])
+    assert_same(y, wy, dt)
 
 
 # ---- gather -----------------------------------------------------------------------------
