@@ -351,7 +351,9 @@ Generated generate(const ask_b200_plan& pl, const std::string& entry, const uint
   }
   src << "// ask_b200 kernel artifact (" << g.body << "), generated from a recipe step.\n"
       << "#include \"artifact_bodies.cuh\"\n\nnamespace {\n" << decls << "}  // namespace\n\n"
-      << "extern \"C\" __global__ void __launch_bounds__(askb::art::kThreads) " << entry << "(" << sig.str() << ") {\n"
+      << "extern \"C\" __global__ void __launch_bounds__(askb::art::kThreads"
+      << (g.body == "elementwise_functor" ? ", askb::art::kFunctorMinBlocks" : "") << ") " << entry << "(" << sig.str()
+      << ") {\n"
       << body.str() << "}\n";
   g.source = src.str();
   return g;

@@ -24,6 +24,12 @@ namespace askb {
 namespace art {
 
 constexpr int kThreads = 256;  // block size of every artifact kernel
+// Resident CTAs an entry with a functor loop is compiled for: the functor
+// loops need at most 48 registers (the library's functor kernels use 47), and
+// the bound keeps the entry's compile-time-program fallback (misaligned
+// ports) from raising the whole kernel's register count and lowering its
+// occupancy.
+constexpr int kFunctorMinBlocks = 5;
 
 __device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -209,7 +209,12 @@ def test_softmax_steps(session, dt, rows, cols):
     assert np.all(np.abs(s.astype(np.float64) - want) <= 2.0 ** -20 * np.abs(want))
     (y,) = run_artifact(session, steps[2], [x, m, s], [dt])
     (wy,) = oracle.elementwise(steps[2], [x, m, s])
-    assert_same(y, wy, dt)
+    # CUDA's expf against the host libm's exp: within one unit of the output type
+    conv = f16_to_f32 if dt == "f16" else bf16_to_f32
+    gyv, wyv = conv(y), conv(wy)
+    step = np.spacing(np.abs(wyv).astype(np.float16)).astype(np.float32) if dt == "f16" else \
+        np.abs(bf16_to_f32(wy + 1) - wyv)
+    assert np.all(np.abs(gyv - wyv) <= step + 1e-45)
 
 
 # ---- gather -----------------------------------------------------------------------------
