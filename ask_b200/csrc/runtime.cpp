@@ -139,6 +139,7 @@ struct State {
   std::map<std::string, uint64_t> counters;
   std::vector<std::shared_ptr<EventImpl>> pending;
   std::map<std::pair<std::string, std::string>, std::shared_ptr<KernelImpl>> kernels;  // (image, entry)
+  std::vector<cudaEvent_t> free_events;  // completion events of retired submissions, for reuse
   int major = 0, minor = 0;
   unsigned max_grid[3] = {0, 0, 0}, max_block[3] = {0, 0, 0}, max_threads = 0;
   ~State() {
@@ -147,6 +148,7 @@ struct State {
       int prev = 0;
       cudaGetDevice(&prev);
       cudaSetDevice(device);
+      for (cudaEvent_t e : free_events) cudaEventDestroy(e);
       if (stream) cudaStreamDestroy(stream);
       if (capture) cudaStreamDestroy(capture);
       cudaSetDevice(prev);
@@ -268,16 +270,29 @@ struct EventImpl {
     kernel.reset();
     finished = true;
   }
+  // The event goes back to the session's pool (the reference keeps retired
+  // completion events for reuse, lib/Runtime/CUDA.cpp:554-564).
   ~EventImpl() {
     if (ev) {
-      int prev = 0;
-      cudaGetDevice(&prev);
-      cudaSetDevice(st->device);
-      cudaEventDestroy(ev);
-      cudaSetDevice(prev);
+      std::lock_guard<std::recursive_mutex> lock(st->mu);
+      st->free_events.push_back(ev);
     }
   }
 };
+
+// A completion event from the session's pool, or a new one.
+cudaEvent_t take_event(State& st) {
+  if (!st.free_events.empty()) {
+    cudaEvent_t e = st.free_events.back();
+    st.free_events.pop_back();
+    ++st.counters["event_reuses"];
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+  ++st.counters["event_creations"];
+  return e;
+}
 
 // Retire completed submissions (Session::reap).
 void reap(State& s) {
@@ -817,7 +832,7 @@ std::shared_ptr<EventImpl> enqueue(const std::shared_ptr<State>& stp, const std:
   const std::vector<uint64_t> addr = addresses(p, bound, *ws);
   auto ev = std::make_shared<EventImpl>();
   ev->st = stp;
-  cuda_check(cudaEventCreateWithFlags(&ev->ev, cudaEventDisableTiming), "cudaEventCreate");
+  ev->ev = take_event(st);
   try {
     if (p.graph) {
       if (!ws->exec)
@@ -982,7 +997,8 @@ int ask_b200_session_create(int device, ask_b200_session** out) {
     cuda_check(cudaStreamCreateWithFlags(&st->capture, cudaStreamNonBlocking), "cudaStreamCreate");
     for (const char* k : {"allocations", "launches", "program_submissions", "workspace_reuses", "prepared_internal_slots",
                           "prepared_internal_bytes", "graph_instantiations", "graph_launches", "graph_nodes",
-                          "graph_edges", "graph_node_updates", "fused_softmax_steps", "module_loads", "module_hits"})
+                          "graph_edges", "graph_node_updates", "fused_softmax_steps", "module_loads", "module_hits", "event_creations",
+                          "event_reuses"})
       st->counters[k] = 0;
     *out = new ask_b200_session{st};
   });
@@ -1240,7 +1256,7 @@ int ask_b200_kernel_submit(ask_b200_session* s, ask_b200_kernel* k, const ask_b2
     reap(st);
     auto ev = std::make_shared<EventImpl>();
     ev->st = s->st;
-    cuda_check(cudaEventCreateWithFlags(&ev->ev, cudaEventDisableTiming), "cudaEventCreate");
+    ev->ev = take_event(st);
     launch_kernel(kern, words, grid, block, shared_bytes, st.stream);
     ++st.counters["launches"];
     cuda_check(cudaEventRecord(ev->ev, st.stream), "cudaEventRecord");

@@ -245,6 +245,26 @@ class PreparedProgram:
                                             ctypes.byref(ev)))
         return Event(ev)
 
+    def bind(self, inputs: Sequence[DeviceBuffer], outputs: Sequence[DeviceBuffer]):
+        """A pre-marshalled ``submit(inputs, outputs)`` for repeated submissions
+        of the same buffers: each call enqueues the program and drops its
+        completion handle (the session keeps the submission alive until the
+        GPU is done; ``Session.synchronize`` waits for it)."""
+        ins, outs = _handles(inputs), _handles(outputs)
+        ni, no = len(inputs), len(outputs)
+        ev = _p()
+        ref = ctypes.byref(ev)
+        h, submit, release = self._h, _lib.ask_b200_program_submit, _lib.ask_b200_event_release
+        keep = (self, list(inputs), list(outputs))
+
+        def run():
+            status = submit(h, ins, ni, outs, no, ref)
+            if status != OK:
+                _check(status)
+            release(ev)
+        run.keep = keep
+        return run
+
     def run(self, inputs: Sequence[DeviceBuffer]):
         outs = (_p * max(self._n_outputs, 1))()
         ev = _p()

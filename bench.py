@@ -172,7 +172,7 @@ def artifact_step_runner(recipe, ins, outs, grid):
     bin_ = [session.importTensor(t, readonly=True) for t in ins]
     bout = [session.importTensor(t) for t in outs]
     body = A.artifact_source(recipe, "bench_step", [grid, 1, 1], A.request_parameters(req))["body"]
-    return session, prog, (lambda: prog.submit(bin_, bout)), f"artifact_{body}"
+    return session, prog, prog.bind(bin_, bout), f"artifact_{body}"
 
 
 def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
@@ -291,11 +291,7 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
                                       [rt.PlanStep(steps[0], [0], [1]), rt.PlanStep(steps[1], [0, 1], [2]),
                                        rt.PlanStep(steps[2], [0, 1, 2], [3])], graph=True)
         kernel = prog.describe()["steps"][0]["kernel"]
-        xin = session.importTensor(x, readonly=True)
-        bufs = [session.importTensor(t) for t in (m, s, y)]
-
-        def run():
-            prog.submit([xin], bufs)
+        run = prog.bind([session.importTensor(x, readonly=True)], [session.importTensor(t) for t in (m, s, y)])
         w.plans = [ask_b200.Plan({"family": "softmax", "dtype": dt, "rows": rows, "cols": cols}, rank_device())]
         w.kernels = [(kernel, 4 * n + 8 * rows, run)]
         w.global_bytes = 4 * 2 * n + 6 * 4 * rows

@@ -257,3 +257,27 @@ def test_closed_session_refuses_work(device):
     session.close()
     rejects(lambda: program.run([src]))
     rejects(lambda: session.allocate(16))
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_bound_submissions_reuse_completion_events(device, graph):
+    """PreparedProgram.bind repeats one submission; retired completion events
+    return to the session's pool (event_reuses), as in the reference."""
+    s = rt.Session.create(0)
+    n = 1 << 12
+    prog = s.prepareProgram([4 * n, 4 * n], [0], [1], [rt.PlanStep(double_i32(n), [0], [1])], graph=graph)
+    x = s.allocate(4 * n)
+    x.copyFromHost(np.arange(n, dtype=np.int32).tobytes())
+    y = s.allocate(4 * n)
+    run = prog.bind([x], [y])
+    for _ in range(200):
+        run()
+    s.synchronize()
+    assert np.array_equal(i32s(y), 2 * np.arange(n, dtype=np.int32))
+    for _ in range(50):
+        run()
+    s.synchronize()
+    st = s.stats()
+    assert st["program_submissions"] == 250
+    assert st["event_reuses"] > 0 and st["event_creations"] + st["event_reuses"] == 250
+    s.close()
