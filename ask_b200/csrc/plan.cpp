@@ -436,6 +436,7 @@ void finish_elementwise(ask_b200_plan& pl) {
   if (pl.views) {
     pl.kernel = "ew_view";
     int occ = pl.device >= 0 ? ew_view_occupancy() : 8;
+    if (pl.blocks_per_sm) occ = std::min(occ, pl.blocks_per_sm);
     const uint64_t needed = (pl.count + kEwThreads - 1) / kEwThreads;
     pl.grid = int(std::max<uint64_t>(1, std::min(needed, uint64_t(std::max(occ, 1)) * uint64_t(pl.num_sms))));
     pl.launches = pl.count ? 1 : 0;
@@ -446,6 +447,7 @@ void finish_elementwise(ask_b200_plan& pl) {
   pl.kernel = names[pl.spec];
   int occ = blocks_per_sm_default(0);
   if (pl.device >= 0) check_cuda(ew_occupancy(pl.spec, &occ), "occupancy");
+  if (pl.blocks_per_sm) occ = std::min(occ, pl.blocks_per_sm);
   const uint64_t units = (pl.count + 3) / 4;
   const uint64_t needed = (units + kEwThreads - 1) / kEwThreads;
   const uint64_t cap = uint64_t(std::max(occ, 1)) * uint64_t(pl.num_sms);
@@ -634,6 +636,7 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   pl.kernel = std::string("reduce_") + strat_names[pl.strategy] + "_" + spec_names[pl.spec];
   int occ = blocks_per_sm_default(0);
   if (pl.device >= 0) check_cuda(red_occupancy(pl.spec, pl.strategy, &occ), "occupancy");
+  if (pl.blocks_per_sm) occ = std::min(occ, pl.blocks_per_sm);
   const uint64_t cap = uint64_t(std::max(occ, 1)) * uint64_t(pl.num_sms);
   uint64_t needed;
   if (pl.strategy == RS_WARP_ROW) needed = (outer + (kRedThreads / 32) - 1) / (kRedThreads / 32);
@@ -942,6 +945,13 @@ int ask_b200_plan_create(const char* recipe_json, int device, ask_b200_plan** ou
     const json::Value r = json::parse(recipe_json);
     if (r.kind != json::Value::Object) fail(ASK_B200_E_INVALID, "recipe must be a JSON object");
     const std::string fam = r.at("family").as_str("family");
+    // Optional cap on resident CTAs per SM of the persistent grids, to leave
+    // room for a kernel that must run beside this one (a collective).
+    if (const json::Value* b = r.get("blocks_per_sm")) {
+      const int64_t v = b->as_int("blocks_per_sm");
+      if (v < 1 || v > 32) fail(ASK_B200_E_INVALID, "blocks_per_sm must be in [1, 32]");
+      pl->blocks_per_sm = int(v);
+    }
     if (fam == "elementwise") { pl->family = FAM_ELEMENTWISE; build_elementwise(*pl, r); }
     else if (fam == "reduce") { pl->family = FAM_REDUCE; build_reduce(*pl, r); }
     else if (fam == "gather") { pl->family = FAM_GATHER; build_index(*pl, r, false); }

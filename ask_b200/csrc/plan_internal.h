@@ -42,5 +42,6 @@ struct ask_b200_plan {
   bool shardable = false;
   std::string kernel;
   int block = 256;  // threads per CTA where the family fixes it (softmax)
+  int blocks_per_sm = 0;  // recipe cap on resident CTAs per SM of a persistent grid (0 = occupancy)
 };
 

@@ -209,3 +209,18 @@ def test_shard_ranges_partition_the_axis():
                 assert e0 == b1
             if total >= 1024 * world:
                 assert all(b % 1024 == 0 for b, _ in spans)
+
+
+def test_blocks_per_sm_caps_persistent_grids():
+    rec = R.cfg5b_step(1 << 28)
+    full = ask_b200.Plan(rec, -1).describe()["launch"]["grid"][0]
+    rec["blocks_per_sm"] = 3
+    assert ask_b200.Plan(rec, -1).describe()["launch"]["grid"][0] == 3 * 148 < full
+    red = R.cfg2_step(65536, 1024)
+    red["blocks_per_sm"] = 2
+    assert ask_b200.Plan(red, -1).describe()["launch"]["grid"][0] == 2 * 148
+    for bad in (0, 33, -1):
+        rec["blocks_per_sm"] = bad
+        with pytest.raises(ask_b200.AskB200Error) as err:
+            ask_b200.Plan(rec, -1)
+        assert "blocks_per_sm" in str(err.value)
