@@ -196,16 +196,7 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         xi = gen(4, SEED["cfg5"], 1, b1 - b0, 0, 0, torch.int32, b0)
         yi = gen(4, SEED["cfg5"], 2, b1 - b0, 0, 0, torch.int32, b0)
         pa = ask_b200.Plan(R.cfg5a_step(a1 - a0, index_base=a0), rank_device())
-        rb = R.cfg5b_step(b1 - b0)
-        if world > 1:
-            # The chain runs beside the sharded reduction's all-gather: one CTA
-            # slot per SM stays free so NCCL's kernel starts as soon as the
-            # reduction ends instead of after the chain's persistent grid.
-            occ = ask_b200.Plan(rb, rank_device()).describe()["launch"]["grid"][0] // torch.cuda.get_device_properties(
-                dev).multi_processor_count
-            if occ > 1:
-                rb["blocks_per_sm"] = occ - 1
-        pb = ask_b200.Plan(rb, rank_device())
+        pb = ask_b200.Plan(R.cfg5b_step(b1 - b0), rank_device())
         outs = [torch.empty(1, dtype=torch.float32, device=dev), torch.empty(1, dtype=torch.float32, device=dev),
                 torch.empty(1, dtype=torch.int64, device=dev)]
         z = torch.empty_like(xi)
