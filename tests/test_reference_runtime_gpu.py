@@ -1,0 +1,132 @@
+"""Kernel artifacts run by the REFERENCE's own Runtime.
+
+oracle/_ref/libask_ref.so is the reference's lib/Runtime/CUDA.cpp (with its
+PASS checker) compiled from source.  Each test compiles an ask_b200 artifact
+through the worker path and hands it to that Runtime exactly as an ASK caller
+would: Session::load with the artifact's entry, element types, arch 100 and
+parameter widths (its cuFuncGetParamInfo layout check included), then
+prepareProgram with one kernel PlanStep, run -- in stream and graph mode, with
+fresh inputs per run so graph mode re-binds its node.  Results are compared
+with the CPU oracle under the same bars as the library's own tests.
+"""
+import base64
+
+import numpy as np
+import pytest
+
+import ask_b200
+import oracle
+from ask_b200 import artifact as A
+from ask_b200 import recipes as R
+from gpu_util import NUMPY, f16_to_f32, bf16_to_f32
+from test_gpu_parity import check_cfg1, random_inputs, random_program, same_with_nan
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ref(device):
+    from oracle import ref as ref_mod
+    if ref_mod.load() is None:
+        pytest.skip("the reference Runtime is not built here (oracle/_ref; oracle/ref_build.py needs its sources)")
+    return ref_mod
+
+
+def run_reference(ref, recipe, inputs, graph=False, repeats=1, grid=592):
+    """(outputs as numpy arrays, session stats) of the recipe's artifact run by the reference Runtime."""
+    req = A.request_for(recipe, entry="ref_step", grid=(grid, 1, 1), scalars=(("n", "i32", 7), ("alpha", "fp32", 0.5)))
+    art = A.build_artifact(req)
+    A.validate_artifact(art, req)
+    ports = ask_b200.Plan(recipe, -1).describe()["port_map"]
+    n_in = len(inputs)
+    arg_buffer, scalars = [], []
+    for a in art["arguments"]:
+        if isinstance(a, str):
+            kind, k = a.split(":")
+            arg_buffer.append(int(k) if kind == "input" else n_in + int(k))
+            scalars.append(b"")
+        else:
+            arg_buffer.append(-1)
+            scalars.append(A.scalar_bytes(a["type"], a["value"]))
+    types = list(dict.fromkeys(art["required_element_types"] + [p["element_type"] for p in ports]))
+    out_ports = ports[n_in:]
+    launch = art["launch"]
+    outs, stats = ref.run_step(base64.b64decode(art["payload"]), art["entry"], types, art["target"]["arch"],
+                               A.parameter_widths(art), arg_buffer, scalars, launch["grid"], launch["block"],
+                               launch["shared_bytes"], [np.ascontiguousarray(x).tobytes() for x in inputs],
+                               [p["elements"] * p["storage_bytes"] for p in out_ports], graph=graph, repeats=repeats)
+    arrays = [np.frombuffer(o, dtype=NUMPY[p["element_type"]]).copy() for o, p in zip(outs, out_ports)]
+    return arrays, stats
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_cfg1_through_the_reference_runtime(ref, graph):
+    n = 1 << 18
+    rng = np.random.default_rng(7)
+    a, b, c = (rng.standard_normal(n).astype(np.float32) * 3 for _ in range(3))
+    (y0, y1), stats = run_reference(ref, R.cfg1_step(n), [a, b, c], graph=graph, repeats=2)
+    check_cfg1(a, b, c, y0, y1)
+    assert stats["module_loads"] == 1 and stats["program_submissions"] == 2
+    if graph:
+        assert stats["graph_instantiations"] == 1 and stats["graph_node_updates"] >= 1
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "i64"])
+def test_random_programs_through_the_reference_runtime(ref, dtype):
+    rng = np.random.default_rng(len(dtype) * 17)
+    p, outs = random_program(rng, dtype)
+    n = 777
+    rec = R.elementwise(p, outs, n)
+    ins = [random_inputs(rng, dtype, n), random_inputs(rng, dtype, n), random_inputs(rng, dtype, 1)]
+    got, _ = run_reference(ref, rec, ins, graph=True)
+    want = oracle.elementwise(rec, ins)
+    for k, (g, w) in enumerate(zip(got, want)):
+        t = outs[k].dtype
+        if t == "f32":
+            assert same_with_nan(g, w), k
+        elif t in ("f16", "bf16"):
+            conv = f16_to_f32 if t == "f16" else bf16_to_f32
+            assert same_with_nan(conv(g), conv(w)), k
+        else:
+            assert np.array_equal(g, w), k
+
+
+def test_cfg5b_through_the_reference_runtime(ref):
+    n = (1 << 20) + 3
+    rng = np.random.default_rng(3)
+    x = rng.integers(-(2 ** 31), 2 ** 31, n, dtype=np.int64).astype(np.int32)
+    y = rng.integers(-(2 ** 31), 2 ** 31, n, dtype=np.int64).astype(np.int32)
+    (z,), _ = run_reference(ref, R.cfg5b_step(n), [x, y])
+    assert np.array_equal(z, oracle.cfg5b(x, y))
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_row_statistics_through_the_reference_runtime(ref, graph):
+    rows, cols = 300, 1000
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal(rows * cols).astype(np.float32)
+    x[::13] = 0.5
+    rec = R.cfg2_step(rows, cols)
+    got, _ = run_reference(ref, rec, [x], graph=graph)
+    want = oracle.reduce(rec, [x])
+    xx = x.reshape(rows, cols).astype(np.float64)
+    assert np.all(np.abs(got[0] - xx.sum(axis=1)) <= 2.0 ** -20 * np.abs(xx).sum(axis=1) + 1e-30)
+    for k in (1, 2, 3):
+        assert np.array_equal(got[k], want[k]), k
+
+
+def test_gather_through_the_reference_runtime(ref):
+    rng = np.random.default_rng(11)
+    dim, inner, n = 500, 32, 3000
+    table = rng.standard_normal(dim * inner).astype(np.float32)
+    idx = rng.integers(-10, dim + 10, n).astype(np.int64)
+    (out,), _ = run_reference(ref, R.gather("f32", "i64", dim, inner, n), [table, idx])
+    assert np.array_equal(out.view(np.uint32), oracle.gather(table, idx, 1, dim, inner).view(np.uint32))
+
+
+def test_view_step_through_the_reference_runtime(ref):
+    from test_lowering import view_steps
+    name, src, ins, want = view_steps()[0]  # a transposed argument plus a full one
+    recipe, args = A._recipe_of(src)
+    (got,), _ = run_reference(ref, recipe, [ins[a] for a in args], grid=4)
+    assert np.array_equal(got.reshape(want.shape), want)

@@ -7,7 +7,9 @@ one -- in stream order, or through declared dependency edges in graph mode.
 Cases mirror the reference's own plan-verifier tests (tests/cpp/pass.cpp:160-318,
 diagnostic texts included); generated plans are checked against an independent
 brute-force validity rule written here (pairwise lifetimes, transitive
-closure), not against the verifier's adjacent-slot search.
+closure), not against the verifier's adjacent-slot search.  Where the
+reference's own PASS checker is built from its sources (oracle/_ref,
+oracle/ref_build.py), every verdict and diagnostic is also compared with it.
 """
 import itertools
 import random
@@ -37,14 +39,26 @@ def allocation(p, sizes, assignments, capacities, graph=False, dependencies=None
     return a
 
 
+def _reference():
+    from oracle import ref
+    return ref if ref.load() is not None else None
+
+
+REF = _reference()
+
+
 def check(a):
-    return rt.check_allocation(a)
+    """Our verifier; equal to the reference's PASS checker, text included."""
+    ours = rt.check_allocation(a)
+    if REF is not None:
+        assert REF.pass_check(a) == ours, a
+    return ours
 
 
 # ---- the reference's explicit cases ------------------------------------------------
 def test_two_slots_for_a_four_step_chain():
     p = chain(4)
-    assert rt.check_allocation(p) == (True, "")
+    assert check(p) == (True, "")
     assert check(allocation(p, [16] * 5, [(1, 0), (2, 1), (3, 0)], [16, 16]))[0]
 
 
@@ -100,7 +114,7 @@ def test_three_lifetimes_in_one_slot_and_a_long_lived_first():
 def test_read_before_write():
     p = chain(4)
     p["steps"][0]["inputs"] = [2]
-    ok, text = rt.check_allocation(p)
+    ok, text = check(p)
     assert not ok and "READ_0_0" in text
 
 
@@ -112,7 +126,7 @@ def test_read_before_write():
     (plan(2, [0], [5], [([0], [1])]), "public output buffer index is out of range"),
 ])
 def test_structural_errors(p, message):
-    assert rt.check_allocation(p) == (False, message)
+    assert check(p) == (False, message)
 
 
 def test_graph_structure_errors():
@@ -325,3 +339,11 @@ def test_capacity_is_the_largest_occupant():
     for b, k in out["assignments"]:
         assert sizes[b] <= caps[k]
     assert sorted(caps) == [8, 300]  # slot 0 holds buffers 1 and 3, slot 1 holds 2 and 4
+
+
+def test_reference_pass_checker_was_compared():
+    """The comparisons above ran against the reference's PASS (when built)."""
+    if REF is None:
+        pytest.skip("the reference's PASS checker is not built here (oracle/_ref)")
+    ok, text = REF.pass_check(chain(4))
+    assert ok and text == ""
