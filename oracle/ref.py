@@ -33,6 +33,11 @@ def load():
             ctypes.POINTER(u), ctypes.POINTER(u), u, ctypes.POINTER(ctypes.c_size_t), ctypes.c_size_t,
             ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
             ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t]
+        lib.askref_run_program.restype = ctypes.c_int
+        lib.askref_run_program.argtypes = [
+            ctypes.c_int, ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t),
+            ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+            ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t]
         _lib = lib
     return _lib
 
@@ -76,3 +81,25 @@ def run_step(image: bytes, entry: str, types, arch: int, widths, arg_buffer, sca
     if rc != 0:
         raise RuntimeError(err.value.decode())
     return [o.raw[:int(s)] for o, s in zip(outs, output_sizes)], json.loads(stats.value.decode())
+
+
+def run_program(program: dict, images, inputs, graph: bool = False, repeats: int = 1, device: int = 0):
+    """A program of kernel steps (the JSON of ask_b200_program_prepare_kernels
+    plus a "kernels" list of {"entry", "types", "arch", "widths"}) through the
+    reference Runtime; images[k] is kernels[k]'s cubin, inputs the host data of
+    the program inputs.  Returns (outputs as bytes, session stats)."""
+    lib = load()
+    sizes = program["buffer_sizes"]
+    out_sizes = [sizes[o] for o in program["outputs"]]
+    imgs = [ctypes.create_string_buffer(bytes(i), len(i)) for i in images]
+    keep = [ctypes.create_string_buffer(bytes(x), max(len(x), 1)) for x in inputs]
+    outs = [ctypes.create_string_buffer(max(int(s), 1)) for s in out_sizes]
+    vp = lambda bufs: (ctypes.c_void_p * max(len(bufs), 1))(*[ctypes.cast(b, ctypes.c_void_p) for b in bufs])
+    stats = ctypes.create_string_buffer(1 << 14)
+    err = ctypes.create_string_buffer(1 << 12)
+    rc = lib.askref_run_program(int(device), json.dumps(program).encode(), vp(imgs),
+                                (ctypes.c_size_t * max(len(images), 1))(*[len(i) for i in images]), vp(keep), vp(outs),
+                                1 if graph else 0, int(repeats), stats, len(stats), err, len(err))
+    if rc != 0:
+        raise RuntimeError(err.value.decode())
+    return [o.raw[:int(s)] for o, s in zip(outs, out_sizes)], json.loads(stats.value.decode())

@@ -10,9 +10,13 @@
 //   - askref_run_step: Session::create, Session::load (cubin, entry, element
 //     types, arch, parameter widths), prepareProgram with one kernel PlanStep,
 //     run, copyToHost and stats (include/ask/Runtime/CUDA.h:64-175) -- the
-//     reference's own loader running an ask_b200 kernel artifact.
+//     reference's own loader running an ask_b200 kernel artifact;
+//   - askref_run_program: a whole program of kernel steps in the JSON form
+//     ask_b200_program_prepare_kernels takes, so the tests can run one
+//     program through both runtimes and compare outputs and counters.
 // Like everything under oracle/, it is a checker for the tests, never part of
 // the product path.
+#include <array>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -138,6 +142,92 @@ __attribute__((visibility("default"))) int askref_run_step(
     }
     for (size_t k = 0; k < n_out; ++k)
       if (sizes[n_in + k]) results[k]->copyToHost(host_out[k], sizes[n_in + k]);
+    std::ostringstream o;
+    o << "{";
+    bool first = true;
+    for (const auto& [name, value] : session->stats()) {
+      o << (first ? "" : ",") << "\"" << name << "\":" << value;
+      first = false;
+    }
+    o << "}";
+    write_text(o.str(), stats, stats_cap);
+    session->close();
+    return 0;
+  } catch (const std::exception& e) {
+    write_text(e.what(), err, err_cap);
+    return -1;
+  }
+}
+
+// program_json: {"buffer_sizes", "inputs", "outputs",
+//   "kernels": [{"entry", "types": [...], "arch", "widths": [...]}],
+//   "steps": [{"kernel": k, "inputs", "outputs", "grid", "block", "shared_bytes",
+//              "arguments": [{"buffer": b} | {"scalar": "<hex>"}]}]}
+// images[k] / image_bytes[k]: the cubin of kernels[k].  Runs the program
+// `repeats` times with the same host inputs uploaded to fresh buffers.
+__attribute__((visibility("default"))) int askref_run_program(int device, const char* program_json,
+                                                              const void* const* images, const size_t* image_bytes,
+                                                              const void* const* host_in, void* const* host_out,
+                                                              int graph, int repeats, char* stats, size_t stats_cap,
+                                                              char* err, size_t err_cap) {
+  try {
+    using namespace ask::runtime;
+    const askb::json::Value v = askb::json::Parser(program_json).parse();
+    auto session = Session::create(device);
+    std::vector<std::shared_ptr<Kernel>> kernels;
+    const auto& ks = v.at("kernels").as_array("kernels");
+    for (size_t k = 0; k < ks.size(); ++k) {
+      std::vector<std::string> types;
+      for (const auto& t : ks[k].at("types").as_array("types")) types.push_back(t.as_str("type"));
+      std::vector<unsigned> widths;
+      for (const auto& w : ks[k].at("widths").as_array("widths")) widths.push_back(unsigned(w.as_int("width")));
+      kernels.push_back(session->load(std::string(static_cast<const char*>(images[k]), image_bytes[k]),
+                                      ks[k].at("entry").as_str("entry"), types, int(ks[k].at("arch").as_int("arch")),
+                                      widths));
+    }
+    auto triple = [](const askb::json::Value& a) {
+      const auto& x = a.as_array("dims");
+      return std::array<unsigned, 3>{unsigned(x.at(0).as_int("d")), unsigned(x.at(1).as_int("d")),
+                                     unsigned(x.at(2).as_int("d"))};
+    };
+    std::vector<PlanStep> steps;
+    for (const auto& sv : v.at("steps").as_array("steps")) {
+      PlanStep st;
+      st.kernel = kernels.at(size_t(sv.at("kernel").as_int("kernel")));
+      st.inputs = list(sv.at("inputs"), "inputs");
+      st.outputs = list(sv.at("outputs"), "outputs");
+      st.grid = triple(sv.at("grid"));
+      st.block = triple(sv.at("block"));
+      st.sharedBytes = sv.get("shared_bytes") ? unsigned(sv.at("shared_bytes").as_int("shared_bytes")) : 0;
+      for (const auto& a : sv.at("arguments").as_array("arguments")) {
+        PlanArgument pa;
+        if (const auto* sc = a.get("scalar")) {
+          const std::string hex = sc->as_str("scalar");
+          for (size_t i = 0; i + 1 < hex.size(); i += 2) pa.scalar.push_back(char(std::stoi(hex.substr(i, 2), nullptr, 16)));
+        } else {
+          pa.buffer = a.at("buffer").as_int("buffer");
+        }
+        st.arguments.push_back(pa);
+      }
+      steps.push_back(st);
+    }
+    const std::vector<size_t> sizes = list(v.at("buffer_sizes"), "buffer_sizes");
+    const std::vector<size_t> ins = list(v.at("inputs"), "inputs"), outs = list(v.at("outputs"), "outputs");
+    auto program = session->prepareProgram(sizes, ins, outs, steps, graph != 0);
+    std::vector<std::shared_ptr<DeviceBuffer>> results;
+    for (int r = 0; r < (repeats > 0 ? repeats : 1); ++r) {
+      std::vector<std::shared_ptr<DeviceBuffer>> bufs;
+      for (size_t k = 0; k < ins.size(); ++k) {
+        auto b = session->allocate(sizes[ins[k]]);
+        if (sizes[ins[k]]) b->copyFromHost(host_in[k], sizes[ins[k]]);
+        bufs.push_back(b);
+      }
+      auto out = program->run(bufs);
+      out.second->wait();
+      results = out.first;
+    }
+    for (size_t k = 0; k < outs.size(); ++k)
+      if (sizes[outs[k]]) results[k]->copyToHost(host_out[k], sizes[outs[k]]);
     std::ostringstream o;
     o << "{";
     bool first = true;

@@ -130,3 +130,65 @@ def test_view_step_through_the_reference_runtime(ref):
     recipe, args = A._recipe_of(src)
     (got,), _ = run_reference(ref, recipe, [ins[a] for a in args], grid=4)
     assert np.array_equal(got.reshape(want.shape), want)
+
+
+# ---- one program through both runtimes -----------------------------------------------
+def _affine_i32(n, mul, add):
+    p = R.Program()
+    x = p.input("i32")
+    return R.elementwise(p, [p.add(p.mul(x, p.const("i32", mul)), p.const("i32", add))], n)
+
+
+def _add_i32(n):
+    p = R.Program()
+    a, b = p.input("i32"), p.input("i32")
+    return R.elementwise(p, [p.add(a, b)], n)
+
+
+def _programs(n):
+    """(name, buffer count, inputs, outputs, steps as (kernel, ins, outs)) with internal buffers."""
+    chain = [("affine", [i], [i + 1]) for i in range(6)]
+    dag = [("affine", [0], [1]), ("affine", [0], [2]), ("add", [1, 2], [3]), ("affine", [3], [4]),
+           ("add", [4, 1], [5]), ("affine", [5], [6])]
+    return [("chain", 7, [0], [6], chain), ("fork_join", 7, [0], [6, 2], dag)]
+
+
+@pytest.mark.parametrize("graph", [False, True])
+@pytest.mark.parametrize("which", [0, 1])
+def test_programs_match_the_reference_runtime(ref, graph, which):
+    """The same kernel-step program through this library's runtime and the
+    reference's: identical outputs and identical slot and graph counters."""
+    from ask_b200 import runtime as rt
+    n = 1 << 16
+    name, nbuf, ins, outs, steps = _programs(n)[which]
+    arts = {}
+    for key, rec in (("affine", _affine_i32(n, 3, 1)), ("add", _add_i32(n))):
+        req = A.request_for(rec, entry=f"k_{key}", grid=(148, 1, 1))
+        arts[key] = (A.build_artifact(req), A.port_types(req))
+    session = rt.Session.create(0)
+    kernels = {k: A.load_artifact(session, a) for k, (a, _) in arts.items()}
+    plan_steps = [A.artifact_step(arts[k][0], kernels[k], i, o, arts[k][1]) for k, i, o in steps]
+    sizes = [4 * n] * nbuf
+    prog = session.prepareProgram(sizes, ins, outs, plan_steps, graph=graph)
+    x = np.random.default_rng(which).integers(-1000, 1000, n).astype(np.int32)
+    xb = session.allocate(4 * n)
+    xb.copyFromHost(x.tobytes())
+    for _ in range(2):
+        got, ev = prog.run([xb])
+        ev.wait()
+    ours = [np.frombuffer(b.copyToHost(), dtype=np.int32) for b in got]
+    mine = session.stats()
+
+    order = list(arts)
+    program = {"buffer_sizes": sizes, "inputs": ins, "outputs": outs,
+               "kernels": [{"entry": arts[k][0]["entry"], "types": ["i32"], "arch": 100,
+                            "widths": A.parameter_widths(arts[k][0])} for k in order],
+               "steps": [s.to_json(order.index(k)) for s, (k, _, _) in zip(plan_steps, steps)]}
+    images = [base64.b64decode(arts[k][0]["payload"]) for k in order]
+    theirs_raw, theirs = ref.run_program(program, images, [x.tobytes()], graph=graph, repeats=2)
+    for a, b in zip(ours, theirs_raw):
+        assert np.array_equal(a, np.frombuffer(b, dtype=np.int32))
+    for key in ("prepared_internal_slots", "prepared_internal_bytes", "graph_nodes", "graph_edges",
+                "graph_instantiations"):
+        assert mine.get(key, 0) == theirs.get(key, 0), (name, graph, key, mine.get(key), theirs.get(key))
+    session.close()
