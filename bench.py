@@ -311,7 +311,9 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
             distinct = int(torch.unique(idx).numel())
             w.kernels = [("gather_rows", 8 * n + 4 * n * dim + 4 * dim * distinct,
                           p.bind([table, idx], [out], None, st))]
-            w.config = dict(static_config(name, world), distinct_rows=distinct)
+            w.config = dict(static_config(name, world), distinct_rows=distinct,
+                            graded_bytes="compulsory 8N + 4ND + 4D*distinct",
+                            logical_bytes=8 * n + 8 * n * dim)
             w.e2e = {"inputs": [table, idx], "results": [out]}
         else:
             grad = gen(1, SEED["cfg4"], 2, n * dim, 0.0, 1.0, torch.float32)
