@@ -735,6 +735,24 @@ std::string describe(const ask_b200_plan& pl) {
   };
   for (size_t k = 0; k < pl.inputs.size(); ++k) port(pl.inputs[k], "input", k);
   for (size_t k = 0; k < pl.outputs.size(); ++k) port(pl.outputs[k], "output", k);
+  // The reference artifact's invocation v2 and required element types
+  // (lib/Lowering/CUDA.cpp:392-407): arguments are the ports in port order.
+  const int block = pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? kRedThreads
+                    : pl.family == FAM_SOFTMAX ? pl.block : 256;
+  o << "],\"invocation\":{\"version\":2,\"kind\":\"ask-b200-recipe\",\"grid\":[" << pl.grid
+    << ",1,1],\"block\":[" << block << ",1,1],\"shared_bytes\":0,\"arguments\":[";
+  for (size_t k = 0; k < pl.inputs.size() + pl.outputs.size(); ++k)
+    o << (k ? "," : "") << "\"" << (k < pl.inputs.size() ? "input:" : "output:")
+      << (k < pl.inputs.size() ? k : k - pl.inputs.size()) << "\"";
+  o << "]},\"required_element_types\":[";
+  bool used[kNumDTypes] = {}, first = true;
+  for (const PortInfo& p : pl.inputs) used[p.dtype] = true;
+  for (const PortInfo& p : pl.outputs) used[p.dtype] = true;
+  for (int t : {kBool, kI32, kI64, kF32, kF16, kBF16})
+    if (used[t]) {
+      o << (first ? "" : ",") << "\"" << kTypeNames[t] << "\"";
+      first = false;
+    }
   o << "],\"requires_disjoint_outputs\":true,\"outputs_must_not_alias_inputs\":"
     << (pl.family == FAM_SCATTER ? "false" : "true") << "}";
   return o.str();

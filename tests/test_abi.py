@@ -92,6 +92,11 @@ def test_port_map_orders_inputs_then_outputs():
     assert [p["argument"] for p in ports] == list(range(5))
     assert all(p["elements"] == 1000 and p["element_type"] == "f32" for p in ports)
     assert d["requires_disjoint_outputs"] is True
+    inv = d["invocation"]
+    assert inv["version"] == 2 and inv["grid"] == d["launch"]["grid"] and inv["block"] == d["launch"]["block"]
+    assert inv["arguments"] == [p["logical_port"] for p in d["port_map"]]
+    assert d["required_element_types"] == sorted({p["element_type"] for p in d["port_map"]},
+                                                 key=["bool", "i32", "i64", "f32", "f16", "bf16"].index)
 
 
 def test_reduce_outputs_and_scratch():
