@@ -67,6 +67,28 @@ __device__ __forceinline__ float max_nan(float a, float b) {
   return r;
 }
 
+// The same on two packed f16/bf16 values at once (NaN-propagating max), and
+// the plain packed minimum; widening to f32 is exact and monotone, so the
+// max/min of the widened values equals the widened max/min.
+template <int T>
+__device__ __forceinline__ uint32_t max2_nan(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (T == kF16)
+    asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <int T>
+__device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (T == kF16)
+    asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else
+    asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 constexpr int kMaxWarps = 16;
 #ifndef ASKB_SOFTMAX_THREADS
 #define ASKB_SOFTMAX_THREADS 128
@@ -88,6 +110,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32) softmax_rows_kernel(const uint
   }
   for (int parity = 0; row < rows; row += gridDim.x, parity ^= 1) {
     float e[VPT * 8];
+    // m = max over the row (NaN-propagating); the thread's smallest value
+    // bounds its exp results from below for the division's check.  Both fold
+    // on the packed 16-bit values, two elements an instruction.
+    uint32_t pmax = v[0].x, pmin = v[0].x;
 #pragma unroll
     for (int q = 0; q < VPT; ++q) {
       const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
@@ -95,6 +121,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) softmax_rows_kernel(const uint
       for (int j = 0; j < 4; ++j) {
         e[q * 8 + 2 * j] = widen_lo<T>(w[j]);
         e[q * 8 + 2 * j + 1] = widen_hi<T>(w[j]);
+        pmax = max2_nan<T>(pmax, w[j]);
+        pmin = min2<T>(pmin, w[j]);
       }
     }
     const uint64_t next = row + gridDim.x;
@@ -102,14 +130,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) softmax_rows_kernel(const uint
 #pragma unroll
       for (int q = 0; q < VPT; ++q) v[q] = ld_stream_v4(x + next * vecs + q * blockDim.x + threadIdx.x);
     }
-    // m = max over the row (NaN-propagating); the thread's smallest value
-    // bounds its exp results from below for the division's check
-    float mx = e[0], mn = e[0];
-#pragma unroll
-    for (int k = 1; k < VPT * 8; ++k) {
-      mx = max_nan(mx, e[k]);
-      mn = fminf(mn, e[k]);
-    }
+    // max.NaN.f32 of the two halves also turns a NaN into the canonical f32 NaN
+    float mx = max_nan(widen_lo<T>(pmax), widen_hi<T>(pmax));
+    const float mn = fminf(widen_lo<T>(pmin), widen_hi<T>(pmin));
 #pragma unroll
     for (int d = 16; d; d >>= 1) mx = max_nan(mx, __shfl_xor_sync(0xffffffffu, mx, d));
     if (lane == 0) red_max[parity][warp] = mx;

@@ -214,6 +214,11 @@ def test_fused_softmax_against_oracle(device, dtype, rows, cols):
         xh[2 * cols:3 * cols] = ninf16
         xh[3 * cols:4 * cols] = 0x8000
         xh[4 * cols] = big
+    if rows > 6:  # maxima -0 and +0 in either order: m is +0 (llvm.maximum orders -0 below +0)
+        neg_one = 0xBC00 if dtype == "f16" else 0xBF80
+        xh[5 * cols:7 * cols] = neg_one
+        xh[5 * cols + 3], xh[5 * cols + 9] = 0x8000, 0x0000
+        xh[6 * cols + 3], xh[6 * cols + 9] = 0x0000, 0x8000
     x = torch.from_numpy(xh.view(np.int16)).cuda()
     plan = ask_b200.Plan({"family": "softmax", "dtype": dtype, "rows": rows, "cols": cols}, 0)
     assert plan.describe()["kernel"] == f"softmax_rows_{dtype}"
