@@ -288,6 +288,7 @@ Generated generate(const ask_b200_plan& pl, const std::string& entry, const uint
     case FAM_REDUCE: {
       const RedArgs& a = pl.red;
       if (pl.ssa.n_in == 0) fail(ASK_B200_E_UNSUPPORTED, "an artifact reduction reads at least one input port");
+      if (pl.views) fail(ASK_B200_E_UNSUPPORTED, "an artifact reduction reads full, outer or scalar ports, not views");
       decls = program_struct(pl.ssa, "Program") + reductions_struct(a);
       pointer_arrays();
       const uint64_t warps = grid[0] * 256 / 32;

@@ -136,6 +136,11 @@ struct ViewSet {
 cudaError_t ew_view_launch(const Program& prog, const EwArgs& args, const ViewSet& views, int grid,
                            cudaStream_t stream);
 int ew_view_occupancy();
+// Reductions whose prologue reads IM_VIEW ports or coordinates: a warp per
+// output over the [outer, extent, inner] domain of the iteration shape.
+cudaError_t red_view_launch(const Program& prog, const RedArgs& a, const ViewSet& views, int grid,
+                            cudaStream_t stream);
+int red_view_occupancy();
 
 // Family S: the three-step softmax plan fused (softmax_kernels.cu).  x and y
 // are [rows, cols] f16/bf16 (16-byte aligned), m and s are [rows] f32.

@@ -22,7 +22,9 @@
 // general broadcasts and reshapes of an argument -- a strided, windowed view
 // (IM_VIEW; pad's elements outside the window read its constant pad value).
 // concatenate becomes views of its operands selected by the coordinate along
-// its axis, iota a cast of that coordinate.  ask.constant/ask.splat become
+// its axis, iota a cast of that coordinate -- in elementwise steps and in the
+// prologues of reductions alike (a reduction's iteration shape is its
+// operand's shape).  ask.constant/ask.splat become
 // constants (MLIR prints each float literal so that it re-parses exactly, or
 // as its bit pattern in hex; either is carried over without double rounding).
 // An index map of a computed value (the reference re-evaluates the value at
@@ -701,10 +703,7 @@ class Lowering {
            ",\"lo\":" + list(w.lo) + ",\"step\":" + list(w.step) + ",\"extent\":" + list(w.extent) +
            ",\"stride\":" + list(w.stride) + ",\"pad\":" + w.pad + "}";
   }
-  int use_view(const ArgView& w) {
-    if (is_reduce_) unsupported("reductions read no strided or windowed views");
-    return use_port(w.arg, "view", view_json(w));
-  }
+  int use_view(const ArgView& w) { return use_port(w.arg, "view", view_json(w)); }
 
   // Index map of an argument broadcast to the output shape (the fast maps).
   bool simple_broadcast(const Type& from, const std::vector<int64_t>& dims, std::string* map) {
@@ -728,7 +727,6 @@ class Lowering {
   }
   int coord(int64_t axis) {
     uses_shape_ = true;
-    if (is_reduce_) unsupported("iota and concatenate inside a reduction");
     return emit("[\"coord\"," + std::to_string(axis) + "]", "i64");
   }
   int value(const std::string& v) {
@@ -969,11 +967,14 @@ class Lowering {
     }
     reductions += "]";
     for (const Port& pt : ports_)
-      if (pt.map == "inner" || pt.map == "view") unsupported("reductions read no per-column or strided operands");
+      if (pt.map == "inner") unsupported("reductions read no per-column operands");
+    if (uses_shape_ && (out_shape_.empty() || out_shape_.size() > 6))
+      unsupported("views and coordinates need an iteration shape of 1..6 axes");
     const std::vector<size_t> order = port_order();
     std::ostringstream o;
-    o << "{\"family\":\"reduce\",\"outer\":" << outer << ",\"extent\":" << extent << ",\"inner\":" << inner
-      << ",\"inputs\":" << inputs_json(order) << ",\"program\":" << program_json(order) << ",\"results\":[";
+    o << "{\"family\":\"reduce\",\"outer\":" << outer << ",\"extent\":" << extent << ",\"inner\":" << inner;
+    if (uses_shape_) o << ",\"shape\":" << shape_json();
+    o << ",\"inputs\":" << inputs_json(order) << ",\"program\":" << program_json(order) << ",\"results\":[";
     for (size_t k = 0; k < results.size(); ++k) o << (k ? "," : "") << results[k];
     o << "],\"reductions\":" << reductions << "}";
     return {o.str(), port_args(order)};

@@ -570,10 +570,34 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   parse_ports(r, "inputs", true, ports.type, ports.map);
   pl.prog = canonical(parse_program(r.at("program"), r.at("results"), ports, false));
   pl.ssa = pl.prog;
-  for (int m : ports.map)
-    if (m == IM_VIEW) fail(ASK_B200_E_UNSUPPORTED, "reduction prologues read full, outer or scalar ports, not views");
+  // Views (IM_VIEW ports) and coordinates are defined over the step's
+  // iteration shape: the reduced operand's shape, whose axes flatten to
+  // [outer, extent, inner].
+  bool coords = false;
+  for (int i = 0; i < pl.prog.n_insn; ++i) coords = coords || pl.prog.insn[i].op == OP_COORD;
+  bool any_view = coords;
+  for (int m : ports.map) {
+    any_view = any_view || m == IM_VIEW;
+    if (m == IM_INNER) fail(ASK_B200_E_UNSUPPORTED, "reduction prologues read full, outer, scalar or view ports");
+  }
+  pl.vs = ViewSet{};
+  pl.vs.rank = 1;
+  pl.vs.shape[0] = mul_checked(mul_checked(outer, extent), inner);
+  if (const json::Value* shape = r.get("shape")) {
+    const auto& sa = shape->as_array("shape");
+    if (sa.empty() || sa.size() > size_t(kMaxRank)) fail(ASK_B200_E_UNSUPPORTED, "iteration shape must have 1..6 axes");
+    pl.vs.rank = int(sa.size());
+    uint64_t count = 1;
+    for (int d = 0; d < pl.vs.rank; ++d) count = mul_checked(count, pl.vs.shape[d] = checked_count(sa[size_t(d)], "shape"));
+    if (count != mul_checked(mul_checked(outer, extent), inner))
+      fail(ASK_B200_E_INVALID, "the iteration shape's element count differs from outer * extent * inner");
+  } else if (any_view) {
+    fail(ASK_B200_E_INVALID, "a view port or coord needs the step's iteration \"shape\"");
+  }
   for (int i = 0; i < pl.prog.n_insn; ++i)
-    if (pl.prog.insn[i].op == OP_COORD) fail(ASK_B200_E_UNSUPPORTED, "coord is an elementwise-step instruction");
+    if (pl.prog.insn[i].op == OP_COORD && int(pl.prog.insn[i].aux) >= pl.vs.rank)
+      fail(ASK_B200_E_INVALID, "coord axis beyond the iteration shape");
+  pl.views = any_view;
   const auto& reds = r.at("reductions").as_array("reductions");
   if (reds.empty() || reds.size() > size_t(kMaxReductions))
     fail(ASK_B200_E_UNSUPPORTED, "1.." + std::to_string(kMaxReductions) + " reductions per step");
@@ -583,8 +607,10 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   a.n_red = uint8_t(reds.size());
   const uint64_t n_outputs = mul_checked(outer, inner);
   const uint64_t n_elems = mul_checked(n_outputs, extent);
+  const auto& in_json = r.at("inputs").as_array("inputs");
   for (size_t k = 0; k < ports.type.size(); ++k) {
-    const uint64_t elems = ports.map[k] == IM_FULL ? n_elems : ports.map[k] == IM_SCALAR ? 1 : n_outputs;
+    uint64_t elems = ports.map[k] == IM_FULL ? n_elems : ports.map[k] == IM_SCALAR ? 1 : n_outputs;
+    if (ports.map[k] == IM_VIEW) pl.vs.port[k] = parse_view(in_json[k].at("view"), pl.vs.rank, ports.type[k], &elems);
     pl.inputs.push_back({ports.type[k], elems, ports.map[k]});
   }
   for (size_t k = 0; k < reds.size(); ++k) {
@@ -609,6 +635,17 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
     for (size_t k = 0; k < arr.size(); ++k)
       if (parse_dtype(arr[k].at("dtype").as_str("dtype")) != pl.outputs[k].dtype)
         fail(ASK_B200_E_INVALID, "output " + std::to_string(k) + " type does not match its reduction");
+  }
+  if (pl.views) {  // the view path: a warp per output, no specialisation, no scratch
+    assign_registers(pl.prog);
+    pl.kernel = "reduce_view";
+    pl.strategy = RS_WARP_ROW;
+    const int occ = std::min(pl.device >= 0 ? red_view_occupancy() : 8, pl.blocks_per_sm ? pl.blocks_per_sm : 64);
+    const uint64_t needed = (n_outputs + (kRedThreads / 32) - 1) / (kRedThreads / 32);
+    pl.grid = int(std::max<uint64_t>(1, std::min(needed, uint64_t(std::max(occ, 1)) * uint64_t(pl.num_sms))));
+    pl.launches = n_outputs ? 1 : 0;
+    pl.scratch = 0;
+    return;
   }
   // Strategy.
   std::string forced = r.get("strategy") ? r.at("strategy").as_str("strategy") : "";
@@ -718,7 +755,7 @@ std::string describe(const ask_b200_plan& pl) {
     << ",1,1],\"shared_bytes\":0},\"kernels_per_launch\":" << pl.launches << ",\"scratch_bytes\":" << pl.scratch;
   if (pl.family == FAM_REDUCE) {
     const char* strat[] = {"warp_row", "column", "split"};
-    o << ",\"strategy\":\"" << strat[pl.strategy] << "\",\"shardable\":" << (pl.shardable ? "true" : "false")
+    o << ",\"strategy\":\"" << (pl.views ? "view" : strat[pl.strategy]) << "\",\"shardable\":" << (pl.shardable ? "true" : "false")
       << ",\"outer\":" << pl.red.outer << ",\"extent\":" << pl.red.extent << ",\"inner\":" << pl.red.inner
       << ",\"index_base\":" << pl.red.index_base;
   }
@@ -811,6 +848,13 @@ void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratc
       break;
     }
     case FAM_REDUCE: {
+      if (pl.views) {
+        RedArgs a = pl.red;
+        for (size_t k = 0; k < ni; ++k) a.in[k] = reinterpret_cast<const void*>(ports[k]);
+        for (size_t k = 0; k < pl.outputs.size(); ++k) a.out[k] = reinterpret_cast<void*>(ports[ni + k]);
+        check_cuda(red_view_launch(pl.prog, a, pl.vs, pl.grid, st), "reduce launch");
+        break;
+      }
       RedArgs a = pl.red;
       bool aligned = true;
       for (size_t k = 0; k < ni; ++k) {

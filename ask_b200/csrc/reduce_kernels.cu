@@ -208,6 +208,73 @@ __global__ void __launch_bounds__(kRedThreads)
   }
 }
 
+// General index maps (RS_VIEW): a warp per output (o, n); lanes stride the
+// reduced extent.  Each element's coordinates in the step's iteration shape
+// are computed once; IM_VIEW ports map them through their view (transpose,
+// slice, pad, general broadcast of an argument) and OP_COORD reads them, as in
+// the elementwise view loop.  Scalar loads: this path serves coverage, the
+// benchmark reductions read full, outer or scalar ports.
+__global__ void __launch_bounds__(kRedThreads)
+    red_view_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a,
+                     const __grid_constant__ ViewSet views) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t warp = (uint64_t(blockIdx.x) * kRedThreads + threadIdx.x) >> 5;
+  const uint64_t nwarps = (uint64_t(gridDim.x) * kRedThreads) >> 5;
+  const uint64_t n_outputs = a.outer * a.inner;
+  uint64_t r[kMaxRegs];
+  for (uint64_t o_idx = warp; o_idx < n_outputs; o_idx += nwarps) {
+    const uint64_t o = o_idx / a.inner, n = o_idx % a.inner;
+    Accs s;
+    accs_init(a, s);
+    for (uint64_t e = lane; e < a.extent; e += 32) {
+      const uint64_t i = (o * a.extent + e) * a.inner + n;
+      int64_t c[kMaxRank];
+      uint64_t rest = i;
+      for (int d = views.rank - 1; d >= 0; --d) {
+        const uint64_t ext = views.shape[d];
+        c[d] = int64_t(rest % ext);
+        rest /= ext;
+      }
+      for (int k = 0; k < prog.n_insn; ++k) {
+        const Insn& ins = prog.insn[k];
+        if (ins.op == OP_INPUT) {
+          const int port = ins.a, t = prog.in_type[port];
+          const void* p = a.in[port];
+          switch (prog.in_map[port]) {
+            case IM_SCALAR: r[ins.dst] = word_from_storage(t, p, 0); break;
+            case IM_OUTER: r[ins.dst] = word_from_storage(t, p, o_idx); break;
+            case IM_VIEW: {
+              const PortView& v = views.port[port];
+              int64_t off = v.offset;
+              bool ok = true;
+              for (int d = 0; d < views.rank; ++d) {
+                const int64_t q0 = c[d] - v.lo[d];
+                const int64_t q = q0 / v.step[d];
+                ok = ok && q0 >= 0 && q * v.step[d] == q0 && q < v.extent[d];
+                off += q * v.stride[d];
+              }
+              r[ins.dst] = ok ? word_from_storage(t, p, uint64_t(off)) : v.pad;
+              break;
+            }
+            default: r[ins.dst] = word_from_storage(t, p, i); break;
+          }
+        } else if (ins.op == OP_COORD) {
+          r[ins.dst] = uint64_t(c[ins.aux]);
+        } else {
+          r[ins.dst] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a], r[ins.b], r[ins.c]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kMaxReductions; ++k)
+        if (k < a.n_red)
+          acc_fold<false>(a.red_op[k], a.red_type[k], s.v[k], s.i[k], r[prog.out_reg[a.red_src[k]]],
+                          int64_t(a.index_base + e));
+    }
+    accs_warp_reduce(a, s);
+    if (lane == 0) write_outputs(a, s, o_idx);
+  }
+}
+
 // Chunk of the extent owned by CTA c of G, aligned to whole units of V*U*blockDim.
 __device__ __forceinline__ void split_chunk(uint64_t extent, uint32_t c, uint32_t g, uint64_t granule, uint64_t& e0,
                                             uint64_t& e1) {
@@ -395,6 +462,18 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
   if (e != cudaSuccess) return e;
   red_combine_kernel<<<unsigned(a.outer), kRedThreads, 0, st>>>(a, part, grid, rec_out);
   return cudaGetLastError();
+}
+
+cudaError_t red_view_launch(const Program& prog, const RedArgs& a, const ViewSet& views, int grid, cudaStream_t st) {
+  if (a.outer == 0 || a.inner == 0) return cudaSuccess;
+  red_view_generic<<<grid, kRedThreads, 0, st>>>(prog, a, views);
+  return cudaGetLastError();
+}
+
+int red_view_occupancy() {
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, red_view_generic, kRedThreads, 0) != cudaSuccess) return 1;
+  return blocks > 0 ? blocks : 1;
 }
 
 cudaError_t red_combine_records(const RedArgs& a, const RedPartial* records, int n, cudaStream_t st) {

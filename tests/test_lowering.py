@@ -252,6 +252,71 @@ def test_index_maps_lower_to_views(case):
     assert len(out["input_arguments"]) == len(r["inputs"])
 
 
+def reduce_view_steps():
+    """(name, step source, input arrays, expected outputs) of reductions whose
+    operand reads arguments through index maps."""
+    rng = np.random.default_rng(9)
+    cases = []
+    # sum and argmax along axis 1 of a transposed argument: a column reduction of x
+    s = Step()
+    x = s.arg([6, 40], "i32")
+    t = s.op("transpose", [x], [40, 6], "i32", "permutation = " + arr([1, 0]))
+    outs = [s.op("reduce_sum", [t], [40], "i32", "axes = array<i64: 1>"), s.op("argmax", [t], [40], "i64", "axis = 1 : i64")]
+    xv = rng.integers(-50, 50, (6, 40)).astype(np.int32)
+    cases.append(("transpose_rows", s.text(outs), [xv], [xv.T.sum(axis=1).astype(np.int32), np.argmax(xv.T, axis=1)]))
+    # max and min over axis 0 (inner > 1) of a strided slice
+    s = Step()
+    x = s.arg([9, 12], "f32")
+    sl = s.op("slice", [x], [4, 6], "f32", f"starts = {arr([1, 0])}, stops = {arr([9, 12])}, steps = {arr([2, 2])}")
+    outs = [s.op("reduce_max", [sl], [6], "f32", "axes = array<i64: 0>"), s.op("reduce_min", [sl], [6], "f32", "axes = array<i64: 0>")]
+    xv = rng.standard_normal((9, 12)).astype(np.float32)
+    sv = xv[1:9:2, 0:12:2]
+    cases.append(("slice_columns", s.text(outs), [xv], [sv.max(axis=0), sv.min(axis=0)]))
+    # weighted row sum with iota: sum_j j * x[i, j] (coordinates inside a reduction prologue)
+    s = Step()
+    x = s.arg([5, 33], "i64")
+    io = s.op("iota", [], [5, 33], "i64", "dimension = 1 : i64")
+    prod = s.op("mul", [io, x], [5, 33], "i64")
+    outs = [s.op("reduce_sum", [prod], [5], "i64", "axes = array<i64: 1>")]
+    xv = rng.integers(-1000, 1000, (5, 33)).astype(np.int64)
+    cases.append(("iota_weights", s.text(outs), [xv], [(xv * np.arange(33)[None, :]).sum(axis=1)]))
+    # a general broadcast of a middle-axis vector added before a reduction over the last two axes
+    s = Step()
+    x = s.arg([3, 4, 7], "i32")
+    v = s.arg([4], "i32")
+    bc = s.op("broadcast_in_dim", [v], [3, 4, 7], "i32", f"dimensions = {arr([1])}, shape = {arr([3, 4, 7])}")
+    outs = [s.op("reduce_sum", [s.op("add", [x, bc], [3, 4, 7], "i32")], [3], "i32", "axes = array<i64: 1, 2>")]
+    xv = rng.integers(-20, 20, (3, 4, 7)).astype(np.int32)
+    vv = rng.integers(-20, 20, 4).astype(np.int32)
+    cases.append(("broadcast_middle", s.text(outs), [xv, vv], [(xv + vv[None, :, None]).sum(axis=(1, 2)).astype(np.int32)]))
+    return cases
+
+
+@pytest.mark.parametrize("case", reduce_view_steps(), ids=lambda c: c[0])
+def test_reductions_over_index_maps_lower_to_the_view_kernel(case):
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    r = out["recipe"]
+    assert r["family"] == "reduce" and "shape" in r
+    d = ask_b200.Plan(r, -1).describe()
+    assert d["kernel"] == "reduce_view" and d["strategy"] == "view"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", reduce_view_steps(), ids=lambda c: c[0])
+def test_reductions_over_index_maps_on_gpu(device, case):
+    import torch
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    plan = ask_b200.Plan(out["recipe"], 0)
+    dev_in = [torch.from_numpy(np.ascontiguousarray(ins[a])).cuda() for a in out["input_arguments"]]
+    dev_out = [torch.empty(w.size, dtype=torch.from_numpy(np.ascontiguousarray(w)).dtype, device="cuda") for w in want]
+    plan.launch(dev_in, dev_out, None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    for got, w in zip(dev_out, want):
+        assert np.array_equal(got.cpu().numpy(), np.asarray(w).reshape(-1)), name
+
+
 def test_index_map_of_a_computed_value_is_unsupported():
     s = Step()
     x = s.arg([4, 8], "f32")
