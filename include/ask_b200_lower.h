@@ -11,7 +11,8 @@
  * be read through broadcast_in_dim, transpose, slice, pad, reshape and
  * concatenate (as strided, windowed views of the argument) and iota;
  * reductions (sum, prod, max, min, any, all, argmax, argmin) over one
- * contiguous block of axes; gather and scatter_add.  Steps outside it fail
+ * contiguous block of axes, their operands built the same way; gather and
+ * scatter_add.  Steps outside it fail
  * with ASK_B200_E_UNSUPPORTED and a message naming the op (an index map of a
  * computed value rather than of an argument, matmul and external steps).
  */
