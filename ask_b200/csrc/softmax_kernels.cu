@@ -1,7 +1,7 @@
 // Family S: the reference's three-step softmax plan fused into one pass.
 //
 // ASK partitions a row softmax into three owned steps (lib/Frontend/
-// Partition.cpp:100-148; SURVEY's canonical recompute form):
+// Partition.cpp:100-148; the recompute form, in which each step casts x itself):
 //   step 0  m = reduce_max(cast(x, f32))                     over each row
 //   step 1  s = reduce_sum(exp(cast(x) + m*(-1)))            over each row
 //   step 2  y = cast(exp(cast(x) + m*(-1)) / s, T)

@@ -281,3 +281,37 @@ def test_bound_submissions_reuse_completion_events(device, graph):
     assert st["program_submissions"] == 250
     assert st["event_reuses"] > 0 and st["event_creations"] + st["event_reuses"] == 250
     s.close()
+
+
+def test_concurrent_submissions_from_threads(device):
+    """Sessions serialise every call (the reference's recursive session mutex):
+    four threads submitting to one session each get their own results."""
+    import threading
+    s = rt.Session.create(0)
+    n = 1 << 14
+    prog = s.prepareProgram([4 * n, 4 * n, 4 * n], [0], [2],
+                            [rt.PlanStep(double_i32(n), [0], [1]), rt.PlanStep(double_i32(n), [1], [2])], graph=True)
+    errors = []
+
+    def worker(t):
+        try:
+            x = s.allocate(4 * n)
+            base = np.arange(n, dtype=np.int32) + 1000 * t
+            x.copyFromHost(base.tobytes())
+            for _ in range(30):
+                outs, ev = prog.run([x])
+                ev.wait()
+                if not np.array_equal(i32s(outs[0]), 4 * base):
+                    errors.append(t)
+                    return
+        except Exception as e:  # surfaced below
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=worker, args=(t,)) for t in range(4)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors
+    assert s.stats()["program_submissions"] == 120
+    s.close()
