@@ -27,8 +27,9 @@
 // operand's shape).  ask.constant/ask.splat become
 // constants (MLIR prints each float literal so that it re-parses exactly, or
 // as its bit pattern in hex; either is carried over without double rounding).
-// An index map of a computed value (the reference re-evaluates the value at
-// the mapped index) and matmul or external steps are reported as unsupported.
+// An index map of a computed elementwise value moves onto that value's
+// operands (push_index_maps); pad of a computed value and matmul or external
+// steps are reported as unsupported.
 #include <algorithm>
 #include <cctype>
 #include <cstdio>
@@ -479,6 +480,7 @@ class Lowering {
   explicit Lowering(const Func& f) : f_(f) {
     for (size_t k = 0; k < f.args.size(); ++k) arg_[f.args[k]] = k;
     for (size_t k = 0; k < f.ops.size(); ++k) def_[f.ops[k].result] = k;
+    push_index_maps();
   }
 
   Lowered run() {
@@ -505,7 +507,7 @@ class Lowering {
     std::string map;   // full, scalar, outer, inner, view
     std::string view;  // the view's JSON for map == view
   };
-  const Func& f_;
+  Func f_;  // the step, with index maps of computed values moved onto their operands
   std::map<std::string, size_t> arg_, def_;
   // op program under construction; insn_port_[i] >= 0 marks an input instruction
   std::vector<std::string> insns_;
@@ -532,6 +534,64 @@ class Lowering {
     const Op* p = producer(v);
     if (!p) invalid("value " + v + " is not defined");
     return p->type;
+  }
+  // An index map (transpose, broadcast_in_dim, slice, reshape) of a computed
+  // elementwise value reads that value at mapped coordinates, which the
+  // reference evaluates by re-evaluating the value at the mapped index
+  // (ScalarEmitter.h:626-774).  Elementwise ops commute with index maps, so
+  // the map moves onto the operands -- transpose(exp(x)) = exp(transpose(x)) --
+  // until it reaches step arguments (views), splats or other maps (composed by
+  // view_of).  pad of a computed value keeps its own rule (its pad value must
+  // not pass through the computation) and stays unsupported.
+  void push_index_maps() {
+    static const std::set<std::string> maps = {"transpose", "broadcast_in_dim", "slice", "reshape"};
+    size_t fresh = 0;
+    auto add = [&](Op op) {
+      op.result = "%ask_b200.moved" + std::to_string(fresh++);
+      f_.ops.push_back(op);
+      def_[op.result] = f_.ops.size() - 1;
+      return f_.ops.back().result;
+    };
+    auto replace_uses = [&](const std::string& from, const std::string& to) {
+      for (Op& o : f_.ops)
+        for (std::string& x : o.operands)
+          if (x == from) x = to;
+      for (std::string& r : f_.returns)
+        if (r == from) r = to;
+    };
+    for (size_t i = 0; i < f_.ops.size(); ++i) {
+      if (f_.ops.size() > 100000) unsupported("index maps of computed values nest too deeply");
+      const Op op = f_.ops[i];  // copies: f_.ops grows below
+      const std::string n = strip(op.name);
+      if (!maps.count(n) || op.operands.empty() || !producer(op.operands[0])) continue;
+      const Op src = *producer(op.operands[0]);
+      const std::string sn = strip(src.name);
+      const bool elementwise = kUnary.count(sn) || kBinary.count(sn) || sn == "cast" || sn == "compare" ||
+                               sn == "select";
+      std::string moved;
+      if (sn == "splat") {
+        Op sp = src;  // a map of a splat is a splat of the mapped shape
+        sp.type.shape = op.type.shape;
+        moved = add(sp);
+      } else if (elementwise) {
+        bool same_shapes = true;
+        for (const std::string& o : src.operands) same_shapes = same_shapes && type_of(o).shape == src.type.shape;
+        if (!same_shapes) continue;
+        Op e = src;
+        e.type.shape = op.type.shape;
+        for (std::string& o : e.operands) {
+          Op m = op;
+          m.operands = {o};
+          m.type = Type{type_of(o).dtype, op.type.shape, true};
+          o = add(m);
+        }
+        moved = add(e);
+      } else {
+        continue;
+      }
+      replace_uses(op.result, moved);
+      f_.ops[i].name = "ask.ask_b200_moved";  // the original map is dead now
+    }
   }
   static std::vector<int64_t> arr(const Op& p, const char* key) {
     auto it = p.attrs.find(key);

@@ -13,8 +13,9 @@
  * reductions (sum, prod, max, min, any, all, argmax, argmin) over one
  * contiguous block of axes, their operands built the same way; gather and
  * scatter_add.  Steps outside it fail
- * with ASK_B200_E_UNSUPPORTED and a message naming the op (an index map of a
- * computed value rather than of an argument, matmul and external steps).
+ * with ASK_B200_E_UNSUPPORTED and a message naming the op (pad of a computed
+ * value, matmul and external steps); transposes, broadcasts, slices and
+ * reshapes of computed elementwise values move onto their operands.
  */
 #ifndef ASK_B200_LOWER_H
 #define ASK_B200_LOWER_H

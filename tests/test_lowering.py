@@ -317,11 +317,77 @@ def test_reductions_over_index_maps_on_gpu(device, case):
         assert np.array_equal(got.cpu().numpy(), np.asarray(w).reshape(-1)), name
 
 
-def test_index_map_of_a_computed_value_is_unsupported():
+def computed_map_steps():
+    """(name, step source, input arrays, expected outputs) of index maps of
+    computed values: the maps move onto the operands."""
+    rng = np.random.default_rng(13)
+    cases = []
+    # transpose of an elementwise expression, then an elementwise use
+    s = Step()
+    x, y, b = s.arg([4, 6], "i32"), s.arg([4, 6], "i32"), s.arg([6, 4], "i32")
+    e = s.op("add", [s.op("mul", [x, s.splat(s.const(3, "i32"), [4, 6])], [4, 6], "i32"), y], [4, 6], "i32")
+    t = s.op("transpose", [e], [6, 4], "i32", "permutation = " + arr([1, 0]))
+    out = s.op("add", [t, b], [6, 4], "i32")
+    xv, yv, bv = (rng.integers(-99, 99, sh).astype(np.int32) for sh in ([4, 6], [4, 6], [6, 4]))
+    cases.append(("transpose_expr", s.text([out]), [xv, yv, bv], [(xv * 3 + yv).T + bv]))
+    # general broadcast of abs(v) along the middle axis, then a slice of a select
+    s = Step()
+    x, v = s.arg([3, 5, 2], "i32"), s.arg([5], "i32")
+    bc = s.op("broadcast_in_dim", [s.op("abs", [v], [5], "i32")], [3, 5, 2], "i32",
+              f"dimensions = {arr([1])}, shape = {arr([3, 5, 2])}")
+    zero = s.splat(s.const(0, "i32"), [3, 5, 2])
+    neg = s.op("mul", [x, s.splat(s.const(-1, "i32"), [3, 5, 2])], [3, 5, 2], "i32")
+    sel = s.op("select", [s.op("compare", [x, zero], [3, 5, 2], "bool", 'predicate = "lt"'), neg, x], [3, 5, 2], "i32")
+    out = s.op("add", [sel, bc], [3, 5, 2], "i32")
+    xv, vv = rng.integers(-9, 9, (3, 5, 2)).astype(np.int32), rng.integers(-9, 9, 5).astype(np.int32)
+    cases.append(("broadcast_select", s.text([out]), [xv, vv], [np.abs(xv) + np.abs(vv)[None, :, None]]))
+    # slice of a reshape of a computed value
+    s = Step()
+    x = s.arg([3, 8], "i64")
+    r = s.op("reshape", [s.op("add", [x, x], [3, 8], "i64")], [6, 4], "i64", f"shape = {arr([6, 4])}")
+    sl = s.op("slice", [r], [3, 2], "i64", f"starts = {arr([0, 1])}, stops = {arr([6, 4])}, steps = {arr([2, 2])}")
+    xv = rng.integers(-1000, 1000, (3, 8)).astype(np.int64)
+    cases.append(("slice_reshape", s.text([sl]), [xv], [(2 * xv).reshape(6, 4)[0:6:2, 1:4:2]]))
+    # a reduction of a transposed product: column sums of x * y
+    s = Step()
+    x, y = s.arg([7, 5], "i32"), s.arg([7, 5], "i32")
+    t = s.op("transpose", [s.op("mul", [x, y], [7, 5], "i32")], [5, 7], "i32", "permutation = " + arr([1, 0]))
+    outs = [s.op("reduce_sum", [t], [5], "i32", "axes = array<i64: 1>"), s.op("argmin", [t], [5], "i64", "axis = 1 : i64")]
+    xv, yv = rng.integers(-30, 30, (7, 5)).astype(np.int32), rng.integers(-30, 30, (7, 5)).astype(np.int32)
+    cases.append(("reduce_transposed_product", s.text(outs), [xv, yv],
+                  [(xv * yv).sum(axis=0).astype(np.int32), np.argmin((xv * yv).T, axis=1)]))
+    return cases
+
+
+@pytest.mark.parametrize("case", computed_map_steps(), ids=lambda c: c[0])
+def test_index_maps_of_computed_values_lower(case):
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    ask_b200.Plan(out["recipe"], -1)  # validates
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", computed_map_steps(), ids=lambda c: c[0])
+def test_index_maps_of_computed_values_on_gpu(device, case):
+    import torch
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    plan = ask_b200.Plan(out["recipe"], 0)
+    dev_in = [torch.from_numpy(np.ascontiguousarray(ins[a])).cuda() for a in out["input_arguments"]]
+    dev_out = [torch.empty(np.asarray(w).size, dtype=torch.from_numpy(np.ascontiguousarray(w)).dtype, device="cuda")
+               for w in want]
+    plan.launch(dev_in, dev_out, None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    for got, w in zip(dev_out, want):
+        assert np.array_equal(got.cpu().numpy(), np.asarray(w).reshape(-1)), name
+
+
+def test_pad_of_a_computed_value_is_unsupported():
     s = Step()
     x = s.arg([4, 8], "f32")
     e = s.op("exp", [x], [4, 8], "f32")
-    y = s.op("transpose", [e], [8, 4], "f32", "permutation = " + arr([1, 0]))
+    pv = s.splat(s.const("0.000000e+00", "f32"), [])
+    y = s.op("pad", [e, pv], [6, 8], "f32", f"pad_low = {arr([1, 0])}, pad_high = {arr([1, 0])}, interior = {arr([0, 0])}")
     with pytest.raises(rt.CUDAError) as err:
         rt.lower_step(s.text([y]))
     assert err.value.status == ask_b200.E_UNSUPPORTED and "computed value" in str(err.value)
