@@ -153,14 +153,35 @@ def _programs(n):
     return [("chain", 7, [0], [6], chain), ("fork_join", 7, [0], [6, 2], dag)]
 
 
+def _random_program(seed):
+    """A random DAG of affine/add steps over internal buffers: each step reads
+    one or two earlier buffers; a random subset of the buffers is public."""
+    rng = np.random.default_rng(seed)
+    nsteps = int(rng.integers(3, 10))
+    steps = []
+    for k in range(nsteps):
+        out = k + 1
+        if k >= 1 and rng.random() < 0.4:
+            a, b = (int(x) for x in rng.choice(out, 2, replace=False))
+            steps.append(("add", [a, b], [out]))
+        else:
+            steps.append(("affine", [int(rng.integers(0, out))], [out]))
+    extra = [int(b) for b in rng.choice(np.arange(1, nsteps), size=min(2, nsteps - 1), replace=False)]
+    outs = sorted(set([nsteps] + extra))
+    return f"random{seed}", nsteps + 1, [0], outs, steps
+
+
 @pytest.mark.parametrize("graph", [False, True])
-@pytest.mark.parametrize("which", [0, 1])
+@pytest.mark.parametrize("which", [0, 1] + [f"r{k}" for k in range(6)])
 def test_programs_match_the_reference_runtime(ref, graph, which):
     """The same kernel-step program through this library's runtime and the
     reference's: identical outputs and identical slot and graph counters."""
     from ask_b200 import runtime as rt
     n = 1 << 16
-    name, nbuf, ins, outs, steps = _programs(n)[which]
+    if isinstance(which, str):
+        name, nbuf, ins, outs, steps = _random_program(int(which[1:]))
+    else:
+        name, nbuf, ins, outs, steps = _programs(n)[which]
     arts = {}
     for key, rec in (("affine", _affine_i32(n, 3, 1)), ("add", _add_i32(n))):
         req = A.request_for(rec, entry=f"k_{key}", grid=(148, 1, 1))
