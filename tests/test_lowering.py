@@ -506,3 +506,106 @@ def test_lowered_gather_scatter_program(device, graph):
     np.add.at(want, ix, t[ix])
     # integer-valued f32 updates: every partial sum is exact, so the result is too
     assert np.array_equal(got, want.astype(np.float32))
+
+
+# ---- random steps: elementwise ops and index maps, against numpy ---------------------------
+def random_map_step(seed, depth=3):
+    """A random i32 step mixing elementwise ops with transpose, slice,
+    broadcast_in_dim and reshape of arguments and of computed values.
+    Returns (source, argument arrays, expected result)."""
+    rng = np.random.default_rng(seed)
+    s = Step()
+    args = []
+
+    def leaf(shape):
+        if rng.random() < 0.2:
+            c = int(rng.integers(-5, 6))
+            return s.splat(s.const(c, "i32"), list(shape)), np.full(shape, c, np.int32)
+        v = rng.integers(-20, 21, shape).astype(np.int32)
+        args.append(v)
+        return s.arg(list(shape), "i32"), v
+
+    def gen(shape, d):
+        r = rng.random()
+        if d == 0 or r < 0.2:
+            return leaf(shape)
+        if r < 0.5:
+            op = ["add", "mul", "maximum", "minimum"][int(rng.integers(4))]
+            (a, av), (b, bv) = gen(shape, d - 1), gen(shape, d - 1)
+            f = {"add": np.add, "mul": np.multiply, "maximum": np.maximum, "minimum": np.minimum}[op]
+            return s.op(op, [a, b], list(shape), "i32"), f(av, bv).astype(np.int32)
+        if r < 0.6:
+            a, av = gen(shape, d - 1)
+            return s.op("abs", [a], list(shape), "i32"), np.abs(av).astype(np.int32)
+        if r < 0.72 and len(shape) > 1:
+            perm = [int(x) for x in rng.permutation(len(shape))]
+            inner = [0] * len(shape)
+            for dd, p in enumerate(perm):
+                inner[p] = shape[dd]
+            a, av = gen(inner, d - 1)
+            return s.op("transpose", [a], list(shape), "i32", "permutation = " + arr(perm)), np.transpose(av, perm)
+        if r < 0.84:
+            starts = [int(rng.integers(0, 3)) for _ in shape]
+            steps = [int(rng.integers(1, 3)) for _ in shape]
+            inner = [st + (n - 1) * sp + 1 + int(rng.integers(0, 2)) for st, sp, n in zip(starts, steps, shape)]
+            stops = [st + (n - 1) * sp + 1 for st, sp, n in zip(starts, steps, shape)]
+            a, av = gen(inner, d - 1)
+            sl = tuple(slice(st, sp_, stp) for st, sp_, stp in zip(starts, stops, steps))
+            return (s.op("slice", [a], list(shape), "i32",
+                         f"starts = {arr(starts)}, stops = {arr(stops)}, steps = {arr(steps)}"), av[sl])
+        if r < 0.94:
+            keep = [dd for dd in range(len(shape)) if rng.random() < 0.6]
+            inner = [shape[dd] for dd in keep]
+            a, av = gen(inner, d - 1)
+            bv = np.broadcast_to(av.reshape([shape[dd] if dd in keep else 1 for dd in range(len(shape))]), shape)
+            return (s.op("broadcast_in_dim", [a], list(shape), "i32",
+                         f"dimensions = {arr(keep)}, shape = {arr(shape)}"), np.ascontiguousarray(bv))
+        n = int(np.prod(shape))
+        a, av = gen([n], d - 1)
+        return s.op("reshape", [a], list(shape), "i32", f"shape = {arr(shape)}"), av.reshape(shape)
+
+    shape = [int(x) for x in rng.integers(2, 6, int(rng.integers(2, 4)))]
+    y, yv = gen(shape, depth)
+    if not args:  # a step reads at least one argument
+        a, av = leaf(shape)
+        while not args:
+            a, av = leaf(shape)
+        y, yv = s.op("add", [y, a], list(shape), "i32"), (yv + av).astype(np.int32)
+    return s.text([y]), args, yv
+
+
+def _lower_random(seed):
+    src, args, want = random_map_step(seed)
+    try:
+        return rt.lower_step(src), args, want
+    except rt.CUDAError as e:
+        assert e.status == ask_b200.E_UNSUPPORTED, str(e)
+        return None, args, want
+
+
+def test_random_map_steps_lower():
+    lowered = 0
+    for seed in range(60):
+        out, args, want = _lower_random(seed)
+        if out is not None:
+            ask_b200.Plan(out["recipe"], -1)
+            lowered += 1
+    assert lowered >= 40, lowered
+
+
+@pytest.mark.gpu
+def test_random_map_steps_on_gpu(device):
+    import torch
+    checked = 0
+    for seed in range(60):
+        out, args, want = _lower_random(seed)
+        if out is None:
+            continue
+        plan = ask_b200.Plan(out["recipe"], 0)
+        dev_in = [torch.from_numpy(np.ascontiguousarray(args[a])).cuda() for a in out["input_arguments"]]
+        y = torch.empty(want.size, dtype=torch.int32, device="cuda")
+        plan.launch(dev_in, [y], None, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        assert np.array_equal(y.cpu().numpy(), want.reshape(-1)), seed
+        checked += 1
+    assert checked >= 40
