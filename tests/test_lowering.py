@@ -609,3 +609,81 @@ def test_random_map_steps_on_gpu(device):
         assert np.array_equal(y.cpu().numpy(), want.reshape(-1)), seed
         checked += 1
     assert checked >= 40
+
+
+def random_reduce_step(seed):
+    """A random map-and-elementwise i32 operand reduced over a random block of
+    contiguous axes with sum, max, min and argmax (argmax over a single axis)."""
+    src, args, yv = random_map_step(seed + 1000, depth=2)
+    # rebuild the step with reductions of its result
+    rng = np.random.default_rng(seed)
+    rank = yv.ndim
+    a0 = int(rng.integers(0, rank))
+    a1 = a0 + 1 if rng.random() < 0.5 else int(rng.integers(a0 + 1, rank + 1))
+    axes = list(range(a0, a1))
+    out_shape = [d for k, d in enumerate(yv.shape) if k not in axes]
+    lines = src.rstrip().splitlines()
+    ret = lines[-3].strip()  # "return %v : type"
+    v, ty = ret[len("return "):].split(" : ")
+    body = lines[:-3]
+    ot = ttype(out_shape, "i32")
+    names = []
+    extra = []
+    for k, op in enumerate(["reduce_sum", "reduce_max", "reduce_min"]):
+        r = f"%red{k}"
+        extra.append(f'    {r} = "ask.{op}"({v}) {{ask.id = "kernel0.red{k}", axes = {arr(axes)}}} : ({ty}) -> {ot}')
+        names.append((r, ot))
+    want = [yv.sum(axis=tuple(axes)).astype(np.int32), yv.max(axis=tuple(axes)), yv.min(axis=tuple(axes))]
+    if len(axes) == 1:
+        extra.append(f'    %red3 = "ask.argmax"({v}) {{ask.id = "kernel0.red3", axis = {a0} : i64}} : ({ty}) -> '
+                     f'{ttype(out_shape, "i64")}')
+        names.append(("%red3", ttype(out_shape, "i64")))
+        want.append(np.argmax(yv, axis=a0))
+    head = body[0:2]
+    sig_line = body[1]
+    # the function's result types follow the new returns
+    res = ", ".join(t for _, t in names)
+    sig_line = sig_line[:sig_line.index("-> (") + 4] + res + sig_line[sig_line.index(") attributes"):]
+    text = "\n".join([body[0], sig_line] + body[2:] + extra +
+                     [f"    return {', '.join(n for n, _ in names)} : {res}", "  }", "}"]) + "\n"
+    return text, args, want
+
+
+def _lower_random_reduce(seed):
+    src, args, want = random_reduce_step(seed)
+    try:
+        return rt.lower_step(src), args, want
+    except rt.CUDAError as e:
+        assert e.status == ask_b200.E_UNSUPPORTED, str(e)
+        return None, args, want
+
+
+def test_random_reduce_steps_lower():
+    lowered = 0
+    for seed in range(40):
+        out, args, want = _lower_random_reduce(seed)
+        if out is not None:
+            assert out["recipe"]["family"] == "reduce"
+            ask_b200.Plan(out["recipe"], -1)
+            lowered += 1
+    assert lowered >= 30, lowered
+
+
+@pytest.mark.gpu
+def test_random_reduce_steps_on_gpu(device):
+    import torch
+    checked = 0
+    for seed in range(40):
+        out, args, want = _lower_random_reduce(seed)
+        if out is None:
+            continue
+        plan = ask_b200.Plan(out["recipe"], 0)
+        dev_in = [torch.from_numpy(np.ascontiguousarray(args[a])).cuda() for a in out["input_arguments"]]
+        outs = [torch.empty(np.asarray(w).size, dtype=torch.from_numpy(np.ascontiguousarray(w)).dtype, device="cuda")
+                for w in want]
+        plan.launch(dev_in, outs, None, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        for got, w in zip(outs, want):
+            assert np.array_equal(got.cpu().numpy(), np.asarray(w).reshape(-1)), seed
+        checked += 1
+    assert checked >= 30
