@@ -19,6 +19,7 @@
 #include "kernels.h"
 #include "programs.h"
 #include "vec_io.cuh"
+#include "pdl.cuh"
 #include "ew_body.cuh"
 
 namespace askb {
@@ -33,6 +34,7 @@ using ew::FnSoftmaxNorm;
 
 template <class P, int V, int U>
 __global__ void __launch_bounds__(kEwThreads) ew_spec_kernel(const __grid_constant__ EwArgs args, int aligned) {
+  pdl_enter();
   ew_spec_loop<P, V, U>(args, aligned);
 }
 
@@ -40,6 +42,7 @@ __global__ void __launch_bounds__(kEwThreads) ew_spec_kernel(const __grid_consta
 template <int V>
 __global__ void __launch_bounds__(kEwThreads)
     ew_generic_kernel(const __grid_constant__ Program prog, const __grid_constant__ EwArgs args, int aligned) {
+  pdl_enter();
   const uint64_t n = args.count;
   const uint64_t units = (n + V - 1) / V;
   const uint64_t nthreads = uint64_t(gridDim.x) * kEwThreads;
@@ -73,11 +76,13 @@ __global__ void __launch_bounds__(kEwThreads)
 __global__ void __launch_bounds__(kEwThreads) ew_view_kernel(const __grid_constant__ Program prog,
                                                              const __grid_constant__ EwArgs args,
                                                              const __grid_constant__ ViewSet views) {
+  pdl_enter();
   ew_view_loop(prog, args, views);
 }
 
 template <class F>
 __global__ void __launch_bounds__(kEwThreads) ew_functor_kernel(const __grid_constant__ EwArgs a, uint64_t units) {
+  pdl_enter();
   ew_functor_loop<F>(a, units);
 }
 
@@ -113,7 +118,7 @@ int ew_num_specs() { return EW_NUM_SPECS; }
 
 cudaError_t ew_view_launch(const Program& prog, const EwArgs& args, const ViewSet& views, int grid, cudaStream_t stream) {
   if (args.count == 0) return cudaSuccess;
-  ew_view_kernel<<<dim3(grid), dim3(kEwThreads), 0, stream>>>(prog, args, views);
+  (void)launch_pdl(&ew_view_kernel, dim3(grid), dim3(kEwThreads), stream, prog, args, views);
   return cudaGetLastError();
 }
 
@@ -136,32 +141,32 @@ cudaError_t ew_launch(int spec, const Program& prog, const EwArgs& args, int ali
   if (args.count == 0) return cudaSuccess;
   const dim3 g(grid), b(kEwThreads);
   if (spec == EW_CFG1 && functor_ok<FnCfg1>(args, aligned)) {
-    ew_functor_kernel<FnCfg1><<<g, b, 0, stream>>>(args, args.count / FnCfg1::V);
+    (void)launch_pdl(&ew_functor_kernel<FnCfg1>, g, b, stream, args, args.count / FnCfg1::V);
     return cudaGetLastError();
   }
   if (spec == EW_SOFTMAX_NORM_F16 && functor_ok<FnSoftmaxNorm<kF16>>(args, aligned)) {
-    ew_functor_kernel<FnSoftmaxNorm<kF16>><<<g, b, 0, stream>>>(args, args.count / 8);
+    (void)launch_pdl(&ew_functor_kernel<FnSoftmaxNorm<kF16>>, g, b, stream, args, args.count / 8);
     return cudaGetLastError();
   }
   if (spec == EW_SOFTMAX_NORM_BF16 && functor_ok<FnSoftmaxNorm<kBF16>>(args, aligned)) {
-    ew_functor_kernel<FnSoftmaxNorm<kBF16>><<<g, b, 0, stream>>>(args, args.count / 8);
+    (void)launch_pdl(&ew_functor_kernel<FnSoftmaxNorm<kBF16>>, g, b, stream, args, args.count / 8);
     return cudaGetLastError();
   }
   switch (spec) {
     case EW_CFG1:
-      ew_spec_kernel<ProgCfg1, 4, 2><<<g, b, 0, stream>>>(args, aligned);
+      (void)launch_pdl(&ew_spec_kernel<ProgCfg1, 4, 2>, g, b, stream, args, aligned);
       break;
     case EW_CFG5B:
-      ew_spec_kernel<ProgCfg5b, 4, 2><<<g, b, 0, stream>>>(args, aligned);
+      (void)launch_pdl(&ew_spec_kernel<ProgCfg5b, 4, 2>, g, b, stream, args, aligned);
       break;
     case EW_SOFTMAX_NORM_F16:
-      ew_spec_kernel<ProgSoftmaxNorm<kF16>, 4, 2><<<g, b, 0, stream>>>(args, aligned);
+      (void)launch_pdl(&ew_spec_kernel<ProgSoftmaxNorm<kF16>, 4, 2>, g, b, stream, args, aligned);
       break;
     case EW_SOFTMAX_NORM_BF16:
-      ew_spec_kernel<ProgSoftmaxNorm<kBF16>, 4, 2><<<g, b, 0, stream>>>(args, aligned);
+      (void)launch_pdl(&ew_spec_kernel<ProgSoftmaxNorm<kBF16>, 4, 2>, g, b, stream, args, aligned);
       break;
     default:
-      ew_generic_kernel<4><<<g, b, 0, stream>>>(prog, args, aligned);
+      (void)launch_pdl(&ew_generic_kernel<4>, g, b, stream, prog, args, aligned);
       break;
   }
   return cudaGetLastError();

@@ -35,6 +35,7 @@
 #include "kernels.h"
 #include "programs.h"
 #include "vec_io.cuh"
+#include "pdl.cuh"
 #include "reduce_acc.cuh"
 #include "reduce_fast.cuh"
 
@@ -157,12 +158,14 @@ __device__ __forceinline__ void write_outputs(const RedArgs& a, const Accs& s, u
 template <class S, class R, int U>
 __global__ void __launch_bounds__(kRedThreads)
     red_warp_row_kernel(const __grid_constant__ RedArgs a, int aligned) {
+  pdl_enter();
   red_warp_row_loop<S, R, U>(a, aligned);
 }
 
 template <int V>
 __global__ void __launch_bounds__(kRedThreads)
     red_warp_row_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a, int aligned) {
+  pdl_enter();
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t warp = (uint64_t(blockIdx.x) * kRedThreads + threadIdx.x) >> 5;
   const uint64_t nwarps = (uint64_t(gridDim.x) * kRedThreads) >> 5;
@@ -179,6 +182,7 @@ __global__ void __launch_bounds__(kRedThreads)
 // inner > 1: thread per output (o, n); element (o, e, n) at (o*extent + e)*inner + n.
 __global__ void __launch_bounds__(kRedThreads)
     red_column_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a) {
+  pdl_enter();
   const uint64_t n_outputs = a.outer * a.inner;
   uint64_t r[kMaxRegs][1];
   for (uint64_t o_idx = uint64_t(blockIdx.x) * kRedThreads + threadIdx.x; o_idx < n_outputs;
@@ -217,6 +221,7 @@ __global__ void __launch_bounds__(kRedThreads)
 __global__ void __launch_bounds__(kRedThreads)
     red_view_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a,
                      const __grid_constant__ ViewSet views) {
+  pdl_enter();
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t warp = (uint64_t(blockIdx.x) * kRedThreads + threadIdx.x) >> 5;
   const uint64_t nwarps = (uint64_t(gridDim.x) * kRedThreads) >> 5;
@@ -287,6 +292,7 @@ __device__ __forceinline__ void split_chunk(uint64_t extent, uint32_t c, uint32_
 template <class S, class R, int U>
 __global__ void __launch_bounds__(kRedThreads)
     red_split_kernel(const __grid_constant__ RedArgs a, int aligned, RedPartial* __restrict__ part) {
+  pdl_enter();
   for (uint64_t o = 0; o < a.outer; ++o) {
     uint64_t e0, e1;
     split_chunk(a.extent, blockIdx.x, gridDim.x, uint64_t(S::V) * 32, e0, e1);
@@ -305,6 +311,7 @@ template <class R, int VT>
 __global__ void __launch_bounds__(kRedThreads)
     red_combine_set_kernel(const __grid_constant__ RedArgs a, const RedPartial* __restrict__ part, int n,
                            RedPartial* __restrict__ rec_out) {
+  pdl_enter();
   const uint64_t o = blockIdx.x;
   AccsT<R> s;
   set_init<R, VT, 0>(s);
@@ -330,6 +337,7 @@ template <int V>
 __global__ void __launch_bounds__(kRedThreads)
     red_split_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a, int aligned,
                       RedPartial* __restrict__ part) {
+  pdl_enter();
   uint64_t r[kMaxRegs][V];
   for (uint64_t o = 0; o < a.outer; ++o) {
     uint64_t e0, e1;
@@ -350,6 +358,7 @@ __global__ void __launch_bounds__(kRedThreads)
 __global__ void __launch_bounds__(kRedThreads)
     red_combine_kernel(const __grid_constant__ RedArgs a, const RedPartial* __restrict__ part, int n,
                        RedPartial* __restrict__ rec_out) {
+  pdl_enter();
   const uint64_t o = blockIdx.x;
   Accs s;
   accs_init(a, s);
@@ -431,7 +440,7 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
                        void* scratch, RedPartial* rec_out, cudaStream_t st) {
   if (a.outer == 0 || a.inner == 0) return cudaSuccess;
   if (strategy == RS_COLUMN) {
-    red_column_generic<<<grid, kRedThreads, 0, st>>>(prog, a);
+    (void)launch_pdl(&red_column_generic, dim3(grid), dim3(kRedThreads), st, prog, a);
     return cudaGetLastError();
   }
   cudaError_t err = cudaSuccess;
@@ -440,33 +449,33 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
     using R = decltype(r);
     constexpr int U = Unroll<S>::U;
     if (strategy == RS_WARP_ROW) {
-      red_warp_row_kernel<S, R, U><<<grid, kRedThreads, 0, st>>>(a, aligned);
+      (void)launch_pdl(&red_warp_row_kernel<S, R, U>, dim3(grid), dim3(kRedThreads), st, a, aligned);
       err = cudaGetLastError();
       return;
     }
     RedPartial* part = static_cast<RedPartial*>(scratch);
-    red_split_kernel<S, R, U><<<grid, kRedThreads, 0, st>>>(a, aligned, part);
+    (void)launch_pdl(&red_split_kernel<S, R, U>, dim3(grid), dim3(kRedThreads), st, a, aligned, part);
     err = cudaGetLastError();
     if (err != cudaSuccess) return;
-    red_combine_set_kernel<R, kF32><<<unsigned(a.outer), kRedThreads, 0, st>>>(a, part, grid, rec_out);
+    (void)launch_pdl(&red_combine_set_kernel<R, kF32>, dim3(unsigned(a.outer)), dim3(kRedThreads), st, a, part, grid, rec_out);
     err = cudaGetLastError();
   });
   if (found) return err;
   if (strategy == RS_WARP_ROW) {
-    red_warp_row_generic<4><<<grid, kRedThreads, 0, st>>>(prog, a, aligned);
+    (void)launch_pdl(&red_warp_row_generic<4>, dim3(grid), dim3(kRedThreads), st, prog, a, aligned);
     return cudaGetLastError();
   }
   RedPartial* part = static_cast<RedPartial*>(scratch);
-  red_split_generic<4><<<grid, kRedThreads, 0, st>>>(prog, a, aligned, part);
+  (void)launch_pdl(&red_split_generic<4>, dim3(grid), dim3(kRedThreads), st, prog, a, aligned, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  red_combine_kernel<<<unsigned(a.outer), kRedThreads, 0, st>>>(a, part, grid, rec_out);
+  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(kRedThreads), st, a, part, grid, rec_out);
   return cudaGetLastError();
 }
 
 cudaError_t red_view_launch(const Program& prog, const RedArgs& a, const ViewSet& views, int grid, cudaStream_t st) {
   if (a.outer == 0 || a.inner == 0) return cudaSuccess;
-  red_view_generic<<<grid, kRedThreads, 0, st>>>(prog, a, views);
+  (void)launch_pdl(&red_view_generic, dim3(grid), dim3(kRedThreads), st, prog, a, views);
   return cudaGetLastError();
 }
 
@@ -477,7 +486,7 @@ int red_view_occupancy() {
 }
 
 cudaError_t red_combine_records(const RedArgs& a, const RedPartial* records, int n, cudaStream_t st) {
-  red_combine_kernel<<<unsigned(a.outer), kRedThreads, 0, st>>>(a, records, n, nullptr);
+  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(kRedThreads), st, a, records, n, nullptr);
   return cudaGetLastError();
 }
 
