@@ -458,6 +458,13 @@ const std::set<std::string> kBinary = {"add", "mul", "div", "floordiv", "mod", "
 
 std::string strip(const std::string& n) { return n.rfind("ask.", 0) == 0 ? n.substr(4) : n; }
 
+// Synthetic ops the lowering adds while moving index maps onto operands: a
+// window map reads its operand at (c - lo) / step per axis (a pad's window
+// without the pad value), a window mask is true where that coordinate is
+// valid (non-negative, divisible, below the operand's extent).
+constexpr const char* kWindow = "ask_b200_window";
+constexpr const char* kWindowMask = "ask_b200_window_mask";
+
 struct Lowered {
   std::string recipe;
   std::vector<size_t> input_args;  // recipe input k reads function argument input_args[k]
@@ -544,7 +551,7 @@ class Lowering {
   // view_of).  pad of a computed value keeps its own rule (its pad value must
   // not pass through the computation) and stays unsupported.
   void push_index_maps() {
-    static const std::set<std::string> maps = {"transpose", "broadcast_in_dim", "slice", "reshape"};
+    static const std::set<std::string> maps = {"transpose", "broadcast_in_dim", "slice", "reshape", kWindow};
     size_t fresh = 0;
     auto add = [&](Op op) {
       op.result = "%ask_b200.moved" + std::to_string(fresh++);
@@ -559,6 +566,87 @@ class Lowering {
       for (std::string& r : f_.returns)
         if (r == from) r = to;
     };
+    // pad and concatenate of computed values: select between window maps of
+    // the operands (pushed below like the other maps) by the coordinates.
+    auto int_array = [](const std::vector<int64_t>& v) {
+      Attr a;
+      a.kind = Attr::IntArray;
+      a.arr = v;
+      return a;
+    };
+    auto window = [&](const std::string& x, const Type& out, const std::vector<int64_t>& lo,
+                      const std::vector<int64_t>& step) {
+      Op w;
+      w.name = std::string("ask.") + kWindow;
+      w.operands = {x};
+      w.attrs["lo"] = int_array(lo);
+      w.attrs["step"] = int_array(step);
+      w.type = Type{type_of(x).dtype, out.shape, true};
+      return add(w);
+    };
+    auto mask = [&](const Type& out, const std::vector<int64_t>& lo, const std::vector<int64_t>& step,
+                    const std::vector<int64_t>& extent) {
+      Op m;
+      m.name = std::string("ask.") + kWindowMask;
+      m.attrs["lo"] = int_array(lo);
+      m.attrs["step"] = int_array(step);
+      m.attrs["extent"] = int_array(extent);
+      m.type = Type{"bool", out.shape, true};
+      return add(m);
+    };
+    auto select = [&](const std::string& c, const std::string& x, const std::string& y, const Type& out) {
+      Op sel;
+      sel.name = "ask.select";
+      sel.operands = {c, x, y};
+      sel.type = out;
+      return add(sel);
+    };
+    const size_t original = f_.ops.size();
+    for (size_t i = 0; i < original; ++i) {
+      const Op op = f_.ops[i];
+      const std::string n = strip(op.name);
+      ArgView ignored;
+      if (n == "pad" && op.operands.size() == 2 && !view_of(op.operands[0], &ignored)) {
+        const std::vector<int64_t> low = arr(op, "pad_low"), interior = arr(op, "interior");
+        const Type in = type_of(op.operands[0]);  // a copy: add() may move the ops
+        std::vector<int64_t> step(low.size());
+        bool nonneg = true;
+        for (size_t d = 0; d < low.size(); ++d) {
+          step[d] = interior[d] + 1;
+          nonneg = nonneg && low[d] >= 0 && interior[d] >= 0;
+        }
+        if (!nonneg) continue;  // stays unsupported
+        Op sp;
+        sp.name = "ask.splat";
+        sp.operands = {op.operands[1]};
+        sp.type = op.type;
+        const std::string padv = add(sp);
+        const std::string w = window(op.operands[0], op.type, low, step);
+        replace_uses(op.result, select(mask(op.type, low, step, in.shape), w, padv, op.type));
+        f_.ops[i].name = "ask.ask_b200_moved";
+      } else if (n == "concatenate") {
+        bool views = true;
+        for (const std::string& o : op.operands) views = views && view_of(o, &ignored);
+        auto ax = op.attrs.find("axis");
+        if (views || ax == op.attrs.end()) continue;  // argument views keep the direct form
+        const size_t axis = size_t(ax->second.i), rank = op.type.shape.size();
+        std::vector<std::pair<std::string, std::string>> parts;  // (window, mask)
+        int64_t at = 0;
+        for (const std::string& o : op.operands) {
+          const Type ot = type_of(o);  // a copy: add() may move the ops
+          if (axis >= ot.shape.size() || ot.shape[axis] == 0) continue;
+          std::vector<int64_t> lo(rank, 0), step(rank, 1);
+          lo[axis] = at;
+          parts.emplace_back(window(o, op.type, lo, step), mask(op.type, lo, step, ot.shape));
+          at += ot.shape[axis];
+        }
+        if (parts.empty()) continue;
+        std::string v = parts.back().first;
+        for (size_t k = parts.size() - 1; k-- > 0;) v = select(parts[k].second, parts[k].first, v, op.type);
+        replace_uses(op.result, v);
+        f_.ops[i].name = "ask.ask_b200_moved";
+      }
+    }
     for (size_t i = 0; i < f_.ops.size(); ++i) {
       if (f_.ops.size() > 100000) unsupported("index maps of computed values nest too deeply");
       const Op op = f_.ops[i];  // copies: f_.ops grows below
@@ -731,6 +819,17 @@ class Lowering {
       out->pad = constant_text(*c);
       return true;
     }
+    if (n == kWindow) {
+      if (!view_of(p->operands.at(0), &in)) return false;
+      const auto lo = arr(*p, "lo"), step = arr(*p, "step");
+      *out = in;
+      for (size_t d = 0; d < t.shape.size(); ++d) {
+        if (in.windowed(d)) return false;
+        out->lo[d] = lo[d];
+        out->step[d] = step[d];
+      }
+      return true;
+    }
     if (n == "reshape") {
       if (!view_of(p->operands.at(0), &in)) return false;
       const Type& it = type_of(p->operands.at(0));
@@ -823,7 +922,8 @@ class Lowering {
       const std::string& src = p->operands.at(0);
       if (!arg_.count(src)) unsupported("splat of a computed scalar inside a step");
       id = use_port(arg_.at(src), "scalar");
-    } else if ((n == "broadcast_in_dim" || n == "transpose" || n == "slice" || n == "pad" || n == "reshape") &&
+    } else if ((n == "broadcast_in_dim" || n == "transpose" || n == "slice" || n == "pad" || n == "reshape" ||
+                n == kWindow) &&
                view_of(v, &w)) {
       if (p->type.shape != out_shape_) unsupported("an index map to a shape other than the step's iteration shape");
       const Type& at = f_.arg_types[w.arg];
@@ -874,7 +974,34 @@ class Lowering {
                         std::to_string(id) + "]", dt);
         }
       }
-    } else if (n == "broadcast_in_dim" || n == "reshape" || n == "transpose" || n == "slice" || n == "pad") {
+    } else if (n == kWindowMask) {
+      // AND over the axes of: 0 <= c - lo < extent * step and (c - lo) divisible by step
+      if (p->type.shape != out_shape_) unsupported("a padded or concatenated value of another shape than the step's");
+      const auto lo = arr(*p, "lo"), step = arr(*p, "step"), ext = arr(*p, "extent");
+      const int f = emit("[\"const\",\"bool\",false]", "bool");
+      id = emit("[\"const\",\"bool\",true]", "bool");
+      for (size_t d = 0; d < out_shape_.size(); ++d) {
+        if (lo[d] == 0 && step[d] == 1 && ext[d] >= out_shape_[d]) continue;
+        const int c = coord(int64_t(d));
+        const int q = emit("[\"add\"," + std::to_string(c) + "," +
+                               std::to_string(emit("[\"const\",\"i64\"," + std::to_string(-lo[d]) + "]", "i64")) + "]",
+                           "i64");
+        const int zero = emit("[\"const\",\"i64\",0]", "i64");
+        const int lim = emit("[\"const\",\"i64\"," + std::to_string(ext[d] * step[d]) + "]", "i64");
+        int ok = emit("[\"compare\",\"ge\"," + std::to_string(q) + "," + std::to_string(zero) + "]", "bool");
+        const int lt = emit("[\"compare\",\"lt\"," + std::to_string(q) + "," + std::to_string(lim) + "]", "bool");
+        ok = emit("[\"select\"," + std::to_string(ok) + "," + std::to_string(lt) + "," + std::to_string(f) + "]", "bool");
+        if (step[d] > 1) {
+          const int st = emit("[\"const\",\"i64\"," + std::to_string(step[d]) + "]", "i64");
+          const int rem = emit("[\"mod\"," + std::to_string(q) + "," + std::to_string(st) + "]", "i64");
+          const int div = emit("[\"compare\",\"eq\"," + std::to_string(rem) + "," + std::to_string(zero) + "]", "bool");
+          ok = emit("[\"select\"," + std::to_string(ok) + "," + std::to_string(div) + "," + std::to_string(f) + "]",
+                    "bool");
+        }
+        id = emit("[\"select\"," + std::to_string(id) + "," + std::to_string(ok) + "," + std::to_string(f) + "]", "bool");
+      }
+    } else if (n == "broadcast_in_dim" || n == "reshape" || n == "transpose" || n == "slice" || n == "pad" ||
+               n == kWindow) {
       unsupported("ask." + n + " of a computed value: only index maps of step arguments are supported");
     } else if (n == "cast") {
       const int x = operand(0);

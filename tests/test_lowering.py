@@ -382,15 +382,58 @@ def test_index_maps_of_computed_values_on_gpu(device, case):
         assert np.array_equal(got.cpu().numpy(), np.asarray(w).reshape(-1)), name
 
 
-def test_pad_of_a_computed_value_is_unsupported():
+def padded_concat_steps():
+    """pad and concatenate of computed values (and a pad with interior padding)."""
+    rng = np.random.default_rng(21)
+    cases = []
     s = Step()
-    x = s.arg([4, 8], "f32")
-    e = s.op("exp", [x], [4, 8], "f32")
-    pv = s.splat(s.const("0.000000e+00", "f32"), [])
-    y = s.op("pad", [e, pv], [6, 8], "f32", f"pad_low = {arr([1, 0])}, pad_high = {arr([1, 0])}, interior = {arr([0, 0])}")
-    with pytest.raises(rt.CUDAError) as err:
-        rt.lower_step(s.text([y]))
-    assert err.value.status == ask_b200.E_UNSUPPORTED and "computed value" in str(err.value)
+    x = s.arg([3, 4], "i32")
+    e = s.op("mul", [x, s.splat(s.const(5, "i32"), [3, 4])], [3, 4], "i32")
+    pv = s.splat(s.const(-7, "i32"), [])
+    y = s.op("pad", [e, pv], [7, 9], "i32", f"pad_low = {arr([1, 2])}, pad_high = {arr([1, 1])}, interior = {arr([1, 1])}")
+    xv = rng.integers(-9, 9, (3, 4)).astype(np.int32)
+    want = np.full((7, 9), -7, np.int32)
+    want[1:1 + 3 * 2:2, 2:2 + 4 * 2:2] = xv * 5
+    cases.append(("pad_interior", s.text([y]), [xv], [want]))
+    s = Step()
+    a, b = s.arg([2, 3], "i32"), s.arg([2, 5], "i32")
+    ea = s.op("abs", [a], [2, 3], "i32")
+    eb = s.op("add", [b, b], [2, 5], "i32")
+    y = s.op("concatenate", [ea, b, eb], [2, 13], "i32", "axis = 1 : i64")
+    av, bv = rng.integers(-9, 9, (2, 3)).astype(np.int32), rng.integers(-9, 9, (2, 5)).astype(np.int32)
+    cases.append(("concat_computed", s.text([y]), [av, bv], [np.concatenate([np.abs(av), bv, 2 * bv], axis=1)]))
+    s = Step()
+    x = s.arg([4, 6], "i32")
+    t = s.op("transpose", [s.op("maximum", [x, s.splat(s.const(0, "i32"), [4, 6])], [4, 6], "i32")], [6, 4], "i32",
+             "permutation = " + arr([1, 0]))
+    pv = s.splat(s.const(3, "i32"), [])
+    y = s.op("pad", [t, pv], [8, 5], "i32", f"pad_low = {arr([2, 0])}, pad_high = {arr([0, 1])}, interior = {arr([0, 0])}")
+    xv = rng.integers(-9, 9, (4, 6)).astype(np.int32)
+    want = np.full((8, 5), 3, np.int32)
+    want[2:8, 0:4] = np.maximum(xv, 0).T
+    cases.append(("pad_of_transposed_max", s.text([y]), [xv], [want]))
+    return cases
+
+
+@pytest.mark.parametrize("case", padded_concat_steps(), ids=lambda c: c[0])
+def test_pad_and_concatenate_of_computed_values_lower(case):
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    assert ask_b200.Plan(out["recipe"], -1).describe()["kernel"] == "ew_view"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", padded_concat_steps(), ids=lambda c: c[0])
+def test_pad_and_concatenate_of_computed_values_on_gpu(device, case):
+    import torch
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    plan = ask_b200.Plan(out["recipe"], 0)
+    dev_in = [torch.from_numpy(np.ascontiguousarray(ins[a])).cuda() for a in out["input_arguments"]]
+    y = torch.empty(want[0].size, dtype=torch.int32, device="cuda")
+    plan.launch(dev_in, [y], None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy().reshape(want[0].shape), want[0]), name
 
 
 @pytest.mark.gpu
@@ -560,9 +603,31 @@ def random_map_step(seed, depth=3):
             bv = np.broadcast_to(av.reshape([shape[dd] if dd in keep else 1 for dd in range(len(shape))]), shape)
             return (s.op("broadcast_in_dim", [a], list(shape), "i32",
                          f"dimensions = {arr(keep)}, shape = {arr(shape)}"), np.ascontiguousarray(bv))
-        n = int(np.prod(shape))
-        a, av = gen([n], d - 1)
-        return s.op("reshape", [a], list(shape), "i32", f"shape = {arr(shape)}"), av.reshape(shape)
+        if r < 0.97:
+            n = int(np.prod(shape))
+            a, av = gen([n], d - 1)
+            return s.op("reshape", [a], list(shape), "i32", f"shape = {arr(shape)}"), av.reshape(shape)
+        if r < 0.985:
+            low = [int(rng.integers(0, 2)) for _ in shape]
+            interior = [int(rng.integers(0, 2)) if n > 1 else 0 for n in shape]
+            inner = [max(1, (n - lo + it) // (it + 1)) for n, lo, it in zip(shape, low, interior)]
+            high = [n - lo - (m - 1) * (it + 1) - 1 for n, lo, m, it in zip(shape, low, inner, interior)]
+            a, av = gen(inner, d - 1)
+            c = int(rng.integers(-5, 6))
+            pv = s.splat(s.const(c, "i32"), [])
+            out = np.full(shape, c, np.int32)
+            out[tuple(slice(lo, lo + (m - 1) * (it + 1) + 1, it + 1) for lo, m, it in zip(low, inner, interior))] = av
+            return (s.op("pad", [a, pv], list(shape), "i32",
+                         f"pad_low = {arr(low)}, pad_high = {arr(high)}, interior = {arr(interior)}"), out)
+        axis = int(rng.integers(0, len(shape)))
+        if shape[axis] < 2:
+            return leaf(shape)
+        cut = int(rng.integers(1, shape[axis]))
+        s1, s2 = list(shape), list(shape)
+        s1[axis], s2[axis] = cut, shape[axis] - cut
+        (a, av), (b, bv) = gen(s1, d - 1), gen(s2, d - 1)
+        return (s.op("concatenate", [a, b], list(shape), "i32", f"axis = {axis} : i64"),
+                np.concatenate([av, bv], axis=axis))
 
     shape = [int(x) for x in rng.integers(2, 6, int(rng.integers(2, 4)))]
     y, yv = gen(shape, depth)
