@@ -28,8 +28,9 @@
 // constants (MLIR prints each float literal so that it re-parses exactly, or
 // as its bit pattern in hex; either is carried over without double rounding).
 // An index map of a computed elementwise value moves onto that value's
-// operands (push_index_maps); pad of a computed value and matmul or external
-// steps are reported as unsupported.
+// operands (push_index_maps); pad and concatenate of computed values become
+// selects, by the coordinates, between window maps of their operands.
+// matmul and external steps are reported as unsupported.
 #include <algorithm>
 #include <cctype>
 #include <cstdio>
@@ -548,8 +549,9 @@ class Lowering {
   // (ScalarEmitter.h:626-774).  Elementwise ops commute with index maps, so
   // the map moves onto the operands -- transpose(exp(x)) = exp(transpose(x)) --
   // until it reaches step arguments (views), splats or other maps (composed by
-  // view_of).  pad of a computed value keeps its own rule (its pad value must
-  // not pass through the computation) and stays unsupported.
+  // view_of).  pad and concatenate of computed values first become selects
+  // between window maps of their operands (a pad value must not pass through
+  // the computation), and the windows move down like the other maps.
   void push_index_maps() {
     static const std::set<std::string> maps = {"transpose", "broadcast_in_dim", "slice", "reshape", kWindow};
     size_t fresh = 0;

@@ -13,9 +13,10 @@
  * reductions (sum, prod, max, min, any, all, argmax, argmin) over one
  * contiguous block of axes, their operands built the same way; gather and
  * scatter_add.  Steps outside it fail
- * with ASK_B200_E_UNSUPPORTED and a message naming the op (pad of a computed
- * value, matmul and external steps); transposes, broadcasts, slices and
- * reshapes of computed elementwise values move onto their operands.
+ * with ASK_B200_E_UNSUPPORTED and a message naming the op (matmul and
+ * external steps, or a slice or reshape of a padded value); index maps of
+ * computed elementwise values move onto their operands, pads and concatenates
+ * of them become coordinate selects.
  */
 #ifndef ASK_B200_LOWER_H
 #define ASK_B200_LOWER_H
