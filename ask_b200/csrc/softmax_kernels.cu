@@ -95,8 +95,12 @@ constexpr int kMaxWarps = 16;
 #endif
 constexpr int kPreferThreads = ASKB_SOFTMAX_THREADS;  // CTA size the row split aims for
 
+// VPT == 4 (4096-element rows, 128-thread CTAs) is compiled for two 512-thread
+// CTAs' worth of registers per SM, 64 a thread: the f16 variant then fits 8
+// CTAs per SM instead of 4 without spilling (same-box A/B on cfg3: 0.111 ms
+// against 0.123 ms); wider rows keep the full budget (VPT == 8 would spill).
 template <int T, int VPT>
-__global__ void __launch_bounds__(kMaxWarps * 32) softmax_rows_kernel(const uint4* __restrict__ x, float* __restrict__ m_out,
+__global__ void __launch_bounds__(kMaxWarps * 32, VPT == 4 ? 2 : 1) softmax_rows_kernel(const uint4* __restrict__ x, float* __restrict__ m_out,
                                                                       float* __restrict__ s_out, uint4* __restrict__ y,
                                                                       uint64_t rows, uint32_t vecs) {
   __shared__ float red_max[2][kMaxWarps];
