@@ -37,6 +37,7 @@
 #include <cstdint>
 #include <cstring>
 #include <map>
+#include <numeric>
 #include <memory>
 #include <set>
 #include <sstream>
@@ -799,10 +800,33 @@ class Lowering {
       const auto steps = arr(*p, "steps");
       *out = in;
       for (size_t d = 0; d < t.shape.size(); ++d) {
-        if (in.windowed(d)) return false;
-        out->offset += starts[d] * in.stride[d];
-        out->stride[d] = in.stride[d] * steps[d];
-        out->extent[d] = t.shape[d];
+        if (!in.windowed(d)) {
+          out->offset += starts[d] * in.stride[d];
+          out->stride[d] = in.stride[d] * steps[d];
+          out->extent[d] = t.shape[d];
+          continue;
+        }
+        // A slice (start s, step k) of a window (lo, step w): output coordinate
+        // c' reads window coordinate s + k c', valid when k c' = lo - s (mod w);
+        // those c' form a progression cf, cf + w/g, ... (g = gcd(k, w)) whose
+        // window index advances by k/g -- again a window.
+        const int64_t k = steps[d], w = in.step[d], diff = in.lo[d] - starts[d];
+        const int64_t g = std::gcd(k, w), period = w / g, advance = k / g;
+        if (((diff % g) + g) % g != 0) {  // no coordinate ever lands on the window
+          out->lo[d] = 0;
+          out->step[d] = 1;
+          out->extent[d] = 0;
+          continue;
+        }
+        const int64_t cmin = diff > 0 ? (diff + k - 1) / k : 0;
+        int64_t cf = cmin;
+        while (((k * cf - diff) % w + w) % w != 0) ++cf;  // at most period - 1 steps
+        const int64_t qf = (starts[d] - in.lo[d] + k * cf) / w;
+        out->offset += qf * in.stride[d];
+        out->lo[d] = cf;
+        out->step[d] = period;
+        out->extent[d] = qf >= in.extent[d] ? 0 : (in.extent[d] - qf + advance - 1) / advance;
+        out->stride[d] = in.stride[d] * advance;
       }
       return true;
     }

@@ -412,6 +412,21 @@ def padded_concat_steps():
     want = np.full((8, 5), 3, np.int32)
     want[2:8, 0:4] = np.maximum(xv, 0).T
     cases.append(("pad_of_transposed_max", s.text([y]), [xv], [want]))
+    # slices of a padded argument: the slice's step meets the pad's interior step
+    for k, (start, step) in enumerate([(1, 3), (0, 2), (2, 4), (3, 1)]):
+        s = Step()
+        x = s.arg([5, 4], "i32")
+        pv = s.splat(s.const(-1, "i32"), [])
+        pd = s.op("pad", [x, pv], [12, 9], "i32",
+                  f"pad_low = {arr([2, 1])}, pad_high = {arr([2, 1])}, interior = {arr([1, 1])}")
+        full = np.full((12, 9), -1, np.int32)
+        xv = rng.integers(-9, 9, (5, 4)).astype(np.int32)
+        full[2:2 + 5 * 2:2, 1:1 + 4 * 2:2] = xv
+        sl = full[start::step, 1::2]
+        y = s.op("slice", [pd], list(sl.shape), "i32",
+                 f"starts = {arr([start, 1])}, stops = {arr([12, 9])}, steps = {arr([step, 2])}")
+        out = s.op("add", [y, s.splat(s.const(0, "i32"), list(sl.shape))], list(sl.shape), "i32")
+        cases.append((f"slice_of_pad_{k}", s.text([out]), [xv], [sl]))
     return cases
 
 
