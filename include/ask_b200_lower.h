@@ -14,7 +14,8 @@
  * contiguous block of axes, their operands built the same way; gather and
  * scatter_add.  Steps outside it fail
  * with ASK_B200_E_UNSUPPORTED and a message naming the op (matmul and
- * external steps, or a slice or reshape of a padded value); index maps of
+ * external steps, a reshape of a padded value, a slice or reshape of a padded
+ * computed value); index maps of
  * computed elementwise values move onto their operands, pads and concatenates
  * of them become coordinate selects.
  */
