@@ -544,6 +544,24 @@ class Lowering {
     if (!p) invalid("value " + v + " is not defined");
     return p->type;
   }
+  // One axis of a window (valid coordinates c: c - lo >= 0, divisible by step,
+  // (c - lo) / step < extent) read through a slice (start s, step k): the
+  // output coordinate c' reads c = s + k c', valid when k c' = lo - s (mod
+  // step); those c' form the progression cf, cf + step / g, ... (g =
+  // gcd(k, step)) whose window index starts at qf and advances by k / g.
+  struct SlicedWindow {
+    int64_t lo, step, extent, qf, advance;
+  };
+  static SlicedWindow slice_window(int64_t lo, int64_t step, int64_t extent, int64_t start, int64_t k) {
+    const int64_t diff = lo - start, g = std::gcd(k, step);
+    if (((diff % g) + g) % g != 0) return {0, 1, 0, 0, 1};  // no coordinate lands on the window
+    int64_t cf = diff > 0 ? (diff + k - 1) / k : 0;
+    while (((k * cf - diff) % step + step) % step != 0) ++cf;  // at most step / g - 1 steps
+    const int64_t qf = (start - lo + k * cf) / step, advance = k / g;
+    const int64_t ext = qf >= extent ? 0 : (extent - qf + advance - 1) / advance;
+    return {cf, step / g, ext, qf, advance};
+  }
+
   // An index map (transpose, broadcast_in_dim, slice, reshape) of a computed
   // elementwise value reads that value at mapped coordinates, which the
   // reference evaluates by re-evaluating the value at the mapped index
@@ -664,6 +682,47 @@ class Lowering {
         Op sp = src;  // a map of a splat is a splat of the mapped shape
         sp.type.shape = op.type.shape;
         moved = add(sp);
+      } else if (sn == kWindowMask && n != "reshape" && n != kWindow) {
+        // a transposed, sliced or broadcast window mask is a window mask
+        const auto lo = arr(src, "lo"), step = arr(src, "step"), ext = arr(src, "extent");
+        const size_t r = op.type.shape.size();
+        std::vector<int64_t> nlo(r, 0), nstep(r, 1), next(op.type.shape.begin(), op.type.shape.end());
+        if (n == "transpose") {
+          const auto perm = arr(op, "permutation");
+          for (size_t d = 0; d < r; ++d) {
+            nlo[d] = lo[size_t(perm[d])];
+            nstep[d] = step[size_t(perm[d])];
+            next[d] = ext[size_t(perm[d])];
+          }
+        } else if (n == "slice") {
+          const auto starts = arr(op, "starts"), steps = arr(op, "steps");
+          for (size_t d = 0; d < r; ++d) {
+            const SlicedWindow sw = slice_window(lo[d], step[d], ext[d], starts[d], steps[d]);
+            nlo[d] = sw.lo;
+            nstep[d] = sw.step;
+            next[d] = sw.extent;
+          }
+        } else {  // broadcast_in_dim: the mapped axes keep their window, a size-1 axis reads coordinate 0
+          const auto dims = arr(op, "dimensions");
+          const Type& in = src.type;
+          for (size_t k = 0; k < dims.size(); ++k) {
+            const size_t d = size_t(dims[k]);
+            if (in.shape[k] == 1 && op.type.shape[d] != 1) {
+              const bool on = lo[k] == 0 && ext[k] > 0;  // coordinate 0 is valid
+              next[d] = on ? op.type.shape[d] : 0;
+              continue;
+            }
+            nlo[d] = lo[k];
+            nstep[d] = step[k];
+            next[d] = ext[k];
+          }
+        }
+        Op m = src;
+        m.attrs["lo"].arr = nlo;
+        m.attrs["step"].arr = nstep;
+        m.attrs["extent"].arr = next;
+        m.type.shape = op.type.shape;
+        moved = add(m);
       } else if (elementwise) {
         bool same_shapes = true;
         for (const std::string& o : src.operands) same_shapes = same_shapes && type_of(o).shape == src.type.shape;
@@ -806,27 +865,12 @@ class Lowering {
           out->extent[d] = t.shape[d];
           continue;
         }
-        // A slice (start s, step k) of a window (lo, step w): output coordinate
-        // c' reads window coordinate s + k c', valid when k c' = lo - s (mod w);
-        // those c' form a progression cf, cf + w/g, ... (g = gcd(k, w)) whose
-        // window index advances by k/g -- again a window.
-        const int64_t k = steps[d], w = in.step[d], diff = in.lo[d] - starts[d];
-        const int64_t g = std::gcd(k, w), period = w / g, advance = k / g;
-        if (((diff % g) + g) % g != 0) {  // no coordinate ever lands on the window
-          out->lo[d] = 0;
-          out->step[d] = 1;
-          out->extent[d] = 0;
-          continue;
-        }
-        const int64_t cmin = diff > 0 ? (diff + k - 1) / k : 0;
-        int64_t cf = cmin;
-        while (((k * cf - diff) % w + w) % w != 0) ++cf;  // at most period - 1 steps
-        const int64_t qf = (starts[d] - in.lo[d] + k * cf) / w;
-        out->offset += qf * in.stride[d];
-        out->lo[d] = cf;
-        out->step[d] = period;
-        out->extent[d] = qf >= in.extent[d] ? 0 : (in.extent[d] - qf + advance - 1) / advance;
-        out->stride[d] = in.stride[d] * advance;
+        const SlicedWindow sw = slice_window(in.lo[d], in.step[d], in.extent[d], starts[d], steps[d]);
+        out->offset += sw.qf * in.stride[d];
+        out->lo[d] = sw.lo;
+        out->step[d] = sw.step;
+        out->extent[d] = sw.extent;
+        out->stride[d] = in.stride[d] * sw.advance;
       }
       return true;
     }
