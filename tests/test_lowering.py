@@ -427,6 +427,19 @@ def padded_concat_steps():
                  f"starts = {arr([start, 1])}, stops = {arr([12, 9])}, steps = {arr([step, 2])}")
         out = s.op("add", [y, s.splat(s.const(0, "i32"), list(sl.shape))], list(sl.shape), "i32")
         cases.append((f"slice_of_pad_{k}", s.text([out]), [xv], [sl]))
+    # slice and transpose of a padded computed value (the pad's mask composes with the map)
+    s = Step()
+    x = s.arg([4, 5], "i32")
+    e = s.op("add", [x, x], [4, 5], "i32")
+    pv = s.splat(s.const(9, "i32"), [])
+    pd = s.op("pad", [e, pv], [10, 8], "i32", f"pad_low = {arr([1, 2])}, pad_high = {arr([2, 1])}, interior = {arr([1, 0])}")
+    xv = rng.integers(-9, 9, (4, 5)).astype(np.int32)
+    full = np.full((10, 8), 9, np.int32)
+    full[1:1 + 4 * 2:2, 2:7] = 2 * xv
+    sl = full[1::3, 0::2]
+    y = s.op("slice", [pd], list(sl.shape), "i32", f"starts = {arr([1, 0])}, stops = {arr([10, 8])}, steps = {arr([3, 2])}")
+    tr = s.op("transpose", [y], list(sl.T.shape), "i32", "permutation = " + arr([1, 0]))
+    cases.append(("transposed_slice_of_padded_sum", s.text([tr]), [xv], [np.ascontiguousarray(sl.T)]))
     return cases
 
 
