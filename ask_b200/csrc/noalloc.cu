@@ -1,10 +1,11 @@
 // Fixed-scratch launch: ask_b200_plan_launch_noalloc.
 //
-// Some callers cannot call cudaMalloc when they launch a step: code that runs
-// while a CUDA graph is being captured in global mode, callers whose device
-// memory is entirely pre-planned by a framework pool (ASK's Runtime sizes and
-// verifies every buffer when a plan is prepared), and embedded or real-time
-// hosts with a fixed device-memory budget.  For the one kernel here that needs
+// Some callers cannot call cudaMalloc when they launch a step: runtimes whose
+// device memory is entirely planned ahead by a pool (ASK's Runtime sizes and
+// verifies every buffer when a plan is prepared, so a launch has no way to add
+// one), and embedded or real-time hosts with a fixed device-memory budget, for
+// which cudaMalloc may fail or stall the launching thread while the device
+// synchronises.  For the one kernel here that needs
 // scratch memory -- the split reduction, which keeps one partial record per CTA
 // between its two kernels -- this entry point supplies that scratch from a
 // file-scope device array instead, so the caller passes only inputs and

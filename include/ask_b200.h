@@ -107,9 +107,10 @@ ASK_B200_API int ask_b200_plan_launch(const ask_b200_plan *plan, const uint64_t 
 /*
  * Launch a reduce plan without any allocation by the caller or the library.
  * This entry point has no counterpart in the reference.  It exists for callers
- * that cannot call cudaMalloc when they launch: code running while a CUDA graph
- * is captured in global mode, callers whose device memory is wholly pre-planned
- * by a framework pool, and hosts with a fixed device-memory budget.  A split
+ * that cannot call cudaMalloc when they launch: runtimes whose device memory is
+ * wholly planned ahead by a pool (nothing may be added at launch time), and
+ * hosts with a fixed device-memory budget, where cudaMalloc may fail or stall
+ * the launching thread while the device synchronises.  A split
  * reduction's scratch (one partial record per CTA) then comes from a
  * file-scope device array of ASK_B200_NOALLOC_SCRATCH_BYTES (1 MiB) that every
  * GPU loading this library holds until the process exits; plans needing more

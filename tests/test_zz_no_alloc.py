@@ -1,8 +1,8 @@
 """The fixed-scratch entry point (ask_b200_plan_launch_noalloc).
 
-Callers that cannot allocate device memory when they launch -- code running
-inside a global-mode CUDA graph capture, or a runtime whose device memory is
-entirely pre-planned -- launch reduce plans through this entry point, which
+Callers that cannot allocate device memory when they launch -- a runtime whose
+device memory is entirely planned ahead by a pool, or a host with a fixed
+device-memory budget -- launch reduce plans through this entry point, which
 takes the split reduction's scratch from a 1 MiB array built into the library
 instead of a buffer the caller allocates.  Its results must equal those of the
 ordinary entry point (ask_b200_plan_launch with caller-provided scratch); the
