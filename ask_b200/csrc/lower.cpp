@@ -481,7 +481,10 @@ struct ArgView {
   std::vector<int64_t> lo, step, extent, stride;
   int64_t offset = 0;
   std::string pad = "0";  // JSON constant for elements outside the window
-  bool windowed(size_t d) const { return lo[d] != 0 || step[d] != 1; }
+  std::vector<int64_t> shape;  // the viewed value's shape (its coordinate ranges)
+  // Whether axis d reads pad at some coordinate: an offset or strided window,
+  // or one that ends before the axis does (a high pad).
+  bool windowed(size_t d) const { return lo[d] != 0 || step[d] != 1 || extent[d] < shape[d]; }
 };
 
 class Lowering {
@@ -521,6 +524,7 @@ class Lowering {
   // op program under construction; insn_port_[i] >= 0 marks an input instruction
   std::vector<std::string> insns_;
   std::vector<int> insn_port_;
+  std::map<std::string, int> shared_;  // emit_shared: instruction text -> its id
   std::vector<std::string> types_;
   std::map<std::string, int> memo_;
   std::vector<Port> ports_;
@@ -622,12 +626,14 @@ class Lowering {
       sel.type = out;
       return add(sel);
     };
+    // Consumers first: a concatenate or pad that takes the select form reads
+    // its operands through windows, which the operands' own decision sees.
     const size_t original = f_.ops.size();
-    for (size_t i = 0; i < original; ++i) {
+    for (size_t i = original; i-- > 0;) {
       const Op op = f_.ops[i];
       const std::string n = strip(op.name);
       ArgView ignored;
-      if (n == "pad" && op.operands.size() == 2 && !view_of(op.operands[0], &ignored)) {
+      if (n == "pad" && op.operands.size() == 2 && !view_of(op.result, &ignored)) {
         const std::vector<int64_t> low = arr(op, "pad_low"), interior = arr(op, "interior");
         const Type in = type_of(op.operands[0]);  // a copy: add() may move the ops
         std::vector<int64_t> step(low.size());
@@ -646,11 +652,17 @@ class Lowering {
         replace_uses(op.result, select(mask(op.type, low, step, in.shape), w, padv, op.type));
         f_.ops[i].name = "ask.ask_b200_moved";
       } else if (n == "concatenate") {
-        bool views = true;
-        for (const std::string& o : op.operands) views = views && view_of(o, &ignored);
         auto ax = op.attrs.find("axis");
-        if (views || ax == op.attrs.end()) continue;  // argument views keep the direct form
+        if (ax == op.attrs.end()) continue;
         const size_t axis = size_t(ax->second.i), rank = op.type.shape.size();
+        // Argument views that are not padded along the axis keep the direct
+        // form unless an index map reads the concatenation.
+        bool direct = !mapped(op.result);
+        for (const std::string& o : op.operands) {
+          ArgView ow;
+          direct = direct && view_of(o, &ow) && (axis >= ow.lo.size() || !ow.windowed(axis));
+        }
+        if (direct) continue;
         std::vector<std::pair<std::string, std::string>> parts;  // (window, mask)
         int64_t at = 0;
         for (const std::string& o : op.operands) {
@@ -682,8 +694,8 @@ class Lowering {
         Op sp = src;  // a map of a splat is a splat of the mapped shape
         sp.type.shape = op.type.shape;
         moved = add(sp);
-      } else if (sn == kWindowMask && n != "reshape" && n != kWindow) {
-        // a transposed, sliced or broadcast window mask is a window mask
+      } else if (sn == kWindowMask && n != "reshape") {
+        // a transposed, sliced, broadcast or windowed window mask is a window mask
         const auto lo = arr(src, "lo"), step = arr(src, "step"), ext = arr(src, "extent");
         const size_t r = op.type.shape.size();
         std::vector<int64_t> nlo(r, 0), nstep(r, 1), next(op.type.shape.begin(), op.type.shape.end());
@@ -701,6 +713,15 @@ class Lowering {
             nlo[d] = sw.lo;
             nstep[d] = sw.step;
             next[d] = sw.extent;
+          }
+        } else if (n == kWindow) {
+          // the outer window's valid coordinate lo2 + step2 i reads the mask at
+          // i, valid when i = lo + step j, j < extent
+          const auto lo2 = arr(op, "lo"), step2 = arr(op, "step");
+          for (size_t d = 0; d < r; ++d) {
+            nlo[d] = lo2[d] + step2[d] * lo[d];
+            nstep[d] = step2[d] * step[d];
+            next[d] = ext[d];
           }
         } else {  // broadcast_in_dim: the mapped axes keep their window, a size-1 axis reads coordinate 0
           const auto dims = arr(op, "dimensions");
@@ -743,10 +764,36 @@ class Lowering {
       f_.ops[i].name = "ask.ask_b200_moved";  // the original map is dead now
     }
   }
+  // Whether an index map (transpose, broadcast_in_dim, slice, reshape,
+  // window) reads v, directly or through elementwise ops (the maps move onto
+  // their operands).
+  bool mapped(const std::string& v, int depth = 0) const {
+    if (depth > 64) return true;
+    for (const Op& o : f_.ops) {
+      if (std::find(o.operands.begin(), o.operands.end(), v) == o.operands.end()) continue;
+      const std::string n = strip(o.name);
+      if (n == "transpose" || n == "broadcast_in_dim" || n == "slice" || n == "reshape" || n == kWindow) {
+        if (o.operands[0] == v) return true;
+      } else if (kUnary.count(n) || kBinary.count(n) || n == "cast" || n == "compare" || n == "select") {
+        if (mapped(o.result, depth + 1)) return true;
+      }
+    }
+    return false;
+  }
   static std::vector<int64_t> arr(const Op& p, const char* key) {
     auto it = p.attrs.find(key);
     if (it == p.attrs.end()) invalid("ask." + strip(p.name) + " needs '" + key + "'");
     return it->second.arr;
+  }
+  // emit() reusing an identical earlier instruction (all are pure); used for
+  // the coordinate arithmetic of window masks, which repeats across masks.
+  int emit_shared(const std::string& insn, const std::string& dtype) {
+    const std::string key = dtype + insn;
+    auto it = shared_.find(key);
+    if (it != shared_.end()) return it->second;
+    const int id = emit(insn, dtype);
+    shared_[key] = id;
+    return id;
   }
   int emit(const std::string& insn, const std::string& dtype, int port = -1) {
     insns_.push_back(insn);
@@ -802,6 +849,11 @@ class Lowering {
     return s;
   }
   bool view_of(const std::string& v, ArgView* out) const {
+    if (!view_of_value(v, out)) return false;
+    out->shape = type_of(v).shape;
+    return true;
+  }
+  bool view_of_value(const std::string& v, ArgView* out) const {
     auto a = arg_.find(v);
     const Type& t = type_of(v);
     if (a != arg_.end()) {
@@ -890,31 +942,73 @@ class Lowering {
       return true;
     }
     if (n == kWindow) {
+      // Coordinate lo + step i reads the operand at i; a windowed operand's i =
+      // in.lo + in.step j reads its argument, so the two compose into one
+      // window (the operand's pad value, if any, fills the rest of it; what
+      // lies outside this window is masked by the select that made it).
       if (!view_of(p->operands.at(0), &in)) return false;
       const auto lo = arr(*p, "lo"), step = arr(*p, "step");
       *out = in;
       for (size_t d = 0; d < t.shape.size(); ++d) {
-        if (in.windowed(d)) return false;
-        out->lo[d] = lo[d];
-        out->step[d] = step[d];
+        out->lo[d] = lo[d] + step[d] * in.lo[d];
+        out->step[d] = step[d] * in.step[d];
       }
       return true;
     }
     if (n == "reshape") {
       if (!view_of(p->operands.at(0), &in)) return false;
-      const Type& it = type_of(p->operands.at(0));
-      if (in.offset != 0 || in.stride != row_major(it.shape) || in.extent != it.shape) return false;
       for (size_t d = 0; d < in.lo.size(); ++d)
         if (in.windowed(d)) return false;
-      out->arg = in.arg;
+      std::vector<int64_t> stride;
+      if (!reshape_strides(type_of(p->operands.at(0)).shape, in.stride, t.shape, &stride)) return false;
+      *out = in;
       out->lo.assign(t.shape.size(), 0);
       out->step.assign(t.shape.size(), 1);
       out->extent = t.shape;
-      out->stride = row_major(t.shape);
-      out->offset = 0;
+      out->stride = stride;
       return true;
     }
     return false;
+  }
+  // Strides that read a strided view of shape `from` (strides `st`) in
+  // row-major order as shape `to`, if a stride per axis can: the axes of
+  // `from` and `to` fall into groups of equal extent products, and the axes
+  // of `from` inside a group must nest (stride[k] = stride[k+1] * extent[k+1]),
+  // as in a reshape without a copy.  Size-1 axes take no part.
+  static bool reshape_strides(const std::vector<int64_t>& from, const std::vector<int64_t>& st,
+                              const std::vector<int64_t>& to, std::vector<int64_t>* out) {
+    out->assign(to.size(), 0);
+    if (product(from, 0, from.size()) == 0) return true;
+    std::vector<int64_t> od, os;  // `from` without its size-1 axes
+    for (size_t k = 0; k < from.size(); ++k)
+      if (from[k] != 1) {
+        od.push_back(from[k]);
+        os.push_back(st[k]);
+      }
+    std::vector<size_t> nd;  // indices of `to`'s axes longer than 1
+    for (size_t k = 0; k < to.size(); ++k)
+      if (to[k] != 1) nd.push_back(k);
+    size_t oi = 0, ni = 0;
+    while (oi < od.size() && ni < nd.size()) {
+      size_t oj = oi + 1, nj = ni + 1;
+      int64_t op = od[oi], np = to[nd[ni]];
+      while (op != np) {
+        if (np < op) {
+          if (nj >= nd.size()) return false;
+          np *= to[nd[nj++]];
+        } else {
+          if (oj >= od.size()) return false;
+          op *= od[oj++];
+        }
+      }
+      for (size_t k = oi; k + 1 < oj; ++k)
+        if (os[k] != od[k + 1] * os[k + 1]) return false;
+      (*out)[nd[nj - 1]] = os[oj - 1];
+      for (size_t k = nj - 1; k > ni; --k) (*out)[nd[k - 1]] = (*out)[nd[k]] * to[nd[k]];
+      oi = oj;
+      ni = nj;
+    }
+    return oi == od.size() && ni == nd.size();
   }
   static bool is_identity(const ArgView& w, const Type& arg, const std::vector<int64_t>& shape) {
     if (arg.numel() != product(shape, 0, shape.size()) || w.offset != 0) return false;
@@ -956,7 +1050,7 @@ class Lowering {
   }
   int coord(int64_t axis) {
     uses_shape_ = true;
-    return emit("[\"coord\"," + std::to_string(axis) + "]", "i64");
+    return emit_shared("[\"coord\"," + std::to_string(axis) + "]", "i64");
   }
   int value(const std::string& v) {
     auto m = memo_.find(v);
@@ -1045,31 +1139,32 @@ class Lowering {
         }
       }
     } else if (n == kWindowMask) {
-      // AND over the axes of: 0 <= c - lo < extent * step and (c - lo) divisible by step
+      // AND over the axes of lo <= c <= lo + (extent - 1) step and c = lo (mod
+      // step); a check the axis's coordinate range already meets is left out.
       if (p->type.shape != out_shape_) unsupported("a padded or concatenated value of another shape than the step's");
       const auto lo = arr(*p, "lo"), step = arr(*p, "step"), ext = arr(*p, "extent");
-      const int f = emit("[\"const\",\"bool\",false]", "bool");
-      id = emit("[\"const\",\"bool\",true]", "bool");
-      for (size_t d = 0; d < out_shape_.size(); ++d) {
-        if (lo[d] == 0 && step[d] == 1 && ext[d] >= out_shape_[d]) continue;
-        const int c = coord(int64_t(d));
-        const int q = emit("[\"add\"," + std::to_string(c) + "," +
-                               std::to_string(emit("[\"const\",\"i64\"," + std::to_string(-lo[d]) + "]", "i64")) + "]",
-                           "i64");
-        const int zero = emit("[\"const\",\"i64\",0]", "i64");
-        const int lim = emit("[\"const\",\"i64\"," + std::to_string(ext[d] * step[d]) + "]", "i64");
-        int ok = emit("[\"compare\",\"ge\"," + std::to_string(q) + "," + std::to_string(zero) + "]", "bool");
-        const int lt = emit("[\"compare\",\"lt\"," + std::to_string(q) + "," + std::to_string(lim) + "]", "bool");
-        ok = emit("[\"select\"," + std::to_string(ok) + "," + std::to_string(lt) + "," + std::to_string(f) + "]", "bool");
-        if (step[d] > 1) {
-          const int st = emit("[\"const\",\"i64\"," + std::to_string(step[d]) + "]", "i64");
-          const int rem = emit("[\"mod\"," + std::to_string(q) + "," + std::to_string(st) + "]", "i64");
-          const int div = emit("[\"compare\",\"eq\"," + std::to_string(rem) + "," + std::to_string(zero) + "]", "bool");
-          ok = emit("[\"select\"," + std::to_string(ok) + "," + std::to_string(div) + "," + std::to_string(f) + "]",
-                    "bool");
+      id = -1;
+      auto both = [&](int x) {
+        id = id < 0 ? x : emit_shared("[\"bitwise_and\"," + std::to_string(id) + "," + std::to_string(x) + "]", "bool");
+      };
+      auto i64 = [&](int64_t c) { return emit_shared("[\"const\",\"i64\"," + std::to_string(c) + "]", "i64"); };
+      for (size_t d = 0; d < out_shape_.size() && id != -2; ++d) {
+        if (ext[d] <= 0) {
+          id = -2;  // no coordinate is inside the window
+          break;
         }
-        id = emit("[\"select\"," + std::to_string(id) + "," + std::to_string(ok) + "," + std::to_string(f) + "]", "bool");
+        const int c = coord(int64_t(d));
+        const int64_t last = lo[d] + (ext[d] - 1) * step[d];
+        if (lo[d] > 0) both(emit_shared("[\"compare\",\"ge\"," + std::to_string(c) + "," + std::to_string(i64(lo[d])) + "]", "bool"));
+        if (last + 1 < out_shape_[d])
+          both(emit_shared("[\"compare\",\"lt\"," + std::to_string(c) + "," + std::to_string(i64(last + 1)) + "]", "bool"));
+        if (step[d] > 1 && ext[d] > 1) {
+          const int rem = emit_shared("[\"mod\"," + std::to_string(c) + "," + std::to_string(i64(step[d])) + "]", "i64");
+          const int64_t want = ((lo[d] % step[d]) + step[d]) % step[d];
+          both(emit_shared("[\"compare\",\"eq\"," + std::to_string(rem) + "," + std::to_string(i64(want)) + "]", "bool"));
+        }
       }
+      if (id < 0) id = emit_shared(std::string("[\"const\",\"bool\",") + (id == -2 ? "false" : "true") + "]", "bool");
     } else if (n == "broadcast_in_dim" || n == "reshape" || n == "transpose" || n == "slice" || n == "pad" ||
                n == kWindow) {
       unsupported("ask." + n + " of a computed value: only index maps of step arguments are supported");
@@ -1103,6 +1198,7 @@ class Lowering {
     insn_port_.clear();
     types_.clear();
     memo_.clear();
+    shared_.clear();
     ports_.clear();
     port_insn_.clear();
     uses_shape_ = false;

@@ -14,10 +14,9 @@
  * contiguous block of axes, their operands built the same way; gather and
  * scatter_add.  Steps outside it fail
  * with ASK_B200_E_UNSUPPORTED and a message naming the op (matmul and
- * external steps, a reshape of a padded value, a slice or reshape of a padded
- * computed value); index maps of
- * computed elementwise values move onto their operands, pads and concatenates
- * of them become coordinate selects.
+ * external steps, a reshape that would need a copy, a reshape of a padded
+ * value); index maps of computed elementwise values move onto their
+ * operands, pads and concatenates of them become coordinate selects.
  */
 #ifndef ASK_B200_LOWER_H
 #define ASK_B200_LOWER_H

@@ -1,0 +1,77 @@
+"""A numpy evaluator for lowered integer elementwise recipes (test helper).
+
+The lowering adapter turns a step source into a recipe whose program reads
+its inputs through index maps ("full", "scalar", "view") and may read the
+iteration coordinates ("coord").  This evaluator runs such a recipe over
+the whole iteration shape at once, with the same view rule as the device
+interpreter (a view port reads element offset + sum((c - lo) / step * stride)
+where every axis has c - lo >= 0, divisible by step, (c - lo) / step < extent,
+else its pad constant), so the lowering's translation can be checked against
+numpy on the CPU.  Only the integer and bool instructions that lowered index
+maps and integer programs use are supported; anything else raises.
+"""
+import numpy as np
+
+_NP = {"i32": np.int32, "i64": np.int64, "bool": np.bool_, "i8": np.int8, "i16": np.int16}
+
+
+def _input(port, arr, shape, inner):
+    m = port.get("map", "full")
+    flat = np.ascontiguousarray(arr).reshape(-1)
+    if m == "scalar":
+        return np.full(shape, flat[0])
+    if m == "full":
+        return flat.reshape(shape)
+    if m in ("outer", "inner"):
+        i = np.arange(int(np.prod(shape)), dtype=np.int64)
+        return flat[i // inner if m == "outer" else i % inner].reshape(shape)
+    if m != "view":
+        raise NotImplementedError(m)
+    v = port["view"]
+    coords = np.indices(shape, dtype=np.int64)
+    ok = np.ones(shape, dtype=bool)
+    off = np.full(shape, v["offset"], dtype=np.int64)
+    for d in range(len(shape)):
+        s = coords[d] - v["lo"][d]
+        q = np.floor_divide(s, v["step"][d])
+        ok &= (s >= 0) & (q * v["step"][d] == s) & (q < v["extent"][d])
+        off += q * v["stride"][d]
+    out = np.full(shape, v["pad"], dtype=flat.dtype)
+    out[ok] = flat[off[ok]]
+    return out
+
+
+def evaluate(recipe, inputs):
+    """Outputs (flat numpy arrays) of an integer elementwise recipe."""
+    assert recipe["family"] == "elementwise"
+    shape = tuple(recipe.get("shape") or [recipe["count"]])
+    regs = []
+    for ins in recipe["program"]:
+        op = ins[0]
+        if op == "const":
+            t = _NP[ins[1]]
+            x = np.full(shape, ins[2], dtype=t)
+        elif op == "input":
+            x = _input(recipe["inputs"][ins[1]], inputs[ins[1]], shape, int(recipe.get("inner", 1)))
+        elif op == "coord":
+            x = np.indices(shape, dtype=np.int64)[ins[1]]
+        elif op == "select":
+            x = np.where(regs[ins[1]].astype(bool), regs[ins[2]], regs[ins[3]])
+        elif op == "compare":
+            a, b = regs[ins[2]], regs[ins[3]]
+            x = {"lt": a < b, "le": a <= b, "gt": a > b, "ge": a >= b, "eq": a == b, "ne": a != b}[ins[1]]
+        elif op == "cast":
+            x = regs[ins[1]].astype(_NP[ins[2]])
+        elif op in ("add", "mul", "maximum", "minimum", "mod", "floordiv", "bitwise_and", "bitwise_or", "bitwise_xor"):
+            a, b = regs[ins[1]], regs[ins[2]]
+            with np.errstate(over="ignore"):
+                x = {"add": np.add, "mul": np.multiply, "maximum": np.maximum, "minimum": np.minimum,
+                     "mod": np.mod, "floordiv": np.floor_divide, "bitwise_and": np.bitwise_and,
+                     "bitwise_or": np.bitwise_or, "bitwise_xor": np.bitwise_xor}[op](a, b).astype(np.result_type(a, b))
+        elif op in ("abs", "bitwise_not"):
+            with np.errstate(over="ignore"):
+                x = {"abs": np.abs, "bitwise_not": np.invert}[op](regs[ins[1]])
+        else:
+            raise NotImplementedError(op)
+        regs.append(x)
+    return [regs[r].reshape(-1) for r in recipe["results"]]

@@ -16,6 +16,7 @@ import pytest
 import ask_b200
 from ask_b200 import recipes as R
 from ask_b200 import runtime as rt
+import recipe_eval
 
 
 def ttype(shape, dt):
@@ -440,6 +441,51 @@ def padded_concat_steps():
     y = s.op("slice", [pd], list(sl.shape), "i32", f"starts = {arr([1, 0])}, stops = {arr([10, 8])}, steps = {arr([3, 2])}")
     tr = s.op("transpose", [y], list(sl.T.shape), "i32", "permutation = " + arr([1, 0]))
     cases.append(("transposed_slice_of_padded_sum", s.text([tr]), [xv], [np.ascontiguousarray(sl.T)]))
+    # a strided slice of a concatenation of arguments, read through an elementwise op
+    s = Step()
+    a, b = s.arg([8, 1, 5], "i32"), s.arg([8, 2, 5], "i32")
+    c = s.op("concatenate", [a, b], [8, 3, 5], "i32", "axis = 1 : i64")
+    ab = s.op("abs", [c], [8, 3, 5], "i32")
+    y = s.op("slice", [ab], [4, 2, 5], "i32",
+             f"starts = {arr([0, 1, 0])}, stops = {arr([7, 3, 5])}, steps = {arr([2, 1, 1])}")
+    av, bv = rng.integers(-9, 9, (8, 1, 5)).astype(np.int32), rng.integers(-9, 9, (8, 2, 5)).astype(np.int32)
+    cases.append(("slice_of_concatenated_arguments", s.text([y]), [av, bv],
+                  [np.abs(np.concatenate([av, bv], axis=1))[0:7:2, 1:3, :]]))
+    # a pad of a padded computed value: the inner window and mask compose with the outer
+    s = Step()
+    x = s.arg([3, 2], "i32")
+    e = s.op("mul", [x, x], [3, 2], "i32")
+    p1 = s.op("pad", [e, s.splat(s.const(4, "i32"), [])], [6, 4], "i32",
+              f"pad_low = {arr([1, 0])}, pad_high = {arr([0, 1])}, interior = {arr([1, 0])}")
+    p2 = s.op("pad", [p1, s.splat(s.const(-2, "i32"), [])], [13, 7], "i32",
+              f"pad_low = {arr([0, 2])}, pad_high = {arr([2, 1])}, interior = {arr([1, 0])}")
+    xv = rng.integers(-9, 9, (3, 2)).astype(np.int32)
+    inner = np.full((6, 4), 4, np.int32)
+    inner[1::2, 0:2] = xv * xv
+    outer = np.full((13, 7), -2, np.int32)
+    outer[0:11:2, 2:6] = inner
+    cases.append(("pad_of_padded_product", s.text([p2]), [xv], [outer]))
+    # a concatenation holding a concatenation of arguments and a computed value
+    s = Step()
+    a, b = s.arg([2, 1, 4], "i32"), s.arg([2, 2, 4], "i32")
+    c = s.op("concatenate", [a, b], [2, 3, 4], "i32", "axis = 1 : i64")
+    d = s.op("slice", [s.splat(s.const(6, "i32"), [4, 4, 5])], [3, 3, 4], "i32",
+             f"starts = {arr([0, 0, 1])}, stops = {arr([3, 3, 5])}, steps = {arr([1, 1, 1])}")
+    y = s.op("concatenate", [c, d], [5, 3, 4], "i32", "axis = 0 : i64")
+    av, bv = rng.integers(-9, 9, (2, 1, 4)).astype(np.int32), rng.integers(-9, 9, (2, 2, 4)).astype(np.int32)
+    cases.append(("concatenation_of_a_concatenation", s.text([y]), [av, bv],
+                  [np.concatenate([np.concatenate([av, bv], axis=1), np.full((3, 3, 4), 6, np.int32)], axis=0)]))
+    # a slice that reaches into a high pad of an argument
+    s = Step()
+    x = s.arg([4, 3], "i32")
+    pd = s.op("pad", [x, s.splat(s.const(5, "i32"), [])], [4, 7], "i32",
+              f"pad_low = {arr([0, 0])}, pad_high = {arr([0, 4])}, interior = {arr([0, 0])}")
+    y = s.op("slice", [pd], [4, 3], "i32", f"starts = {arr([0, 1])}, stops = {arr([4, 7])}, steps = {arr([1, 2])}")
+    out = s.op("add", [y, s.splat(s.const(0, "i32"), [4, 3])], [4, 3], "i32")
+    xv = rng.integers(-9, 9, (4, 3)).astype(np.int32)
+    full = np.full((4, 7), 5, np.int32)
+    full[:, :3] = xv
+    cases.append(("slice_into_a_high_pad", s.text([out]), [xv], [full[:, 1:7:2]]))
     return cases
 
 
@@ -448,6 +494,15 @@ def test_pad_and_concatenate_of_computed_values_lower(case):
     name, src, ins, want = case
     out = rt.lower_step(src)
     assert ask_b200.Plan(out["recipe"], -1).describe()["kernel"] == "ew_view"
+
+
+@pytest.mark.parametrize("case", padded_concat_steps(), ids=lambda c: c[0])
+def test_pad_and_concatenate_of_computed_values_evaluate(case):
+    """The lowered recipe, evaluated on the CPU by the recipe evaluator, equals numpy."""
+    name, src, ins, want = case
+    out = rt.lower_step(src)
+    got = recipe_eval.evaluate(out["recipe"], [ins[a] for a in out["input_arguments"]])
+    assert np.array_equal(got[0].reshape(want[0].shape), want[0]), name
 
 
 @pytest.mark.gpu
@@ -686,6 +741,21 @@ def test_random_map_steps_lower():
     assert lowered >= 40, lowered
 
 
+def test_random_map_steps_evaluate():
+    """400 random steps: at least 95% lower, and every lowered recipe,
+    evaluated on the CPU by the recipe evaluator, equals numpy."""
+    lowered = 0
+    for seed in range(400):
+        out, args, want = _lower_random(seed)
+        if out is None:
+            continue
+        ask_b200.Plan(out["recipe"], -1)
+        got = recipe_eval.evaluate(out["recipe"], [args[a] for a in out["input_arguments"]])
+        assert np.array_equal(got[0].astype(np.int32), want.reshape(-1)), seed
+        lowered += 1
+    assert lowered >= 380, lowered
+
+
 @pytest.mark.gpu
 def test_random_map_steps_on_gpu(device):
     import torch
@@ -702,6 +772,106 @@ def test_random_map_steps_on_gpu(device):
         assert np.array_equal(y.cpu().numpy(), want.reshape(-1)), seed
         checked += 1
     assert checked >= 40
+
+
+def _factor_shape(rng, n):
+    """A random shape (rank 1..4) whose extents multiply to n."""
+    dims, left = [], n
+    for _ in range(int(rng.integers(0, 3))):
+        divs = [d for d in range(1, left + 1) if left % d == 0]
+        d = int(rng.choice(divs))
+        dims.append(d)
+        left //= d
+    dims.append(left)
+    return [int(x) for x in rng.permutation(dims)]
+
+
+def random_reshape_step(seed):
+    """An i32 argument read through a transpose, strided slice or broadcast,
+    then reshaped to a random shape of the same size, plus one.  Returns
+    (source, argument arrays, expected result)."""
+    rng = np.random.default_rng(seed)
+    s = Step()
+    shape = [int(x) for x in rng.integers(1, 6, int(rng.integers(2, 4)))]
+    kind = ["transpose", "slice", "broadcast"][seed % 3]
+    if kind == "transpose":
+        perm = [int(x) for x in rng.permutation(len(shape))]
+        src_shape = [0] * len(shape)
+        for d, p_ in enumerate(perm):
+            src_shape[p_] = shape[d]
+        x = s.arg(src_shape, "i32")
+        xv = rng.integers(-50, 50, src_shape).astype(np.int32)
+        v = s.op("transpose", [x], shape, "i32", "permutation = " + arr(perm))
+        vv = np.transpose(xv, perm)
+    elif kind == "slice":
+        steps = [int(rng.integers(1, 3)) for _ in shape]
+        starts = [int(rng.integers(0, 2)) for _ in shape]
+        src_shape = [st + (n - 1) * sp + 1 + int(rng.integers(0, 2)) for st, sp, n in zip(starts, steps, shape)]
+        stops = [st + (n - 1) * sp + 1 for st, sp, n in zip(starts, steps, shape)]
+        x = s.arg(src_shape, "i32")
+        xv = rng.integers(-50, 50, src_shape).astype(np.int32)
+        v = s.op("slice", [x], shape, "i32", f"starts = {arr(starts)}, stops = {arr(stops)}, steps = {arr(steps)}")
+        vv = xv[tuple(slice(a, b, c) for a, b, c in zip(starts, stops, steps))]
+    else:
+        keep = sorted(set(int(d) for d in rng.choice(len(shape), int(rng.integers(1, len(shape))), replace=False)))
+        src_shape = [shape[d] for d in keep]
+        x = s.arg(src_shape, "i32")
+        xv = rng.integers(-50, 50, src_shape).astype(np.int32)
+        v = s.op("broadcast_in_dim", [x], shape, "i32", f"dimensions = {arr(keep)}, shape = {arr(shape)}")
+        vv = np.broadcast_to(xv.reshape([shape[d] if d in keep else 1 for d in range(len(shape))]), shape)
+    to = _factor_shape(rng, int(np.prod(shape)))
+    r = s.op("reshape", [v], to, "i32", f"shape = {arr(to)}")
+    y = s.op("add", [r, s.splat(s.const(1, "i32"), to)], to, "i32")
+    nocopy = vv.view()
+    try:
+        nocopy.shape = to  # numpy refuses when the reshape would need a copy
+    except AttributeError:
+        nocopy = None
+    return s.text([y]), [xv], np.ascontiguousarray(vv).reshape(to) + 1, nocopy is not None
+
+
+def _lower_reshape(seed):
+    src, args, want, strided = random_reshape_step(seed)
+    try:
+        return rt.lower_step(src), args, want, strided
+    except rt.CUDAError as e:
+        assert e.status == ask_b200.E_UNSUPPORTED, str(e)
+        return None, args, want, strided
+
+
+def test_reshapes_of_views_evaluate():
+    """A reshape of a transposed, sliced or broadcast argument lowers to one
+    strided view exactly when numpy can reshape that view without a copy (the
+    axes merged or split nest in memory); each one that lowers equals numpy."""
+    lowered = 0
+    for seed in range(300):
+        out, args, want, strided = _lower_reshape(seed)
+        assert (out is not None) == strided, seed
+        if out is None:
+            continue
+        ask_b200.Plan(out["recipe"], -1)
+        got = recipe_eval.evaluate(out["recipe"], [args[a] for a in out["input_arguments"]])
+        assert np.array_equal(got[0], want.reshape(-1)), seed
+        lowered += 1
+    assert lowered >= 100, lowered
+
+
+@pytest.mark.gpu
+def test_reshapes_of_views_on_gpu(device):
+    import torch
+    checked = 0
+    for seed in range(120):
+        out, args, want, _ = _lower_reshape(seed)
+        if out is None:
+            continue
+        plan = ask_b200.Plan(out["recipe"], 0)
+        dev_in = [torch.from_numpy(np.ascontiguousarray(args[a])).cuda() for a in out["input_arguments"]]
+        y = torch.empty(want.size, dtype=torch.int32, device="cuda")
+        plan.launch(dev_in, [y], None, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        assert np.array_equal(y.cpu().numpy(), want.reshape(-1)), seed
+        checked += 1
+    assert checked >= 60, checked
 
 
 def random_reduce_step(seed):
