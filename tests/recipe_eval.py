@@ -1,4 +1,4 @@
-"""A numpy evaluator for lowered integer elementwise recipes (test helper).
+"""A numpy evaluator for lowered integer recipes (test helper).
 
 The lowering adapter turns a step source into a recipe whose program reads
 its inputs through index maps ("full", "scalar", "view") and may read the
@@ -15,7 +15,7 @@ import numpy as np
 _NP = {"i32": np.int32, "i64": np.int64, "bool": np.bool_, "i8": np.int8, "i16": np.int16}
 
 
-def _input(port, arr, shape, inner):
+def _input(port, arr, shape, inner, reduce_dims=None):
     m = port.get("map", "full")
     flat = np.ascontiguousarray(arr).reshape(-1)
     if m == "scalar":
@@ -24,6 +24,9 @@ def _input(port, arr, shape, inner):
         return flat.reshape(shape)
     if m in ("outer", "inner"):
         i = np.arange(int(np.prod(shape)), dtype=np.int64)
+        if reduce_dims:  # a reduction's outer port holds one value per output (o, i)
+            _, e, n = reduce_dims
+            return flat[(i // (e * n)) * n + i % n].reshape(shape)
         return flat[i // inner if m == "outer" else i % inner].reshape(shape)
     if m != "view":
         raise NotImplementedError(m)
@@ -41,10 +44,45 @@ def _input(port, arr, shape, inner):
     return out
 
 
+def _reduce(recipe, values):
+    """Reductions of an integer reduce recipe: each value is viewed as
+    [outer, extent, inner] and folded over the middle axis (sums wrap in the
+    value's type; arg positions are the first extreme plus index_base)."""
+    o, e, i = recipe["outer"], recipe["extent"], recipe["inner"]
+    out = []
+    for r in recipe["reductions"]:
+        v = values[r["value"]].reshape(o, e, i)
+        op = r["op"]
+        if op == "reduce_sum":
+            x = v.sum(axis=1, dtype=np.int64).astype(v.dtype)
+        elif op == "reduce_prod":
+            x = v.prod(axis=1, dtype=np.int64).astype(v.dtype)
+        elif op in ("reduce_max", "reduce_any"):
+            x = v.max(axis=1)
+        elif op in ("reduce_min", "reduce_all"):
+            x = v.min(axis=1)
+        elif op in ("argmax", "argmin"):
+            x = (np.argmax(v, axis=1) if op == "argmax" else np.argmin(v, axis=1)).astype(np.int64)
+            x = x + int(recipe.get("index_base", 0))
+        else:
+            raise NotImplementedError(op)
+        out.append(x.reshape(-1))
+    return out
+
+
 def evaluate(recipe, inputs):
-    """Outputs (flat numpy arrays) of an integer elementwise recipe."""
+    """Outputs (flat numpy arrays) of an integer elementwise or reduce recipe."""
+    if recipe["family"] == "reduce":
+        shape = tuple(recipe.get("shape") or [recipe["outer"], recipe["extent"], recipe["inner"]])
+        values = _program(dict(recipe, shape=list(shape)), inputs, shape)
+        return _reduce(recipe, [v.reshape(-1) for v in values])
     assert recipe["family"] == "elementwise"
     shape = tuple(recipe.get("shape") or [recipe["count"]])
+    return [v.reshape(-1) for v in _program(recipe, inputs, shape)]
+
+
+def _program(recipe, inputs, shape):
+    """The program's result arrays over the iteration shape."""
     regs = []
     for ins in recipe["program"]:
         op = ins[0]
@@ -52,7 +90,8 @@ def evaluate(recipe, inputs):
             t = _NP[ins[1]]
             x = np.full(shape, ins[2], dtype=t)
         elif op == "input":
-            x = _input(recipe["inputs"][ins[1]], inputs[ins[1]], shape, int(recipe.get("inner", 1)))
+            dims = (recipe["outer"], recipe["extent"], recipe["inner"]) if recipe["family"] == "reduce" else None
+            x = _input(recipe["inputs"][ins[1]], inputs[ins[1]], shape, int(recipe.get("inner", 1)), dims)
         elif op == "coord":
             x = np.indices(shape, dtype=np.int64)[ins[1]]
         elif op == "select":
@@ -74,4 +113,4 @@ def evaluate(recipe, inputs):
         else:
             raise NotImplementedError(op)
         regs.append(x)
-    return [regs[r].reshape(-1) for r in recipe["results"]]
+    return [regs[r] for r in recipe["results"]]

@@ -921,6 +921,17 @@ def _lower_random_reduce(seed):
         return None, args, want
 
 
+def test_random_reduce_steps_evaluate():
+    """Every random reduction lowers, and its recipe, evaluated on the CPU by
+    the recipe evaluator, gives numpy's sums, extremes and first arg positions."""
+    for seed in range(200):
+        out, args, want = _lower_random_reduce(seed)
+        assert out is not None, seed
+        got = recipe_eval.evaluate(out["recipe"], [args[a] for a in out["input_arguments"]])
+        for k, (g, w) in enumerate(zip(got, want)):
+            assert np.array_equal(g, w.reshape(-1)), (seed, k)
+
+
 def test_random_reduce_steps_lower():
     lowered = 0
     for seed in range(40):
