@@ -1048,6 +1048,46 @@ class Lowering {
     *map = prefix ? "outer" : "inner";
     return true;
   }
+  // An elementwise view whose addresses follow one of the fast maps: element 0
+  // everywhere ("scalar"), the output's flat index divided by `inner`
+  // ("outer": row-major over the leading axes, constant over the rest) or
+  // modulo `inner` ("inner": constant over the leading axes) -- e.g. a
+  // rank-preserving broadcast of a [rows, 1] column or a [1, cols] row.
+  // Size-1 axes take no part.
+  bool fast_map(const ArgView& w, std::string* map) {
+    const size_t r = out_shape_.size();
+    if (is_reduce_ || w.offset != 0) return false;
+    for (size_t d = 0; d < r; ++d)
+      if (w.windowed(d)) return false;
+    auto nested = [&](size_t a, size_t b) {  // row-major strides over axes [a, b)
+      int64_t expect = 1;
+      for (size_t d = b; d-- > a;) {
+        if (out_shape_[d] == 1) continue;
+        if (w.stride[d] != expect) return false;
+        expect *= out_shape_[d];
+      }
+      return true;
+    };
+    auto constant = [&](size_t a, size_t b) {
+      for (size_t d = a; d < b; ++d)
+        if (out_shape_[d] != 1 && w.stride[d] != 0) return false;
+      return true;
+    };
+    if (constant(0, r)) {
+      *map = "scalar";
+      return true;
+    }
+    for (size_t k = 1; k < r; ++k) {
+      const bool outer = nested(0, k) && constant(k, r), inner = constant(0, k) && nested(k, r);
+      if (!outer && !inner) continue;
+      const uint64_t n = product(out_shape_, k, r);
+      if (map_inner_ && map_inner_ != n) continue;
+      map_inner_ = n;
+      *map = outer ? "outer" : "inner";
+      return true;
+    }
+    return false;
+  }
   int coord(int64_t axis) {
     uses_shape_ = true;
     return emit_shared("[\"coord\"," + std::to_string(axis) + "]", "i64");
@@ -1096,6 +1136,8 @@ class Lowering {
         id = use_port(w.arg, "full");
       } else if (n == "broadcast_in_dim" && arg_.count(p->operands.at(0)) &&
                  simple_broadcast(at, arr(*p, "dimensions"), &map)) {
+        id = use_port(w.arg, map);
+      } else if (fast_map(w, &map)) {
         id = use_port(w.arg, map);
       } else {
         id = use_view(w);

@@ -8,11 +8,12 @@ interpreter (a view port reads element offset + sum((c - lo) / step * stride)
 where every axis has c - lo >= 0, divisible by step, (c - lo) / step < extent,
 else its pad constant), so the lowering's translation can be checked against
 numpy on the CPU.  Only the integer and bool instructions that lowered index
-maps and integer programs use are supported; anything else raises.
+maps and integer programs use (plus f32 add, mul, maximum and minimum, exact
+on small integers) are supported; anything else raises.
 """
 import numpy as np
 
-_NP = {"i32": np.int32, "i64": np.int64, "bool": np.bool_, "i8": np.int8, "i16": np.int16}
+_NP = {"i32": np.int32, "i64": np.int64, "bool": np.bool_, "i8": np.int8, "i16": np.int16, "f32": np.float32}
 
 
 def _input(port, arr, shape, inner, reduce_dims=None):

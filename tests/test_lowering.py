@@ -874,6 +874,59 @@ def test_reshapes_of_views_on_gpu(device):
     assert checked >= 45, checked
 
 
+def broadcast_steps():
+    """Rank-preserving broadcasts (a [rows, 1] column, a [1, cols] row, a
+    [1, 1] scalar, a transposed column) added to a full argument, f32: these
+    read through the fast vector maps, not the view interpreter."""
+    rng = np.random.default_rng(9)
+    cases = []
+    for name, bshape, dims, want_map in (("column", [32, 1], [0, 1], "outer"), ("row", [1, 64], [0, 1], "inner"),
+                                         ("scalar", [1, 1], [0, 1], "scalar"), ("row_rank3", [1, 1, 64], [0, 1, 2], "inner"),
+                                         ("column_rank3", [2, 16, 1], [0, 1, 2], "outer")):
+        shape = [32, 64] if len(bshape) == 2 else [2, 16, 64]
+        s = Step()
+        x, b = s.arg(shape, "f32"), s.arg(bshape, "f32")
+        bc = s.op("broadcast_in_dim", [b], shape, "f32", f"dimensions = {arr(dims)}, shape = {arr(shape)}")
+        y = s.op("add", [x, bc], shape, "f32")
+        xv = rng.integers(-50, 50, shape).astype(np.float32)
+        bv = rng.integers(-50, 50, bshape).astype(np.float32)
+        cases.append((name, s.text([y]), [xv, bv], xv + bv, want_map))
+    # a [64, 1] column read through a transpose as a row of the [32, 64] output
+    s = Step()
+    x, b = s.arg([32, 64], "f32"), s.arg([64, 1], "f32")
+    t = s.op("transpose", [b], [1, 64], "f32", "permutation = " + arr([1, 0]))
+    bc = s.op("broadcast_in_dim", [t], [32, 64], "f32", f"dimensions = {arr([0, 1])}, shape = {arr([32, 64])}")
+    y = s.op("add", [x, bc], [32, 64], "f32")
+    xv = rng.integers(-50, 50, (32, 64)).astype(np.float32)
+    bv = rng.integers(-50, 50, (64, 1)).astype(np.float32)
+    cases.append(("transposed_column_as_row", s.text([y]), [xv, bv], xv + bv.T, "inner"))
+    return cases
+
+
+@pytest.mark.parametrize("case", broadcast_steps(), ids=lambda c: c[0])
+def test_rank_preserving_broadcasts_use_fast_maps(case):
+    name, src, ins, want, want_map = case
+    out = rt.lower_step(src)
+    assert [p["map"] for p in out["recipe"]["inputs"]] == ["full", want_map]
+    assert ask_b200.Plan(out["recipe"], -1).describe()["kernel"] == "ew_generic"
+    got = recipe_eval.evaluate(out["recipe"], [ins[a] for a in out["input_arguments"]])
+    assert np.array_equal(got[0].reshape(want.shape), want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", broadcast_steps(), ids=lambda c: c[0])
+def test_rank_preserving_broadcasts_on_gpu(device, case):
+    import torch
+    name, src, ins, want, _ = case
+    out = rt.lower_step(src)
+    plan = ask_b200.Plan(out["recipe"], 0)
+    dev_in = [torch.from_numpy(np.ascontiguousarray(ins[a])).cuda() for a in out["input_arguments"]]
+    y = torch.empty(want.size, dtype=torch.float32, device="cuda")
+    plan.launch(dev_in, [y], None, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy().reshape(want.shape), want), name
+
+
 def random_reduce_step(seed):
     """A random map-and-elementwise i32 operand reduced over a random block of
     contiguous axes with sum, max, min and argmax (argmax over a single axis)."""
