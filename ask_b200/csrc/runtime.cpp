@@ -9,7 +9,10 @@
 //     device work; submit validates every public port before enqueueing;
 //   - a workspace (one set of slots, plus a CUDA graph in graph mode) is busy
 //     from its submission until that submission's event completes; an idle
-//     one is reused, otherwise a new one is allocated (CUDA.cpp:921-955);
+//     one is reused, otherwise a new one is allocated (CUDA.cpp:921-955) --
+//     except that a program without internal buffers reuses its one
+//     workspace while earlier submissions still run (stream order keeps its
+//     graph's launches and updates apart), instead of building a new graph;
 //   - counters: allocations, launches (steps enqueued), program_submissions,
 //     workspace_reuses, prepared_internal_slots/bytes, graph_instantiations,
 //     graph_launches, graph_nodes, graph_edges, graph_node_updates.
@@ -816,6 +819,11 @@ std::shared_ptr<EventImpl> enqueue(const std::shared_ptr<State>& stp, const std:
     return std::shared_ptr<Workspace>();
   };
   ws = idle();
+  // A program without internal buffers keeps one workspace: nothing of an
+  // earlier submission lives in it but its graph, and a graph is launched and
+  // updated in stream order (an update affects later launches only), so a
+  // submission need not wait for -- or rebuild beside -- one still running.
+  if (!ws && p.capacity.empty() && !p.workspaces.empty()) ws = p.workspaces.front();
   if (!ws || st.pending.size() >= 64) {
     reap(st);
     if (!ws) ws = idle();

@@ -116,6 +116,34 @@ def test_chain_uses_two_slots_and_reuses_its_workspace(device, graph):
 
 
 @pytest.mark.parametrize("graph", [False, True])
+def test_slot_free_program_keeps_one_workspace_in_flight(device, graph):
+    """A program without internal buffers reuses its one workspace while
+    earlier submissions still run: 40 submissions without waiting, cycling
+    through four input/output pairs (so graph nodes are re-recorded while
+    earlier launches of the same graph are queued), each result exact, one
+    graph instantiated."""
+    session = rt.Session.create(0)
+    n = 1 << 20
+    step = rt.PlanStep(double_i32(n), [0], [1])
+    program = session.prepareProgram([4 * n, 4 * n], [0], [1], [step], graph)
+    assert program.describe()["slot_capacity_bytes"] == []
+    rng = np.random.default_rng(3)
+    data = [rng.integers(-1000, 1000, n).astype(np.int32) for _ in range(4)]
+    srcs = [session.allocate(4 * n) for _ in range(4)]
+    dsts = [session.allocate(4 * n) for _ in range(4)]
+    for src, d in zip(srcs, data):
+        src.copyFromHost(d)
+    events = [program.submit([srcs[k % 4]], [dsts[k % 4]]) for k in range(40)]
+    events[-1].wait()
+    for dst, d in zip(dsts, data):
+        assert np.array_equal(i32s(dst), d * 2)
+    st = session.stats()
+    assert st["program_submissions"] == 40 and st["workspace_reuses"] == 39
+    if graph:
+        assert st["graph_instantiations"] == 1 and st["graph_launches"] == 40
+
+
+@pytest.mark.parametrize("graph", [False, True])
 def test_pre_copy(device, graph):
     session = rt.Session.create(0)
     with pytest.raises(rt.CUDAError):
