@@ -47,7 +47,13 @@ __device__ __forceinline__ uint4 ld_cached_v4(const void* p) { return __ldg(stat
 // prefetching, default write-back stores, an asynchronous-copy ring through
 // shared memory, smaller grids, and skipping the index division when outer is 1
 // were each slower than this -- 1.83 to 2.04 ms against 1.73 ms.  Issuing the
-// table-row loads sooner appears to cost L1 hits on the hot rows.)
+// table-row loads sooner appears to cost L1 hits on the hot rows.  A ring of
+// whole-row bulk copies (cp.async.bulk global -> shared -> global, one issuing
+// thread per 32-thread CTA, mbarrier per stage) took 1.89 ms with 16 stages
+// and stores 8 rows behind, and 3.52 ms with 32 stages at half the CTAs: each
+// CTA refills a stage only after the bulk store that read it has finished
+// reading shared memory, which under the 8 GiB write stream capped every CTA
+// near 2.5 rows per microsecond.  Register stores do not hold the stage.)
 __global__ void __launch_bounds__(kIdxThreads) gather_rows_vec(const __grid_constant__ IndexArgs a, uint32_t vecs) {
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t warp = (uint64_t(blockIdx.x) * kIdxThreads + threadIdx.x) >> 5;
