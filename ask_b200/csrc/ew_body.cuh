@@ -66,22 +66,72 @@ __device__ __forceinline__ void ew_spec_loop(const EwArgs& args, int aligned) {
   }
 }
 
-// One element per thread iteration: the element's coordinates in the iteration
-// shape are computed once, every IM_VIEW port maps them through its view, and
+// ---- general index maps ------------------------------------------------------------
+// The coordinates of linear index i in the iteration shape (row-major).
+__device__ __forceinline__ void view_coords(uint64_t i, const ViewSet& views, int64_t (&c)[kMaxRank]) {
+  for (int d = views.rank - 1; d >= 0; --d) {
+    const uint64_t e = views.shape[d];
+    c[d] = int64_t(i % e);
+    i /= e;
+  }
+}
+
+// The mixed-radix digits of a stride, the leading one not reduced.
+__device__ __forceinline__ void view_stride_digits(uint64_t stride, const ViewSet& views, int64_t (&by)[kMaxRank]) {
+  for (int d = views.rank - 1; d > 0; --d) {
+    const uint64_t e = views.shape[d];
+    by[d] = int64_t(stride % e);
+    stride /= e;
+  }
+  if (views.rank > 0) by[0] = int64_t(stride);
+}
+
+// c += the mixed-radix digits `by` of a fixed stride, with carries: the
+// coordinates of i + stride without a division.  The leading axis takes no
+// modulus (it only leaves its range once i + stride is past the end).
+__device__ __forceinline__ void view_advance(int64_t (&c)[kMaxRank], const int64_t (&by)[kMaxRank],
+                                             const ViewSet& views) {
+  int64_t carry = 0;
+  for (int d = views.rank - 1; d > 0; --d) {
+    const int64_t e = int64_t(views.shape[d]), x = c[d] + by[d] + carry;
+    carry = x >= e;
+    c[d] = carry ? x - e : x;
+  }
+  if (views.rank > 0) c[0] += by[0] + carry;
+}
+
+// An IM_VIEW port's element at coordinates c, or its pad outside the window:
+// per axis q = (c - lo) / step must be a whole number in [0, extent).
+__device__ __forceinline__ uint64_t view_read(const PortView& v, int rank, const int64_t (&c)[kMaxRank], int type,
+                                              const void* p) {
+  int64_t off = v.offset;
+  bool ok = true;
+  for (int d = 0; d < rank; ++d) {
+    const int64_t q0 = c[d] - v.lo[d], st = v.step[d];
+    const int64_t q = st == 1 ? q0 : q0 / st;
+    ok = ok && q0 >= 0 && (st == 1 || q * st == q0) && q < v.extent[d];
+    off += q * v.stride[d];
+  }
+  return ok ? word_from_storage(type, p, uint64_t(off)) : v.pad;
+}
+
+// One element per thread iteration (grid-stride): the element's coordinates
+// in the iteration shape are advanced by the grid's stride with carries (no
+// division per element), every IM_VIEW port maps them through its view, and
 // OP_COORD reads them.  Scalar loads and stores; this path serves the index
-// maps the fused kernels above have no vector form for.
+// maps the fused kernels above have no vector form for.  (Four elements per
+// thread with the generic kernel's vector loads and stores measured no
+// faster: the interpreter's latency and the views' scattered reads bound it.)
 __device__ __forceinline__ void ew_view_loop(const Program& prog, const EwArgs& args, const ViewSet& views) {
   const uint64_t n = args.count;
   const uint64_t nthreads = uint64_t(gridDim.x) * kEwThreads;
   uint64_t r[kMaxRegs];
-  for (uint64_t i = uint64_t(blockIdx.x) * kEwThreads + threadIdx.x; i < n; i += nthreads) {
-    int64_t c[kMaxRank];
-    uint64_t rest = i;
-    for (int d = views.rank - 1; d >= 0; --d) {
-      const uint64_t e = views.shape[d];
-      c[d] = int64_t(rest % e);
-      rest /= e;
-    }
+  uint64_t i = uint64_t(blockIdx.x) * kEwThreads + threadIdx.x;
+  if (i >= n) return;
+  int64_t c[kMaxRank], by[kMaxRank];
+  view_coords(i, views, c);
+  view_stride_digits(nthreads, views, by);
+  for (; i < n; i += nthreads, view_advance(c, by, views)) {
     for (int k = 0; k < prog.n_insn; ++k) {
       const Insn& ins = prog.insn[k];
       if (ins.op == OP_INPUT) {
@@ -91,19 +141,7 @@ __device__ __forceinline__ void ew_view_loop(const Program& prog, const EwArgs& 
           case IM_SCALAR: r[ins.dst] = word_from_storage(t, p, 0); break;
           case IM_OUTER: r[ins.dst] = word_from_storage(t, p, i / args.inner.d); break;
           case IM_INNER: r[ins.dst] = word_from_storage(t, p, i % args.inner.d); break;
-          case IM_VIEW: {
-            const PortView& v = views.port[port];
-            int64_t off = v.offset;
-            bool ok = true;
-            for (int d = 0; d < views.rank; ++d) {
-              const int64_t s = c[d] - v.lo[d];
-              const int64_t q = s / v.step[d];
-              ok = ok && s >= 0 && q * v.step[d] == s && q < v.extent[d];
-              off += q * v.stride[d];
-            }
-            r[ins.dst] = ok ? word_from_storage(t, p, uint64_t(off)) : v.pad;
-            break;
-          }
+          case IM_VIEW: r[ins.dst] = view_read(views.port[port], views.rank, c, t, p); break;
           default: r[ins.dst] = word_from_storage(t, p, i); break;
         }
       } else if (ins.op == OP_COORD) {

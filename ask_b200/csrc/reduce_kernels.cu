@@ -38,6 +38,7 @@
 #include "pdl.cuh"
 #include "reduce_acc.cuh"
 #include "reduce_fast.cuh"
+#include "ew_body.cuh"
 
 namespace askb {
 
@@ -213,8 +214,9 @@ __global__ void __launch_bounds__(kRedThreads)
 }
 
 // General index maps (RS_VIEW): a warp per output (o, n); lanes stride the
-// reduced extent.  Each element's coordinates in the step's iteration shape
-// are computed once; IM_VIEW ports map them through their view (transpose,
+// reduced extent.  A lane's coordinates in the step's iteration shape are
+// computed once per output and advanced by its stride (32 elements of the
+// extent) with carries; IM_VIEW ports map them through their view (transpose,
 // slice, pad, general broadcast of an argument) and OP_COORD reads them, as in
 // the elementwise view loop.  Scalar loads: this path serves coverage, the
 // benchmark reductions read full, outer or scalar ports.
@@ -227,19 +229,16 @@ __global__ void __launch_bounds__(kRedThreads)
   const uint64_t nwarps = (uint64_t(gridDim.x) * kRedThreads) >> 5;
   const uint64_t n_outputs = a.outer * a.inner;
   uint64_t r[kMaxRegs];
+  int64_t by[kMaxRank];  // a lane's step e += 32 moves the linear index by 32 * inner
+  ew::view_stride_digits(32 * a.inner, views, by);
   for (uint64_t o_idx = warp; o_idx < n_outputs; o_idx += nwarps) {
     const uint64_t o = o_idx / a.inner, n = o_idx % a.inner;
     Accs s;
     accs_init(a, s);
-    for (uint64_t e = lane; e < a.extent; e += 32) {
+    int64_t c[kMaxRank];
+    if (lane < a.extent) ew::view_coords((o * a.extent + lane) * a.inner + n, views, c);
+    for (uint64_t e = lane; e < a.extent; e += 32, ew::view_advance(c, by, views)) {
       const uint64_t i = (o * a.extent + e) * a.inner + n;
-      int64_t c[kMaxRank];
-      uint64_t rest = i;
-      for (int d = views.rank - 1; d >= 0; --d) {
-        const uint64_t ext = views.shape[d];
-        c[d] = int64_t(rest % ext);
-        rest /= ext;
-      }
       for (int k = 0; k < prog.n_insn; ++k) {
         const Insn& ins = prog.insn[k];
         if (ins.op == OP_INPUT) {
@@ -248,19 +247,7 @@ __global__ void __launch_bounds__(kRedThreads)
           switch (prog.in_map[port]) {
             case IM_SCALAR: r[ins.dst] = word_from_storage(t, p, 0); break;
             case IM_OUTER: r[ins.dst] = word_from_storage(t, p, o_idx); break;
-            case IM_VIEW: {
-              const PortView& v = views.port[port];
-              int64_t off = v.offset;
-              bool ok = true;
-              for (int d = 0; d < views.rank; ++d) {
-                const int64_t q0 = c[d] - v.lo[d];
-                const int64_t q = q0 / v.step[d];
-                ok = ok && q0 >= 0 && q * v.step[d] == q0 && q < v.extent[d];
-                off += q * v.stride[d];
-              }
-              r[ins.dst] = ok ? word_from_storage(t, p, uint64_t(off)) : v.pad;
-              break;
-            }
+            case IM_VIEW: r[ins.dst] = ew::view_read(views.port[port], views.rank, c, t, p); break;
             default: r[ins.dst] = word_from_storage(t, p, i); break;
           }
         } else if (ins.op == OP_COORD) {
