@@ -295,11 +295,14 @@ def reduce_view_steps():
 
 @pytest.mark.parametrize("case", reduce_view_steps(), ids=lambda c: c[0])
 def test_reductions_over_index_maps_lower_to_the_view_kernel(case):
+    """Reductions read index maps through the view kernel (a transposed
+    operand whose reduction would be a column reduction of the argument
+    included: that kernel is slower for it)."""
     name, src, ins, want = case
     out = rt.lower_step(src)
     r = out["recipe"]
-    assert r["family"] == "reduce" and "shape" in r
     d = ask_b200.Plan(r, -1).describe()
+    assert r["family"] == "reduce" and "shape" in r
     assert d["kernel"] == "reduce_view" and d["strategy"] == "view"
 
 
@@ -925,6 +928,76 @@ def test_rank_preserving_broadcasts_on_gpu(device, case):
     plan.launch(dev_in, [y], None, torch.cuda.current_stream())
     torch.cuda.synchronize()
     assert np.array_equal(y.cpu().numpy().reshape(want.shape), want), name
+
+
+def permuted_reduce_step(seed):
+    """An i32 argument read through a random axis permutation (plus one) and
+    reduced over a random block of axes with sum, max, min and, over one axis,
+    argmax.  Returns (source, [argument], expected results, whether the
+    reduction maps onto the argument's own axes)."""
+    rng = np.random.default_rng(seed)
+    rank = int(rng.integers(2, 5))
+    ashape = [int(x) for x in rng.integers(2, 7, rank)]
+    perm = [int(x) for x in rng.permutation(rank)]
+    tshape = [ashape[p_] for p_ in perm]
+    a0 = int(rng.integers(0, rank))
+    a1 = a0 + 1 if rng.random() < 0.6 else int(rng.integers(a0 + 1, rank + 1))
+    axes = list(range(a0, a1))
+    s = Step()
+    x = s.arg(ashape, "i32")
+    t = s.op("transpose", [x], tshape, "i32", "permutation = " + arr(perm))
+    y = s.op("add", [t, s.splat(s.const(1, "i32"), tshape)], tshape, "i32")
+    kept_shape = [d for k, d in enumerate(tshape) if k not in axes]
+    ot = ttype(kept_shape, "i32")
+    outs = [s.op(op, [y], kept_shape, "i32", "axes = " + arr(axes)) for op in ("reduce_sum", "reduce_max", "reduce_min")]
+    xv = rng.integers(-50, 50, ashape).astype(np.int32)
+    yv = np.transpose(xv, perm) + 1
+    want = [yv.sum(axis=tuple(axes)).astype(np.int32), yv.max(axis=tuple(axes)), yv.min(axis=tuple(axes))]
+    if len(axes) == 1:
+        outs.append(s.op("argmax", [y], kept_shape, "i64", f"axis = {a0} : i64"))
+        want.append(np.argmax(yv, axis=a0))
+    red = sorted(perm[k] for k in axes)
+    kept = [perm[k] for k in range(rank) if k not in axes]
+    last = max(k for k in range(rank) if ashape[k] != 1) if any(d != 1 for d in ashape) else -1
+    trailing = red[-1] == last
+    identity = [perm[k] for k in range(rank) if ashape[perm[k]] != 1] == sorted(perm[k] for k in range(rank) if ashape[perm[k]] != 1)
+    maps = identity or (red == list(range(red[0], red[-1] + 1)) and kept == sorted(kept) and trailing)
+    return s.text(outs), [xv], want, maps
+
+
+def test_permuted_reductions_read_the_arguments_axes():
+    """A reduction of a transposed argument lowers over the argument's own
+    layout (full ports, the row or split kernels) exactly when the reduced
+    axes form the argument's trailing block of axes and the kept axes keep
+    their order; every result equals numpy's."""
+    rewritten = 0
+    for seed in range(300):
+        src, args, want, maps = permuted_reduce_step(seed)
+        out = rt.lower_step(src)
+        strategy = ask_b200.Plan(out["recipe"], -1).describe()["strategy"]
+        assert (strategy != "view") == maps, seed
+        rewritten += maps
+        got = recipe_eval.evaluate(out["recipe"], [args[a] for a in out["input_arguments"]])
+        for k, (g, w) in enumerate(zip(got, want)):
+            assert np.array_equal(g, w.reshape(-1)), (seed, k)
+    assert rewritten >= 60, rewritten
+
+
+@pytest.mark.gpu
+def test_permuted_reductions_on_gpu(device):
+    import torch
+    for seed in range(80):
+        src, args, want, _ = permuted_reduce_step(seed)
+        out = rt.lower_step(src)
+        plan = ask_b200.Plan(out["recipe"], 0)
+        dev_in = [torch.from_numpy(np.ascontiguousarray(args[a])).cuda() for a in out["input_arguments"]]
+        kinds = {"i32": torch.int32, "i64": torch.int64}
+        outs = [torch.empty(p["elements"], dtype=kinds[p["element_type"]], device="cuda")
+                for p in plan.describe()["port_map"][len(dev_in):]]
+        plan.launch(dev_in, outs, None, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        for k, (g, w) in enumerate(zip(outs, want)):
+            assert np.array_equal(g.cpu().numpy(), w.reshape(-1)), (seed, k)
 
 
 def random_reduce_step(seed):
