@@ -106,6 +106,11 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
 // Combine `n` records per reduction laid out [n][n_red] into the outputs.
 cudaError_t red_combine_records(const RedArgs& args, const RedPartial* records, int n, cudaStream_t stream);
 size_t red_split_scratch_bytes(int grid, int n_red);
+// RS_COLUMN with few outputs: grid.y = chunks of the extent, one partial
+// record per (output, chunk) in scratch, then a combine in chunk order.
+cudaError_t red_column_chunks_launch(const Program& prog, const RedArgs& args, int grid, int chunks, void* scratch,
+                                     cudaStream_t stream);
+size_t red_column_chunks_scratch_bytes(uint64_t n_outputs, int chunks, int n_red);
 
 // ---- family G / X: gather and scatter_add over [outer, D, inner] ------------------
 struct IndexArgs {

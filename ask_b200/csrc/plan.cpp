@@ -682,6 +682,23 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   pl.grid = int(std::max<uint64_t>(1, std::min(needed, cap)));
   pl.launches = n_outputs ? (pl.strategy == RS_SPLIT ? 2 : 1) : 0;
   pl.scratch = 0;
+  pl.col_chunks = 1;
+  if (pl.strategy == RS_COLUMN && n_outputs && extent >= 64) {
+    // Too few columns to fill the GPU: split the extent into chunks (grid.y)
+    // of at least 32 elements, none empty.
+    const uint64_t threads = cap * uint64_t(kRedThreads);
+    if (n_outputs * 2 <= threads) {
+      uint64_t chunks = std::min<uint64_t>({(threads + n_outputs - 1) / n_outputs, extent / 32, 1024});
+      if (chunks > 1) {
+        const uint64_t per = (extent + chunks - 1) / chunks;
+        chunks = (extent + per - 1) / per;
+        pl.col_chunks = int(chunks);
+        pl.launches = 2;
+        pl.kernel = std::string("reduce_column_chunks_") + spec_names[pl.spec];
+        pl.scratch = red_column_chunks_scratch_bytes(n_outputs, pl.col_chunks, a.n_red);
+      }
+    }
+  }
   if (pl.strategy == RS_SPLIT) {
     const size_t part = red_split_scratch_bytes(pl.grid, a.n_red) * size_t(outer);
     pl.record_offset = (part + 255) & ~size_t(255);
@@ -749,7 +766,7 @@ std::string describe(const ask_b200_plan& pl) {
   std::ostringstream o;
   o << "{\"format\":\"ask-b200-recipe\",\"abi_version\":" << ASK_B200_ABI_VERSION << ",\"family\":\""
     << kFamilyNames[pl.family] << "\",\"kernel\":\"" << pl.kernel << "\",\"device\":" << pl.device
-    << ",\"target\":{\"backend\":\"cuda\",\"arch\":100},\"launch\":{\"grid\":[" << pl.grid << ",1,1],\"block\":["
+    << ",\"target\":{\"backend\":\"cuda\",\"arch\":100},\"launch\":{\"grid\":[" << pl.grid << "," << pl.col_chunks << ",1],\"block\":["
     << (pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? kRedThreads :
         pl.family == FAM_SOFTMAX ? pl.block : 256)
     << ",1,1],\"shared_bytes\":0},\"kernels_per_launch\":" << pl.launches << ",\"scratch_bytes\":" << pl.scratch;
@@ -865,8 +882,14 @@ void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratc
         }
       }
       for (size_t k = 0; k < pl.outputs.size(); ++k) a.out[k] = reinterpret_cast<void*>(ports[ni + k]);
-      if (pl.strategy == RS_SPLIT && !scratch) fail(ASK_B200_E_INVALID, "this plan needs scratch memory");
+      if ((pl.strategy == RS_SPLIT || pl.col_chunks > 1) && !scratch)
+        fail(ASK_B200_E_INVALID, "this plan needs scratch memory");
       if (scratch && !aligned16(scratch)) fail(ASK_B200_E_INVALID, "scratch must be 16-byte aligned");
+      if (pl.col_chunks > 1) {
+        check_cuda(red_column_chunks_launch(pl.prog, a, pl.grid, pl.col_chunks, reinterpret_cast<void*>(scratch), st),
+                   "reduce launch");
+        break;
+      }
       check_cuda(red_launch(pl.spec, pl.strategy, pl.prog, a, aligned ? 1 : 0, pl.grid,
                             reinterpret_cast<void*>(scratch), rec_out, st),
                  "reduce launch");
@@ -1146,7 +1169,9 @@ int askb_internal_launch_reduce_fixed_scratch(const ask_b200_plan* plan, const u
     check_ports(*plan, ports, n_ports);
     check_device(*plan);
     const size_t needed =
-        plan->strategy == RS_SPLIT ? red_split_scratch_bytes(plan->grid, plan->red.n_red) * size_t(plan->red.outer) : 0;
+        plan->strategy == RS_SPLIT ? red_split_scratch_bytes(plan->grid, plan->red.n_red) * size_t(plan->red.outer)
+        : plan->col_chunks > 1     ? plan->scratch
+                                   : 0;
     if (needed > capacity)
       fail(ASK_B200_E_INVALID, "plan needs " + std::to_string(needed) + " bytes of scratch; the fixed scratch array "
                                "holds at most " + std::to_string(capacity) + " bytes (use ask_b200_plan_launch "

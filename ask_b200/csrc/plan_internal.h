@@ -42,6 +42,7 @@ struct ask_b200_plan {
   bool shardable = false;
   std::string kernel;
   int block = 256;  // threads per CTA where the family fixes it (softmax)
+  int col_chunks = 1;  // RS_COLUMN: chunks of the extent over grid.y (1 = the one-pass column kernel)
   int blocks_per_sm = 0;  // recipe cap on resident CTAs per SM of a persistent grid (0 = occupancy)
 };
 

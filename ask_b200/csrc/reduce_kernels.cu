@@ -213,6 +213,50 @@ __global__ void __launch_bounds__(kRedThreads)
   }
 }
 
+// inner > 1 with few outputs: the column kernel's thread per output would
+// leave most of the GPU idle over a long extent, so grid.y splits the extent
+// into chunks.  Thread (o_idx, chunk) folds its chunk's elements of one column
+// (consecutive threads read consecutive columns) into a partial record at
+// part[(o_idx * chunks + chunk) * n_red]; red_combine_kernel then folds each
+// output's records in chunk order, so the result does not depend on timing.
+// No chunk is empty (the host picks the chunk count so).
+__global__ void __launch_bounds__(kRedThreads)
+    red_column_chunks(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a,
+                      RedPartial* __restrict__ part) {
+  pdl_enter();
+  const uint64_t n_outputs = a.outer * a.inner;
+  const uint64_t chunks = gridDim.y, c = blockIdx.y;
+  const uint64_t per = (a.extent + chunks - 1) / chunks;
+  const uint64_t e0 = min(a.extent, c * per), e1 = min(a.extent, e0 + per);
+  uint64_t r[kMaxRegs][1];
+  for (uint64_t o_idx = uint64_t(blockIdx.x) * kRedThreads + threadIdx.x; o_idx < n_outputs;
+       o_idx += uint64_t(gridDim.x) * kRedThreads) {
+    const uint64_t o = o_idx / a.inner, n = o_idx % a.inner;
+    Accs s;
+    accs_init(a, s);
+    for (uint64_t e = e0; e < e1; ++e) {
+      const uint64_t idx = (o * a.extent + e) * a.inner + n;
+      for (int i = 0; i < prog.n_insn; ++i) {
+        const Insn& ins = prog.insn[i];
+        if (ins.op == OP_INPUT) {
+          const int map = prog.in_map[ins.a];
+          r[ins.dst][0] = word_from_storage(prog.in_type[ins.a], a.in[ins.a],
+                                            map == IM_FULL ? idx : map == IM_SCALAR ? 0 : o_idx);
+        } else {
+          r[ins.dst][0] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][0], r[ins.b][0], r[ins.c][0]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kMaxReductions; ++k)
+        if (k < a.n_red)
+          acc_fold<false>(a.red_op[k], a.red_type[k], s.v[k], s.i[k], r[prog.out_reg[a.red_src[k]]][0],
+                          int64_t(a.index_base + e));
+    }
+    RedPartial* dst = part + (o_idx * chunks + c) * a.n_red;
+    for (int k = 0; k < a.n_red; ++k) dst[k] = RedPartial{s.v[k], s.i[k]};
+  }
+}
+
 // General index maps (RS_VIEW): a warp per output (o, n); lanes stride the
 // reduced extent.  A lane's coordinates in the step's iteration shape are
 // computed once per output and advanced by its stride (32 elements of the
@@ -458,6 +502,22 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
   if (e != cudaSuccess) return e;
   (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(kRedThreads), st, a, part, grid, rec_out);
   return cudaGetLastError();
+}
+
+cudaError_t red_column_chunks_launch(const Program& prog, const RedArgs& a, int grid, int chunks, void* scratch,
+                                     cudaStream_t st) {
+  const uint64_t n_outputs = a.outer * a.inner;
+  if (n_outputs == 0) return cudaSuccess;
+  RedPartial* part = static_cast<RedPartial*>(scratch);
+  (void)launch_pdl(&red_column_chunks, dim3(unsigned(grid), unsigned(chunks)), dim3(kRedThreads), st, prog, a, part);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(n_outputs)), dim3(kRedThreads), st, a, part, chunks, nullptr);
+  return cudaGetLastError();
+}
+
+size_t red_column_chunks_scratch_bytes(uint64_t n_outputs, int chunks, int n_red) {
+  return size_t(n_outputs) * size_t(chunks) * size_t(n_red) * sizeof(RedPartial);
 }
 
 cudaError_t red_view_launch(const Program& prog, const RedArgs& a, const ViewSet& views, int grid, cudaStream_t st) {
