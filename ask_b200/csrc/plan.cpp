@@ -684,9 +684,9 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   pl.scratch = 0;
   pl.col_chunks = 1;
   if (pl.strategy == RS_COLUMN && n_outputs && extent >= 64) {
-    // Too few columns to fill the GPU: split the extent into chunks (grid.y)
-    // of at least 32 elements, none empty.
-    const uint64_t threads = cap * uint64_t(kRedThreads);
+    // Too few columns to fill the GPU (2048 threads per SM): split the extent
+    // into chunks (grid.y) of at least 32 elements, none empty.
+    const uint64_t threads = uint64_t(pl.num_sms) * 2048;
     if (n_outputs * 2 <= threads) {
       uint64_t chunks = std::min<uint64_t>({(threads + n_outputs - 1) / n_outputs, extent / 32, 1024});
       if (chunks > 1) {

@@ -31,6 +31,8 @@
 #include <cuda_runtime.h>
 #include <float.h>
 
+#include <algorithm>
+
 #include "ask_numerics.cuh"
 #include "kernels.h"
 #include "programs.h"
@@ -180,35 +182,57 @@ __global__ void __launch_bounds__(kRedThreads)
   }
 }
 
-// inner > 1: thread per output (o, n); element (o, e, n) at (o*extent + e)*inner + n.
+// Fold elements e0 <= e < e1 of column (o, n) -- element (o, e, n) at
+// (o*extent + e)*inner + n -- into s, in order.  A program reading one full
+// port (the common prologue) has four elements' loads issued before it
+// interprets them, so more than one load per thread is in flight.
+__device__ __forceinline__ void column_fold(const Program& prog, const RedArgs& a, uint64_t o, uint64_t n,
+                                            uint64_t o_idx, uint64_t e0, uint64_t e1, Accs& s) {
+  uint64_t r[kMaxRegs][1];
+  auto run = [&](uint64_t e, bool loaded, uint64_t w) {
+    const uint64_t idx = (o * a.extent + e) * a.inner + n;
+    for (int i = 0; i < prog.n_insn; ++i) {
+      const Insn& ins = prog.insn[i];
+      if (ins.op == OP_INPUT) {
+        const int map = prog.in_map[ins.a];
+        r[ins.dst][0] = loaded ? w : word_from_storage(prog.in_type[ins.a], a.in[ins.a],
+                                                       map == IM_FULL ? idx : map == IM_SCALAR ? 0 : o_idx);
+      } else {
+        r[ins.dst][0] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][0], r[ins.b][0], r[ins.c][0]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxReductions; ++k)
+      if (k < a.n_red)
+        acc_fold<false>(a.red_op[k], a.red_type[k], s.v[k], s.i[k], r[prog.out_reg[a.red_src[k]]][0],
+                        int64_t(a.index_base + e));
+  };
+  uint64_t e = e0;
+  if (prog.n_in == 1 && prog.in_map[0] == IM_FULL) {
+    const int t = prog.in_type[0];
+    const void* p = a.in[0];
+    for (; e + 4 <= e1; e += 4) {
+      uint64_t w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) w[u] = word_from_storage(t, p, (o * a.extent + e + u) * a.inner + n);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) run(e + u, true, w[u]);
+    }
+  }
+  for (; e < e1; ++e) run(e, false, 0);
+}
+
+// inner > 1: thread per output (o, n).
 __global__ void __launch_bounds__(kRedThreads)
     red_column_generic(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a) {
   pdl_enter();
   const uint64_t n_outputs = a.outer * a.inner;
-  uint64_t r[kMaxRegs][1];
   for (uint64_t o_idx = uint64_t(blockIdx.x) * kRedThreads + threadIdx.x; o_idx < n_outputs;
        o_idx += uint64_t(gridDim.x) * kRedThreads) {
     const uint64_t o = o_idx / a.inner, n = o_idx % a.inner;
     Accs s;
     accs_init(a, s);
-    for (uint64_t e = 0; e < a.extent; ++e) {
-      const uint64_t idx = (o * a.extent + e) * a.inner + n;
-      for (int i = 0; i < prog.n_insn; ++i) {
-        const Insn& ins = prog.insn[i];
-        if (ins.op == OP_INPUT) {
-          const int map = prog.in_map[ins.a];
-          r[ins.dst][0] = word_from_storage(prog.in_type[ins.a], a.in[ins.a],
-                                            map == IM_FULL ? idx : map == IM_SCALAR ? 0 : o_idx);
-        } else {
-          r[ins.dst][0] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][0], r[ins.b][0], r[ins.c][0]);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < kMaxReductions; ++k)
-        if (k < a.n_red)
-          acc_fold<false>(a.red_op[k], a.red_type[k], s.v[k], s.i[k], r[prog.out_reg[a.red_src[k]]][0],
-                          int64_t(a.index_base + e));
-    }
+    column_fold(prog, a, o, n, o_idx, 0, a.extent, s);
     write_outputs(a, s, o_idx);
   }
 }
@@ -217,9 +241,9 @@ __global__ void __launch_bounds__(kRedThreads)
 // leave most of the GPU idle over a long extent, so grid.y splits the extent
 // into chunks.  Thread (o_idx, chunk) folds its chunk's elements of one column
 // (consecutive threads read consecutive columns) into a partial record at
-// part[(o_idx * chunks + chunk) * n_red]; red_combine_kernel then folds each
-// output's records in chunk order, so the result does not depend on timing.
-// No chunk is empty (the host picks the chunk count so).
+// part[(chunk * n_outputs + o_idx) * n_red]; red_column_combine then folds
+// each output's records in chunk order, so the result does not depend on
+// timing.  No chunk is empty (the host picks the chunk count so).
 __global__ void __launch_bounds__(kRedThreads)
     red_column_chunks(const __grid_constant__ Program prog, const __grid_constant__ RedArgs a,
                       RedPartial* __restrict__ part) {
@@ -228,32 +252,36 @@ __global__ void __launch_bounds__(kRedThreads)
   const uint64_t chunks = gridDim.y, c = blockIdx.y;
   const uint64_t per = (a.extent + chunks - 1) / chunks;
   const uint64_t e0 = min(a.extent, c * per), e1 = min(a.extent, e0 + per);
-  uint64_t r[kMaxRegs][1];
   for (uint64_t o_idx = uint64_t(blockIdx.x) * kRedThreads + threadIdx.x; o_idx < n_outputs;
        o_idx += uint64_t(gridDim.x) * kRedThreads) {
     const uint64_t o = o_idx / a.inner, n = o_idx % a.inner;
     Accs s;
     accs_init(a, s);
-    for (uint64_t e = e0; e < e1; ++e) {
-      const uint64_t idx = (o * a.extent + e) * a.inner + n;
-      for (int i = 0; i < prog.n_insn; ++i) {
-        const Insn& ins = prog.insn[i];
-        if (ins.op == OP_INPUT) {
-          const int map = prog.in_map[ins.a];
-          r[ins.dst][0] = word_from_storage(prog.in_type[ins.a], a.in[ins.a],
-                                            map == IM_FULL ? idx : map == IM_SCALAR ? 0 : o_idx);
-        } else {
-          r[ins.dst][0] = eval_insn(ins.op, ins.type, ins.src_type, ins.aux, ins.imm, r[ins.a][0], r[ins.b][0], r[ins.c][0]);
-        }
-      }
+    column_fold(prog, a, o, n, o_idx, e0, e1, s);
+    RedPartial* dst = part + (c * n_outputs + o_idx) * a.n_red;
+    for (int k = 0; k < a.n_red; ++k) dst[k] = RedPartial{s.v[k], s.i[k]};
+  }
+}
+
+// A thread per output folds its `chunks` partial records in chunk order
+// (records of consecutive outputs are adjacent, so the loads coalesce).
+__global__ void __launch_bounds__(kRedThreads)
+    red_column_combine(const __grid_constant__ RedArgs a, const RedPartial* __restrict__ part, int chunks) {
+  pdl_enter();
+  const uint64_t n_outputs = a.outer * a.inner;
+  for (uint64_t o_idx = uint64_t(blockIdx.x) * kRedThreads + threadIdx.x; o_idx < n_outputs;
+       o_idx += uint64_t(gridDim.x) * kRedThreads) {
+    Accs s;
+    accs_init(a, s);
+    for (int c = 0; c < chunks; ++c) {
+      const RedPartial* src = part + (uint64_t(c) * n_outputs + o_idx) * a.n_red;
+      Accs x;
 #pragma unroll
       for (int k = 0; k < kMaxReductions; ++k)
-        if (k < a.n_red)
-          acc_fold<false>(a.red_op[k], a.red_type[k], s.v[k], s.i[k], r[prog.out_reg[a.red_src[k]]][0],
-                          int64_t(a.index_base + e));
+        if (k < a.n_red) { x.v[k] = src[k].v; x.i[k] = src[k].idx; }
+      accs_merge(a, s, x);
     }
-    RedPartial* dst = part + (o_idx * chunks + c) * a.n_red;
-    for (int k = 0; k < a.n_red; ++k) dst[k] = RedPartial{s.v[k], s.i[k]};
+    write_outputs(a, s, o_idx);
   }
 }
 
@@ -512,7 +540,9 @@ cudaError_t red_column_chunks_launch(const Program& prog, const RedArgs& a, int 
   (void)launch_pdl(&red_column_chunks, dim3(unsigned(grid), unsigned(chunks)), dim3(kRedThreads), st, prog, a, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(n_outputs)), dim3(kRedThreads), st, a, part, chunks, nullptr);
+  const uint64_t blocks = (n_outputs + kRedThreads - 1) / kRedThreads;
+  (void)launch_pdl(&red_column_combine, dim3(unsigned(std::min<uint64_t>(blocks, 65535))), dim3(kRedThreads), st, a,
+                   static_cast<const RedPartial*>(part), chunks);
   return cudaGetLastError();
 }
 
