@@ -780,6 +780,86 @@ def test_random_map_steps_on_gpu(device):
     assert checked >= 40
 
 
+def strided_view_step(seed, dt="i32"):
+    """A step over [batch..., R, C] adding transposed arguments (stored
+    [batch..., C, R]), a straight strided slice, a full argument, a scalar and
+    a view that moves a batch axis.  Returns (source, arrays, expected,
+    number of transposed reads)."""
+    rng = np.random.default_rng(seed)
+    batch = [int(x) for x in rng.integers(1, 4, int(rng.integers(0, 3)))]
+    R, C = int(rng.integers(1, 80)), int(rng.integers(2, 80))
+    shape = batch + [R, C]
+    rank = len(shape)
+    npdt = {"i32": np.int32, "i64": np.int64, "f16": np.float16}[dt]
+    s = Step()
+    terms, arrays, values = [], [], []
+
+    def arg(sh):
+        v = rng.integers(-9, 10, sh).astype(npdt)
+        arrays.append(v)
+        return s.arg(list(sh), dt), v
+
+    n_t = int(rng.integers(0, 5))
+    for _ in range(n_t):  # transposed: the argument's last two axes swapped
+        a, av = arg(batch + [C, R])
+        perm = list(range(len(batch))) + [rank - 1, rank - 2]
+        terms.append(s.op("transpose", [a], shape, dt, "permutation = " + arr(perm)))
+        values.append(np.transpose(av, perm))
+    if rng.random() < 0.6:  # a straight strided slice (step 1, an offset)
+        a, av = arg([d + 2 for d in shape])
+        terms.append(s.op("slice", [a], shape, dt, f"starts = {arr([1] * rank)}, stops = {arr([d + 1 for d in shape])}, "
+                                                  f"steps = {arr([1] * rank)}"))
+        values.append(av[tuple(slice(1, d + 1) for d in shape)])
+    if rng.random() < 0.5:
+        a, av = arg(shape)
+        terms.append(a)
+        values.append(av)
+    if batch and rng.random() < 0.5:  # a batch axis moved past R: still contiguous along C
+        a, av = arg([R] + batch + [C])
+        perm = list(range(1, len(batch) + 1)) + [0, rank - 1]
+        terms.append(s.op("transpose", [a], shape, dt, "permutation = " + arr(perm)))
+        values.append(np.transpose(av, perm))
+    if not terms:
+        a, av = arg(shape)
+        terms.append(a)
+        values.append(av)
+    y, want = terms[0], values[0].copy()
+    for tm, v in zip(terms[1:], values[1:]):
+        y = s.op("add", [y, tm], shape, dt)
+        want = (want + v).astype(npdt)
+    return s.text([y]), arrays, want, n_t
+
+
+def test_strided_views_evaluate():
+    """Steps adding transposed, sliced, batch-permuted, full and scalar reads
+    lower (to the view kernel when a transposed read remains) and equal numpy."""
+    for seed in range(150):
+        src, args, want, n_t = strided_view_step(seed)
+        out = rt.lower_step(src)
+        kernel = ask_b200.Plan(out["recipe"], -1).describe()["kernel"]
+        assert kernel in ("ew_view", "ew_generic"), (seed, kernel)
+        if n_t and want.shape[-1] > 1 and want.shape[-2] > 1:
+            assert kernel == "ew_view", seed
+        got = recipe_eval.evaluate(out["recipe"], [args[a] for a in out["input_arguments"]])
+        assert np.array_equal(got[0].reshape(want.shape), want), seed
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dt", ["i32", "i64", "f16"])
+def test_strided_views_on_gpu(device, dt):
+    import torch
+    from gpu_util import NUMPY
+    for seed in range(60):
+        src, args, want, _ = strided_view_step(seed, dt)
+        out = rt.lower_step(src)
+        plan = ask_b200.Plan(out["recipe"], 0)
+        dev_in = [torch.from_numpy(np.ascontiguousarray(args[a]).view(NUMPY[dt])).cuda() for a in out["input_arguments"]]
+        y = torch.empty(want.size, dtype=dev_in[0].dtype, device="cuda")
+        plan.launch(dev_in, [y], None, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        assert np.array_equal(y.cpu().numpy().view(want.dtype).reshape(want.shape), want), (dt, seed)
+
+
 def _factor_shape(rng, n):
     """A random shape (rank 1..4) whose extents multiply to n."""
     dims, left = [], n
