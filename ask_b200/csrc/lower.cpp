@@ -492,6 +492,7 @@ class Lowering {
   explicit Lowering(const Func& f) : f_(f) {
     for (size_t k = 0; k < f.args.size(); ++k) arg_[f.args[k]] = k;
     for (size_t k = 0; k < f.ops.size(); ++k) def_[f.ops[k].result] = k;
+    gather_reduced_axes();
     push_index_maps();
   }
 
@@ -538,6 +539,52 @@ class Lowering {
   bool uses_shape_ = false;    // a view or a coordinate needs the iteration shape
 
   static bool is_reduction(const std::string& n) { return n.rfind("reduce_", 0) == 0 || n == "argmax" || n == "argmin"; }
+
+  // A reduction over axes that are not one contiguous block (say axes 0 and 2
+  // of a rank-3 value) reads its operand through a transpose that puts the
+  // kept axes first, in their order, and the reduced axes last, in theirs;
+  // its axes become that trailing block.  The outputs keep their row-major
+  // order over the kept axes, and the fold runs over the reduced index space
+  // in the same row-major order.  The transpose then moves onto the operand's
+  // arguments like any index map.
+  void gather_reduced_axes() {
+    const size_t original = f_.ops.size();
+    size_t fresh = 0;
+    for (size_t i = 0; i < original; ++i) {
+      const std::string n = strip(f_.ops[i].name);
+      if (n.rfind("reduce_", 0) != 0 || f_.ops[i].operands.empty()) continue;  // argmax/argmin take one axis
+      auto ax = f_.ops[i].attrs.find("axes");
+      if (ax == f_.ops[i].attrs.end()) continue;
+      std::vector<int64_t> axes = ax->second.arr;
+      std::sort(axes.begin(), axes.end());
+      bool contiguous = true;
+      for (size_t k = 1; k < axes.size(); ++k) contiguous = contiguous && axes[k] == axes[k - 1] + 1;
+      const Type in = type_of(f_.ops[i].operands[0]);  // a copy: the ops may move
+      const int64_t rank = int64_t(in.shape.size());
+      if (contiguous || axes.empty() || axes.front() < 0 || axes.back() >= rank) continue;
+      std::vector<int64_t> perm;
+      for (int64_t d = 0; d < rank; ++d)
+        if (!std::binary_search(axes.begin(), axes.end(), d)) perm.push_back(d);
+      const int64_t kept = int64_t(perm.size());
+      for (int64_t d : axes) perm.push_back(d);
+      Op t;
+      t.name = "ask.transpose";
+      t.operands = {f_.ops[i].operands[0]};
+      t.type = Type{in.dtype, {}, true};
+      for (int64_t d : perm) t.type.shape.push_back(in.shape[size_t(d)]);
+      Attr pa;
+      pa.kind = Attr::IntArray;
+      pa.arr = perm;
+      t.attrs["permutation"] = pa;
+      t.result = "%ask_b200.gathered" + std::to_string(fresh++);
+      f_.ops.push_back(t);
+      def_[t.result] = f_.ops.size() - 1;
+      f_.ops[i].operands[0] = t.result;
+      std::vector<int64_t> block;
+      for (int64_t d = kept; d < rank; ++d) block.push_back(d);
+      f_.ops[i].attrs["axes"].arr = block;
+    }
+  }
 
   const Op* producer(const std::string& v) const {
     auto it = def_.find(v);

@@ -10,8 +10,9 @@
  * path: elementwise ops over the step's iteration shape, whose arguments may
  * be read through broadcast_in_dim, transpose, slice, pad, reshape and
  * concatenate (as strided, windowed views of the argument) and iota;
- * reductions (sum, prod, max, min, any, all, argmax, argmin) over one
- * contiguous block of axes, their operands built the same way; gather and
+ * reductions (sum, prod, max, min, any, all, argmax, argmin) over any set
+ * of axes (a scattered set is gathered last by a transpose), their operands
+ * built the same way; gather and
  * scatter_add.  Steps outside it fail
  * with ASK_B200_E_UNSUPPORTED and a message naming the op (matmul and
  * external steps, a reshape that would need a copy, a reshape of a padded

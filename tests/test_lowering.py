@@ -1081,6 +1081,57 @@ def test_permuted_reductions_on_gpu(device):
             assert np.array_equal(g.cpu().numpy(), w.reshape(-1)), (seed, k)
 
 
+def scattered_axes_reduce_step(seed):
+    """An i32 value (an argument times three plus a second argument) reduced
+    with sum, max and min over a random non-contiguous set of axes."""
+    rng = np.random.default_rng(seed)
+    rank = int(rng.integers(3, 5))
+    shape = [int(x) for x in rng.integers(2, 6, rank)]
+    while True:
+        axes = sorted(int(a) for a in rng.choice(rank, int(rng.integers(2, rank)), replace=False))
+        if axes != list(range(axes[0], axes[-1] + 1)):
+            break
+    kept = [d for d in range(rank) if d not in axes]
+    s = Step()
+    x, y = s.arg(shape, "i32"), s.arg(shape, "i32")
+    v = s.op("add", [s.op("mul", [x, s.splat(s.const(3, "i32"), shape)], shape, "i32"), y], shape, "i32")
+    kshape = [shape[d] for d in kept]
+    outs = [s.op(op, [v], kshape, "i32", "axes = " + arr(axes)) for op in ("reduce_sum", "reduce_max", "reduce_min")]
+    xv, yv = (rng.integers(-40, 40, shape).astype(np.int32) for _ in range(2))
+    vv = xv * 3 + yv
+    want = [vv.sum(axis=tuple(axes)).astype(np.int32), vv.max(axis=tuple(axes)), vv.min(axis=tuple(axes))]
+    return s.text(outs), [xv, yv], want
+
+
+def test_reductions_over_scattered_axes_evaluate():
+    """Reductions over axes that are not one block (axes 0 and 2 of a rank-3
+    value, ...) lower through a transpose that gathers the reduced axes last;
+    the outputs equal numpy's."""
+    for seed in range(120):
+        src, args, want = scattered_axes_reduce_step(seed)
+        out = rt.lower_step(src)
+        ask_b200.Plan(out["recipe"], -1)
+        got = recipe_eval.evaluate(out["recipe"], [args[a] for a in out["input_arguments"]])
+        for k, (g, w) in enumerate(zip(got, want)):
+            assert np.array_equal(g, w.reshape(-1)), (seed, k)
+
+
+@pytest.mark.gpu
+def test_reductions_over_scattered_axes_on_gpu(device):
+    import torch
+    for seed in range(40):
+        src, args, want = scattered_axes_reduce_step(seed)
+        out = rt.lower_step(src)
+        plan = ask_b200.Plan(out["recipe"], 0)
+        dev_in = [torch.from_numpy(np.ascontiguousarray(args[a])).cuda() for a in out["input_arguments"]]
+        outs = [torch.empty(w.size, dtype=torch.int32, device="cuda") for w in want]
+        scratch = torch.empty(max(plan.scratch_bytes, 16), dtype=torch.uint8, device="cuda")
+        plan.launch(dev_in, outs, scratch, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        for k, (g, w) in enumerate(zip(outs, want)):
+            assert np.array_equal(g.cpu().numpy(), w.reshape(-1)), (seed, k)
+
+
 def random_reduce_step(seed):
     """A random map-and-elementwise i32 operand reduced over a random block of
     contiguous axes with sum, max, min and argmax (argmax over a single axis)."""
