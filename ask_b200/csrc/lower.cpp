@@ -492,6 +492,7 @@ class Lowering {
   explicit Lowering(const Func& f) : f_(f) {
     for (size_t k = 0; k < f.args.size(); ++k) arg_[f.args[k]] = k;
     for (size_t k = 0; k < f.ops.size(); ++k) def_[f.ops[k].result] = k;
+    erase_marks();
     gather_reduced_axes();
     push_index_maps();
   }
@@ -539,6 +540,23 @@ class Lowering {
   bool uses_shape_ = false;    // a view or a coordinate needs the iteration shape
 
   static bool is_reduction(const std::string& n) { return n.rfind("reduce_", 0) == 0 || n == "argmax" || n == "argmin"; }
+
+  // ask.mark is a tracing pass-through (a value's identity or port binding)
+  // that the reference's prepare phase extracts and erases, connecting the
+  // marked value directly to its users (docs/en/ir.md:42, 125-131); a step
+  // source that still carries one lowers as if it had been erased.
+  void erase_marks() {
+    for (Op& op : f_.ops) {
+      if (strip(op.name) != "mark" || op.operands.size() != 1) continue;
+      const std::string from = op.result, to = op.operands[0];
+      for (Op& o : f_.ops)
+        for (std::string& x : o.operands)
+          if (x == from) x = to;
+      for (std::string& r : f_.returns)
+        if (r == from) r = to;
+      op.name = "ask.ask_b200_moved";
+    }
+  }
 
   // A reduction over axes that are not one contiguous block (say axes 0 and 2
   // of a rank-3 value) reads its operand through a transpose that puts the

@@ -539,6 +539,25 @@ def test_index_map_steps_on_gpu(device, case):
     assert np.array_equal(y.cpu().numpy().reshape(want.shape), want)
 
 
+def test_marks_lower_as_erased():
+    """ask.mark pass-throughs (value and port markers, which the reference's
+    prepare phase erases) leave the lowered recipe unchanged."""
+    def build(marks):
+        s = Step()
+        x, y = s.arg([8, 16], "f32"), s.arg([16, 8], "f32")
+        if marks:
+            x = s.op("mark", [x], [8, 16], "f32", 'mark_id = "m0", role = "input", port_id = "x"')
+        t = s.op("transpose", [y], [8, 16], "f32", "permutation = " + arr([1, 0]))
+        if marks:
+            t = s.op("mark", [t], [8, 16], "f32", 'mark_id = "m1", role = "value", value_id = "t"')
+        z = s.op("add", [x, t], [8, 16], "f32")
+        r = s.op("reduce_sum", [z], [8], "f32", "axes = " + arr([1]))
+        if marks:
+            r = s.op("mark", [r], [8], "f32", 'mark_id = "m2", role = "output", port_id = "r"')
+        return s.text([r])
+    assert rt.lower_step(build(True)) == rt.lower_step(build(False))
+
+
 def test_malformed_sources_are_invalid():
     for text in ["module {}", "module { func.func @f(%arg0: tensor<?xf32>) -> tensor<?xf32> { return %arg0 : tensor<?xf32> } }"]:
         with pytest.raises(rt.CUDAError) as err:
