@@ -1549,6 +1549,76 @@ Lowered lower_source(const std::string& text) {
   return Lowering(f).run();
 }
 
+// A step whose results one recipe cannot hold together -- elementwise results
+// of different shapes, reductions over different operand shapes or axes, or
+// both kinds -- lowers to one recipe per group of results, the way the
+// reference emits one batch per output shape in a step's kernel
+// (lib/Lowering/CUDA.cpp:210-244).  Groups keep the order of their first
+// result; each lists the function results it returns.
+std::vector<std::pair<Lowered, std::vector<size_t>>> lower_source_groups(const std::string& text) {
+  Reader r(text);
+  const Func f = r.read_function();
+  std::map<std::string, const Op*> def;
+  std::map<std::string, size_t> arg;
+  for (const Op& op : f.ops) def[op.result] = &op;
+  for (size_t k = 0; k < f.args.size(); ++k) arg[f.args[k]] = k;
+  auto shape_key = [](const std::vector<int64_t>& v) {
+    std::string o;
+    for (int64_t d : v) o += std::to_string(d) + ",";
+    return o;
+  };
+  std::vector<std::string> keys;
+  std::vector<std::vector<size_t>> groups;
+  for (size_t k = 0; k < f.returns.size(); ++k) {
+    std::string key;
+    auto d = def.find(f.returns[k]);
+    if (d == def.end()) {
+      auto a = arg.find(f.returns[k]);
+      key = "E|" + (a != arg.end() ? shape_key(f.arg_types[a->second].shape) : std::string("?"));
+    } else {
+      const Op& op = *d->second;
+      const std::string n = strip(op.name);
+      if (n == "gather" || n == "scatter_add") {
+        key = "X|" + std::to_string(k);
+      } else if (n.rfind("reduce_", 0) == 0 || n == "argmax" || n == "argmin") {
+        std::vector<int64_t> axes;
+        auto ax = op.attrs.find(n == "argmax" || n == "argmin" ? "axis" : "axes");
+        if (ax != op.attrs.end()) axes = ax->second.kind == Attr::IntArray ? ax->second.arr
+                                                                          : std::vector<int64_t>{ax->second.i};
+        std::sort(axes.begin(), axes.end());
+        auto od = op.operands.empty() ? def.end() : def.find(op.operands[0]);
+        auto oa = op.operands.empty() ? arg.end() : arg.find(op.operands[0]);
+        const std::vector<int64_t> in = od != def.end() ? od->second->type.shape
+                                        : oa != arg.end() ? f.arg_types[oa->second].shape : std::vector<int64_t>{};
+        key = "R|" + shape_key(in) + "|" + shape_key(axes);
+      } else {
+        key = "E|" + shape_key(op.type.shape);
+      }
+    }
+    size_t g = 0;
+    while (g < keys.size() && keys[g] != key) ++g;
+    if (g == keys.size()) {
+      keys.push_back(key);
+      groups.emplace_back();
+    }
+    groups[g].push_back(k);
+  }
+  std::vector<std::pair<Lowered, std::vector<size_t>>> out;
+  if (groups.size() <= 1) {
+    std::vector<size_t> all(f.returns.size());
+    for (size_t k = 0; k < all.size(); ++k) all[k] = k;
+    out.emplace_back(Lowering(f).run(), all);
+    return out;
+  }
+  for (const auto& g : groups) {
+    Func part = f;
+    part.returns.clear();
+    for (size_t k : g) part.returns.push_back(f.returns[k]);
+    out.emplace_back(Lowering(part).run(), g);
+  }
+  return out;
+}
+
 size_t element_bytes(const std::string& t) {
   if (t == "bool") return 1;
   if (t == "i32" || t == "f32") return 4;
@@ -1598,21 +1668,30 @@ std::string lower_report(const char* report_json) {
       unsupported("step " + id + " is a '" + kind->str + "' step; only owned steps lower to recipes");
     const json::Value* src = sources->get(id);
     if (!src) invalid("no step source for " + id);
-    Lowered l;
+    std::vector<std::pair<Lowered, std::vector<size_t>>> parts;
     try {
-      l = lower_source(src->as_str("step source"));
+      parts = lower_source_groups(src->as_str("step source"));
     } catch (const Failure& f) {
       fail(f.code, "step " + id + ": " + f.message);
     }
     const std::vector<size_t> ins = ids(step.at("inputs"), "step inputs");
-    std::vector<size_t> bound;
-    for (size_t a : l.input_args) {
-      if (a >= ins.size()) invalid("step " + id + " source has more arguments than the plan binds");
-      bound.push_back(ins[a]);
+    const std::vector<size_t> outs = ids(step.at("outputs"), "step outputs");
+    for (size_t g = 0; g < parts.size(); ++g) {
+      const Lowered& l = parts[g].first;
+      std::vector<size_t> bound, written;
+      for (size_t a : l.input_args) {
+        if (a >= ins.size()) invalid("step " + id + " source has more arguments than the plan binds");
+        bound.push_back(ins[a]);
+      }
+      for (size_t k : parts[g].second) {
+        if (k >= outs.size()) invalid("step " + id + " source returns more results than the plan binds");
+        written.push_back(outs[k]);
+      }
+      const std::string sid = parts.size() > 1 ? id + "#" + std::to_string(g) : id;
+      o << (first ? "" : ",") << "{\"id\":" << json_str(sid) << ",\"recipe\":" << json_str(l.recipe)
+        << ",\"inputs\":" << list(bound) << ",\"outputs\":" << list(written) << "}";
+      first = false;
     }
-    o << (first ? "" : ",") << "{\"id\":" << json_str(id) << ",\"recipe\":" << json_str(l.recipe)
-      << ",\"inputs\":" << list(bound) << ",\"outputs\":" << list(ids(step.at("outputs"), "step outputs")) << "}";
-    first = false;
   }
   o << "]}";
   return o.str();

@@ -41,7 +41,13 @@ ASK_B200_API int ask_b200_lower_step(const char *step_source, char *buf, size_t 
  * reference's report fields) to a runtime program for
  * ask_b200_program_prepare (ask_b200_runtime.h): buffer sizes from the plan's
  * buffer shapes and element types, public inputs and outputs, and one recipe
- * step per owned step with its ports bound to the plan's buffers.
+ * step per owned step with its ports bound to the plan's buffers.  A step
+ * whose results one recipe cannot hold (elementwise results of different
+ * shapes, reductions over different axes or operand shapes) becomes one
+ * program step per group of results, ids "<step>#<k>", each writing its own
+ * outputs -- the reference's one batch per output shape
+ * (lib/Lowering/CUDA.cpp:210-244).  ask_b200_lower_step returns one recipe
+ * and rejects such a step.
  */
 ASK_B200_API int ask_b200_lower_report(const char *report_json, char *buf, size_t cap, size_t *needed);
 

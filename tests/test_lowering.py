@@ -604,6 +604,55 @@ def test_report_lowers_to_a_program():
     assert [s["inputs"] for s in prog["steps"]] == [[0, 1], [2, 1, 3]]
 
 
+def mixed_results_step(rows=6, cols=10):
+    """One step returning row sums [rows], column sums [cols], a row maximum
+    [rows] and two elementwise results [rows, cols] of the same argument."""
+    s = Step()
+    x = s.arg([rows, cols], "i32")
+    y = s.op("mul", [x, s.splat(s.const(2, "i32"), [rows, cols])], [rows, cols], "i32")
+    outs = [s.op("reduce_sum", [x], [rows], "i32", "axes = " + arr([1])),
+            s.op("reduce_sum", [x], [cols], "i32", "axes = " + arr([0])),
+            y,
+            s.op("reduce_max", [x], [rows], "i32", "axes = " + arr([1])),
+            s.op("abs", [x], [rows, cols], "i32")]
+    return s.text(outs)
+
+
+def test_steps_with_mixed_results_lower_to_one_recipe_per_group():
+    """A step whose results one recipe cannot hold together (reductions over
+    different axes and elementwise results) becomes one program step per
+    group -- row reductions, column reductions, elementwise -- each writing
+    its own outputs; every recipe evaluated on the CPU equals numpy."""
+    rows, cols = 6, 10
+    buffers = [{"id": "v_x", "shape": [rows, cols], "element_type": "i32"},
+               {"id": "v_r", "shape": [rows], "element_type": "i32"},
+               {"id": "v_c", "shape": [cols], "element_type": "i32"},
+               {"id": "v_y", "shape": [rows, cols], "element_type": "i32"},
+               {"id": "v_m", "shape": [rows], "element_type": "i32"},
+               {"id": "v_a", "shape": [rows, cols], "element_type": "i32"}]
+    rep = report([mixed_results_step(rows, cols)], buffers, ["v_x"], ["v_r", "v_c", "v_y", "v_m", "v_a"],
+                 [(["v_x"], ["v_r", "v_c", "v_y", "v_m", "v_a"])])
+    prog = rt.lower_report(rep)
+    assert [s["id"] for s in prog["steps"]] == ["kernel0#0", "kernel0#1", "kernel0#2"]
+    ok, why = rt.check_allocation({"buffer_count": len(prog["buffer_sizes"]), "public_inputs": prog["inputs"],
+                                   "public_outputs": prog["outputs"],
+                                   "steps": [{"inputs": s["inputs"], "outputs": s["outputs"]} for s in prog["steps"]]})
+    assert ok, why
+    assert [s["outputs"] for s in prog["steps"]] == [[1, 4], [2], [3, 5]]
+    x = np.random.default_rng(4).integers(-50, 50, (rows, cols)).astype(np.int32)
+    want = {1: x.sum(axis=1), 2: x.sum(axis=0), 3: 2 * x, 4: x.max(axis=1), 5: np.abs(x)}
+    for st in prog["steps"]:
+        rec = json.loads(st["recipe"])
+        ask_b200.Plan(rec, -1)
+        got = recipe_eval.evaluate(rec, [x for _ in st["inputs"]])
+        for g, b in zip(got, st["outputs"]):
+            assert np.array_equal(g, want[b].astype(np.int32).reshape(-1)), b
+    # a step that one recipe holds stays one program step with its own id
+    single = report([cfg1_source(64)], [{"id": f"v{k}", "shape": [64], "element_type": "f32"} for k in range(5)],
+                    ["v0", "v1", "v2"], ["v3", "v4"], [(["v0", "v1", "v2"], ["v3", "v4"])])
+    assert [s["id"] for s in rt.lower_report(single)["steps"]] == ["kernel0"]
+
+
 def test_non_owned_steps_are_unsupported():
     r = softmax_report("f16", 8, 16)
     r["execution_plan"]["steps"][1]["kind"] = "external"
