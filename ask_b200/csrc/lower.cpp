@@ -1549,13 +1549,31 @@ Lowered lower_source(const std::string& text) {
   return Lowering(f).run();
 }
 
-// A step whose results one recipe cannot hold together -- elementwise results
-// of different shapes, reductions over different operand shapes or axes, or
-// both kinds -- lowers to one recipe per group of results, the way the
-// reference emits one batch per output shape in a step's kernel
-// (lib/Lowering/CUDA.cpp:210-244).  Groups keep the order of their first
-// result; each lists the function results it returns.
-std::vector<std::pair<Lowered, std::vector<size_t>>> lower_source_groups(const std::string& text) {
+size_t element_bytes(const std::string& t);
+
+// One program step of a lowered source: per recipe input, the function
+// argument it reads (>= 0) or internal buffer k (-1 - k); per recipe output,
+// the function result it writes (>= 0) or internal buffer k (-1 - k).
+struct Part {
+  Lowered l;
+  std::vector<int64_t> ins, outs;
+};
+struct Split {
+  std::vector<Part> parts;
+  std::vector<uint64_t> internal_bytes;  // sizes of the internal buffers the parts exchange
+};
+
+// A step lowers to one recipe when it can; otherwise:
+//   - results one recipe cannot hold together (elementwise results of
+//     different shapes, reductions over different operand shapes or axes, or
+//     both kinds) lower as one recipe per group, the way the reference emits
+//     one batch per output shape in a step's kernel (lib/Lowering/CUDA.cpp:
+//     210-244); groups keep the order of their first result;
+//   - a gather or scatter_add whose operands are computed in the step reads
+//     them from internal buffers that elementwise recipes write first (the
+//     reference evaluates such operands per element inside its kernel,
+//     lib/Lowering/ScalarEmitter.h:775-815).
+Split lower_source_split(const std::string& text) {
   Reader r(text);
   const Func f = r.read_function();
   std::map<std::string, const Op*> def;
@@ -1603,18 +1621,53 @@ std::vector<std::pair<Lowered, std::vector<size_t>>> lower_source_groups(const s
     }
     groups[g].push_back(k);
   }
-  std::vector<std::pair<Lowered, std::vector<size_t>>> out;
-  if (groups.size() <= 1) {
-    std::vector<size_t> all(f.returns.size());
-    for (size_t k = 0; k < all.size(); ++k) all[k] = k;
-    out.emplace_back(Lowering(f).run(), all);
-    return out;
-  }
-  for (const auto& g : groups) {
+  Split out;
+  auto plain = [](const Lowered& l, const std::vector<size_t>& results) {
+    Part p{l, {}, {}};
+    for (size_t a : l.input_args) p.ins.push_back(int64_t(a));
+    for (size_t k : results) p.outs.push_back(int64_t(k));
+    return p;
+  };
+  for (size_t g = 0; g < groups.size(); ++g) {
     Func part = f;
     part.returns.clear();
-    for (size_t k : g) part.returns.push_back(f.returns[k]);
-    out.emplace_back(Lowering(part).run(), g);
+    for (size_t k : groups[g]) part.returns.push_back(f.returns[k]);
+    const bool indexed = keys[g].rfind("X|", 0) == 0;
+    if (!indexed) {
+      out.parts.push_back(plain(Lowering(part).run(), groups[g]));
+      continue;
+    }
+    // a gather/scatter_add: computed operands first, into internal buffers
+    const Op& op = *def.at(f.returns[groups[g][0]]);
+    size_t op_index = 0;
+    while (part.ops[op_index].result != op.result) ++op_index;
+    std::vector<int64_t> internal_of_arg;  // per extra argument of `part`, its internal buffer
+    for (size_t j = 0; j < op.operands.size(); ++j) {
+      const std::string& v = op.operands[j];
+      if (arg.count(v)) continue;
+      auto pd = def.find(v);
+      if (pd == def.end()) invalid("value " + v + " is not defined");
+      const Type t = pd->second->type;
+      Func pre = f;
+      pre.returns = {v};
+      const Lowered lp = Lowering(pre).run();
+      const int64_t k = int64_t(out.internal_bytes.size());
+      out.internal_bytes.push_back(t.numel() * element_bytes(t.dtype));
+      Part pp{lp, {}, {-1 - k}};
+      for (size_t a : lp.input_args) pp.ins.push_back(int64_t(a));
+      out.parts.push_back(pp);
+      const std::string name = "%ask_b200.internal" + std::to_string(k);
+      part.args.push_back(name);
+      part.arg_types.push_back(t);
+      internal_of_arg.push_back(k);
+      part.ops[op_index].operands[j] = name;
+    }
+    const Lowered l = Lowering(part).run();
+    Part p{l, {}, {}};
+    for (size_t a : l.input_args)
+      p.ins.push_back(a < f.args.size() ? int64_t(a) : -1 - internal_of_arg[a - f.args.size()]);
+    for (size_t k : groups[g]) p.outs.push_back(int64_t(k));
+    out.parts.push_back(p);
   }
   return out;
 }
@@ -1655,11 +1708,7 @@ std::string lower_report(const char* report_json) {
     for (size_t i = 0; i < v.size(); ++i) o += (i ? "," : "") + std::to_string(v[i]);
     return o + "]";
   };
-  std::ostringstream o;
-  o << "{\"buffer_sizes\":[";
-  for (size_t i = 0; i < sizes.size(); ++i) o << (i ? "," : "") << sizes[i];
-  o << "],\"inputs\":" << list(ids(plan.at("inputs"), "inputs")) << ",\"outputs\":" << list(ids(plan.at("outputs"), "outputs"))
-    << ",\"steps\":[";
+  std::ostringstream steps;
   bool first = true;
   for (const auto& step : plan.at("steps").as_array("steps")) {
     const std::string id = step.at("id").as_str("step id");
@@ -1668,32 +1717,37 @@ std::string lower_report(const char* report_json) {
       unsupported("step " + id + " is a '" + kind->str + "' step; only owned steps lower to recipes");
     const json::Value* src = sources->get(id);
     if (!src) invalid("no step source for " + id);
-    std::vector<std::pair<Lowered, std::vector<size_t>>> parts;
+    Split split;
     try {
-      parts = lower_source_groups(src->as_str("step source"));
+      split = lower_source_split(src->as_str("step source"));
     } catch (const Failure& f) {
       fail(f.code, "step " + id + ": " + f.message);
     }
     const std::vector<size_t> ins = ids(step.at("inputs"), "step inputs");
     const std::vector<size_t> outs = ids(step.at("outputs"), "step outputs");
-    for (size_t g = 0; g < parts.size(); ++g) {
-      const Lowered& l = parts[g].first;
-      std::vector<size_t> bound, written;
-      for (size_t a : l.input_args) {
-        if (a >= ins.size()) invalid("step " + id + " source has more arguments than the plan binds");
-        bound.push_back(ins[a]);
-      }
-      for (size_t k : parts[g].second) {
-        if (k >= outs.size()) invalid("step " + id + " source returns more results than the plan binds");
-        written.push_back(outs[k]);
-      }
-      const std::string sid = parts.size() > 1 ? id + "#" + std::to_string(g) : id;
-      o << (first ? "" : ",") << "{\"id\":" << json_str(sid) << ",\"recipe\":" << json_str(l.recipe)
-        << ",\"inputs\":" << list(bound) << ",\"outputs\":" << list(written) << "}";
+    const size_t internal0 = sizes.size();  // this step's internal buffers follow the plan's
+    for (uint64_t b : split.internal_bytes) sizes.push_back(b);
+    auto buffer = [&](int64_t x, const std::vector<size_t>& bound, const char* what) {
+      if (x < 0) return internal0 + size_t(-1 - x);
+      if (size_t(x) >= bound.size()) invalid("step " + id + " source has more " + what + " than the plan binds");
+      return bound[size_t(x)];
+    };
+    for (size_t g = 0; g < split.parts.size(); ++g) {
+      const Part& part = split.parts[g];
+      std::vector<size_t> read, written;
+      for (int64_t x : part.ins) read.push_back(buffer(x, ins, "arguments"));
+      for (int64_t x : part.outs) written.push_back(buffer(x, outs, "results"));
+      const std::string sid = split.parts.size() > 1 ? id + "#" + std::to_string(g) : id;
+      steps << (first ? "" : ",") << "{\"id\":" << json_str(sid) << ",\"recipe\":" << json_str(part.l.recipe)
+            << ",\"inputs\":" << list(read) << ",\"outputs\":" << list(written) << "}";
       first = false;
     }
   }
-  o << "]}";
+  std::ostringstream o;
+  o << "{\"buffer_sizes\":[";
+  for (size_t i = 0; i < sizes.size(); ++i) o << (i ? "," : "") << sizes[i];
+  o << "],\"inputs\":" << list(ids(plan.at("inputs"), "inputs")) << ",\"outputs\":" << list(ids(plan.at("outputs"), "outputs"))
+    << ",\"steps\":[" << steps.str() << "]}";
   return o.str();
 }
 

@@ -46,8 +46,10 @@ ASK_B200_API int ask_b200_lower_step(const char *step_source, char *buf, size_t 
  * shapes, reductions over different axes or operand shapes) becomes one
  * program step per group of results, ids "<step>#<k>", each writing its own
  * outputs -- the reference's one batch per output shape
- * (lib/Lowering/CUDA.cpp:210-244).  ask_b200_lower_step returns one recipe
- * and rejects such a step.
+ * (lib/Lowering/CUDA.cpp:210-244).  A gather or scatter_add whose operands
+ * are computed in the step reads them from internal buffers (appended after
+ * the plan's buffers) that elementwise steps write first.
+ * ask_b200_lower_step returns one recipe and rejects both kinds of step.
  */
 ASK_B200_API int ask_b200_lower_report(const char *report_json, char *buf, size_t cap, size_t *needed);
 

@@ -653,6 +653,78 @@ def test_steps_with_mixed_results_lower_to_one_recipe_per_group():
     assert [s["id"] for s in rt.lower_report(single)["steps"]] == ["kernel0"]
 
 
+def run_program_on_cpu(prog, inputs, dtypes):
+    """Runs a lowered program's steps in order on the CPU (test helper):
+    elementwise and reduce recipes through the recipe evaluator, gather and
+    scatter_add through the oracle.  `dtypes` gives each buffer's numpy type."""
+    import oracle
+    bufs = {b: np.ascontiguousarray(v).reshape(-1) for b, v in zip(prog["inputs"], inputs)}
+    for st in prog["steps"]:
+        rec = json.loads(st["recipe"])
+        ask_b200.Plan(rec, -1)
+        args = [bufs[b] for b in st["inputs"]]
+        if rec["family"] == "gather":
+            got = [oracle.gather(args[0], args[1], rec["outer"], rec["dim"], rec["inner"])]
+        elif rec["family"] == "scatter_add":
+            got = [oracle.scatter_add(rec["dtype"], args[0], args[1], args[2], rec["outer"], rec["dim"], rec["inner"])]
+        else:
+            got = recipe_eval.evaluate(rec, args)
+        for b, g in zip(st["outputs"], got):
+            bufs[b] = np.asarray(g).astype(dtypes[b]).reshape(-1)
+    return bufs
+
+
+def test_gather_and_scatter_of_computed_operands():
+    """A step gathering rows of a computed table at a computed index, and
+    a step scattering computed updates, lower to elementwise steps writing
+    internal buffers followed by the gather/scatter_add step; the program,
+    run step by step on the CPU, equals numpy."""
+    rows, dim, n = 40, 8, 300
+    g = Step("ask_kernel_0", "kernel0")
+    t, i = g.arg([rows, dim], "i32"), g.arg([n], "i64")
+    t2 = g.op("add", [g.op("mul", [t, g.splat(g.const(2, "i32"), [rows, dim])], [rows, dim], "i32"),
+                      g.splat(g.const(1, "i32"), [rows, dim])], [rows, dim], "i32")
+    i2 = g.op("add", [i, g.splat(g.const(3, "i64"), [n])], [n], "i64")
+    gsrc = g.text([g.op("gather", [t2, i2], [n, dim], "i32", "axis = 0 : i64")])
+    s = Step("ask_kernel_1", "kernel1")
+    base, idx, upd = s.arg([rows, dim], "i32"), s.arg([n], "i64"), s.arg([n, dim], "i32")
+    u2 = s.op("abs", [upd], [n, dim], "i32")
+    ssrc = s.text([s.op("scatter_add", [base, idx, u2], [rows, dim], "i32", "axis = 0 : i64")])
+    buffers = [{"id": "table", "shape": [rows, dim], "element_type": "i32"},
+               {"id": "idx", "shape": [n], "element_type": "i64"},
+               {"id": "base", "shape": [rows, dim], "element_type": "i32"},
+               {"id": "g", "shape": [n, dim], "element_type": "i32"},
+               {"id": "out", "shape": [rows, dim], "element_type": "i32"}]
+    rep = report([gsrc, ssrc], buffers, ["table", "idx", "base"], ["out"],
+                 [(["table", "idx"], ["g"]), (["base", "idx", "g"], ["out"])])
+    prog = rt.lower_report(rep)
+    # table * 2 + 1 and idx + 3 into internal buffers 5 and 6, then the gather;
+    # |g| into internal buffer 7, then the scatter_add
+    assert [st["id"] for st in prog["steps"]] == ["kernel0#0", "kernel0#1", "kernel0#2", "kernel1#0", "kernel1#1"]
+    assert len(prog["buffer_sizes"]) == 8 and prog["buffer_sizes"][5:] == [4 * rows * dim, 8 * n, 4 * n * dim]
+    assert [st["outputs"] for st in prog["steps"]] == [[5], [6], [3], [7], [4]]
+    assert prog["steps"][2]["inputs"] == [5, 6] and prog["steps"][4]["inputs"] == [2, 1, 7]
+    ok, why = rt.check_allocation({"buffer_count": len(prog["buffer_sizes"]), "public_inputs": prog["inputs"],
+                                   "public_outputs": prog["outputs"],
+                                   "steps": [{"inputs": st["inputs"], "outputs": st["outputs"]} for st in prog["steps"]]})
+    assert ok, why
+    rng = np.random.default_rng(8)
+    tv = rng.integers(-9, 9, (rows, dim)).astype(np.int32)
+    iv = rng.integers(-6, rows, n).astype(np.int64)  # idx + 3 falls outside [0, rows) at both ends
+    bv = rng.integers(-9, 9, (rows, dim)).astype(np.int32)
+    dtypes = {0: np.int32, 1: np.int64, 2: np.int32, 3: np.int32, 4: np.int32, 5: np.int32, 6: np.int64, 7: np.int32}
+    bufs = run_program_on_cpu(prog, [tv, iv, bv], dtypes)
+    table2, idx2 = tv * 2 + 1, iv + 3
+    ok_rows = (idx2 >= 0) & (idx2 < rows)
+    want_g = np.zeros((n, dim), np.int32)
+    want_g[ok_rows] = table2[idx2[ok_rows]]
+    assert np.array_equal(bufs[3].reshape(n, dim), want_g)
+    want_out = bv.copy()
+    in_range = (iv >= 0) & (iv < rows)
+    np.add.at(want_out, iv[in_range], np.abs(want_g[in_range]))
+    assert np.array_equal(bufs[4].reshape(rows, dim), want_out)
+
+
 def test_non_owned_steps_are_unsupported():
     r = softmax_report("f16", 8, 16)
     r["execution_plan"]["steps"][1]["kind"] = "external"
