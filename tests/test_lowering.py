@@ -725,6 +725,52 @@ def test_gather_and_scatter_of_computed_operands():
     assert np.array_equal(bufs[4].reshape(rows, dim), want_out)
 
 
+def random_mixed_step(seed):
+    """A rank-3 i32 argument with results: a sum and a max over random axis
+    sets (scattered ones included), an elementwise value and a strided slice
+    of another shape.  Returns (source, argument, [expected results], result
+    shapes)."""
+    rng = np.random.default_rng(seed)
+    shape = [int(x) for x in rng.integers(2, 6, 3)]
+    s = Step()
+    x = s.arg(shape, "i32")
+    xv = rng.integers(-30, 30, shape).astype(np.int32)
+    results, want = [], []
+    for op, f in (("reduce_sum", np.sum), ("reduce_max", np.max)):
+        axes = sorted(int(a) for a in rng.choice(3, int(rng.integers(1, 3)), replace=False))
+        kept = [shape[d] for d in range(3) if d not in axes]
+        results.append(s.op(op, [x], kept, "i32", "axes = " + arr(axes)))
+        want.append(f(xv, axis=tuple(axes)).astype(np.int32))
+    results.append(s.op("mul", [x, s.splat(s.const(3, "i32"), shape)], shape, "i32"))
+    want.append(xv * 3)
+    sl_shape = [(d + 1) // 2 for d in shape]
+    results.append(s.op("slice", [x], sl_shape, "i32", f"starts = {arr([0, 0, 0])}, stops = {arr(shape)}, "
+                                                     f"steps = {arr([2, 2, 2])}"))
+    want.append(xv[::2, ::2, ::2])
+    return s.text(results), xv, want, [list(w.shape) for w in want]
+
+
+def test_random_mixed_steps_through_reports():
+    """Random steps mixing reductions over different (and scattered) axis
+    sets with elementwise and sliced results lower through a partition report
+    to one program step per group, pass the plan verifier, and, run step by
+    step on the CPU, give numpy's results."""
+    for seed in range(60):
+        src, xv, want, shapes = random_mixed_step(seed)
+        buffers = [{"id": "x", "shape": list(xv.shape), "element_type": "i32"}] + \
+                  [{"id": f"r{k}", "shape": sh, "element_type": "i32"} for k, sh in enumerate(shapes)]
+        outs = [f"r{k}" for k in range(len(shapes))]
+        prog = rt.lower_report(report([src], buffers, ["x"], outs, [(["x"], outs)]))
+        ok, why = rt.check_allocation({"buffer_count": len(prog["buffer_sizes"]), "public_inputs": prog["inputs"],
+                                       "public_outputs": prog["outputs"],
+                                       "steps": [{"inputs": st["inputs"], "outputs": st["outputs"]}
+                                                 for st in prog["steps"]]})
+        assert ok, (seed, why)
+        bufs = run_program_on_cpu(prog, [xv], {b: np.int32 for b in range(len(prog["buffer_sizes"]))})
+        for k, w in enumerate(want):
+            assert np.array_equal(bufs[1 + k], w.reshape(-1)), (seed, k)
+
+
 def test_non_owned_steps_are_unsupported():
     r = softmax_report("f16", 8, 16)
     r["execution_plan"]["steps"][1]["kind"] = "external"
