@@ -1,4 +1,10 @@
 // Execution-plan verification and slot assignment (see plan_check.h).
+//
+// The verdicts and the diagnostic texts (and the order in which they are
+// reported) are the contract with callers of the reference's plan verifier
+// (lib/Pass/Pass.cpp:13-49, 96-209); the checks are organised here around
+// buffer lifetimes: each buffer's life runs from the step that writes it to
+// the last step that touches it, and a slot is a sequence of such lives.
 #include "plan_check.h"
 
 #include <algorithm>
@@ -10,44 +16,53 @@ namespace check {
 
 namespace {
 
-constexpr size_t kNone = SIZE_MAX;
+constexpr size_t kNone = SIZE_MAX;          // no writer (yet)
+constexpr size_t kCaller = SIZE_MAX - 1;    // public input: written by the caller before step 0
 
-// birth[b]: 0 for a public input, producing step + 1 otherwise.  Returns the
-// first structural error, or "" when every buffer has exactly one source.
-std::string births(const Plan& p, std::vector<size_t>& birth) {
-  birth.assign(p.buffer_count, kNone);
+// Who writes each buffer.  Returns the first structural error of the plan, or
+// "" when every buffer has exactly one writer (a step or the caller).  The
+// checks run in the order the reference reports them, so a plan with several
+// defects gets the same message.
+std::string find_writers(const Plan& p, std::vector<size_t>& writer) {
+  writer.assign(p.buffer_count, kNone);
+  const auto in_range = [&](size_t b) { return b < p.buffer_count; };
   for (size_t b : p.public_inputs) {
-    if (b >= p.buffer_count) return "public input buffer index is out of range";
-    if (birth[b] != kNone) return "public input buffer is repeated";
-    birth[b] = 0;
+    if (!in_range(b)) return "public input buffer index is out of range";
+    if (writer[b] == kCaller) return "public input buffer is repeated";
+    writer[b] = kCaller;
   }
   for (size_t s = 0; s < p.steps.size(); ++s) {
-    for (size_t b : p.steps[s].inputs)
-      if (b >= p.buffer_count) return "step input buffer index is out of range";
-    for (size_t b : p.steps[s].outputs) {
-      if (b >= p.buffer_count) return "step output buffer index is out of range";
-      if (birth[b] != kNone) return "buffer has multiple writers or aliases a public input";
-      birth[b] = s + 1;
+    const StepPorts& step = p.steps[s];
+    if (!std::all_of(step.inputs.begin(), step.inputs.end(), in_range))
+      return "step input buffer index is out of range";
+    for (size_t b : step.outputs) {
+      if (!in_range(b)) return "step output buffer index is out of range";
+      if (writer[b] != kNone) return "buffer has multiple writers or aliases a public input";
+      writer[b] = s;
     }
   }
   if (p.public_outputs.empty()) return "plan must have a public output";
-  for (size_t b : p.public_outputs)
-    if (b >= p.buffer_count) return "public output buffer index is out of range";
-  for (size_t v : birth)
-    if (v == kNone) return "plan contains a buffer without a writer";
+  if (!std::all_of(p.public_outputs.begin(), p.public_outputs.end(), in_range))
+    return "public output buffer index is out of range";
+  if (std::find(writer.begin(), writer.end(), kNone) != writer.end()) return "plan contains a buffer without a writer";
   return {};
 }
 
-void fail(std::string& out, const std::string& name) {
+void report(std::string& out, const std::string& name) {
   out += "verify ";
   out += name;
   out += " FAIL\n";
 }
 
-void check_reads(const Plan& p, const std::vector<size_t>& birth, std::string& out) {
-  for (size_t s = 0; s < p.steps.size(); ++s)
-    for (size_t port = 0; port < p.steps[s].inputs.size(); ++port)
-      if (birth[p.steps[s].inputs[port]] > s) fail(out, "READ_" + std::to_string(s) + "_" + std::to_string(port));
+// A step may read a buffer only once the caller or an earlier step wrote it.
+void report_early_reads(const Plan& p, const std::vector<size_t>& writer, std::string& out) {
+  for (size_t s = 0; s < p.steps.size(); ++s) {
+    const std::vector<size_t>& in = p.steps[s].inputs;
+    for (size_t port = 0; port < in.size(); ++port) {
+      const size_t w = writer[in[port]];
+      if (w != kCaller && w >= s) report(out, "READ_" + std::to_string(s) + "_" + std::to_string(port));
+    }
+  }
 }
 
 // Ancestor marking over a dependency DAG: mark(step, floor) visits every
@@ -74,109 +89,123 @@ class Ancestors {
   std::vector<size_t> stack_;
 };
 
+// The life of one slot occupant: written at `from`, last touched at `to`.
+struct Life {
+  size_t from, to, buffer;
+  bool operator<(const Life& o) const { return from != o.from ? from < o.from : buffer < o.buffer; }
+};
+
+// Shape of the mapping itself: every internal buffer in exactly one slot, no
+// public buffer in a slot, no empty slot.  Fills the occupants of each slot.
+std::string place_buffers(const Allocation& a, std::vector<std::vector<size_t>>& occupants) {
+  const Plan& p = a.plan;
+  std::vector<char> role(p.buffer_count, 0);  // 1 public, 2 placed internal
+  for (size_t b : p.public_inputs) role[b] = 1;
+  for (size_t b : p.public_outputs) role[b] = 1;
+  occupants.assign(a.slot_capacity_bytes.size(), {});
+  for (const SlotAssignment& e : a.assignments) {
+    if (e.buffer >= p.buffer_count || e.slot >= occupants.size()) return "allocation assignment index is out of range";
+    if (role[e.buffer] == 1) return "public port cannot use an internal slot";
+    if (role[e.buffer] == 2) return "internal buffer has multiple slot assignments";
+    role[e.buffer] = 2;
+    occupants[e.slot].push_back(e.buffer);
+  }
+  if (std::find(role.begin(), role.end(), 0) != role.end()) return "internal buffer has no slot assignment";
+  for (const auto& o : occupants)
+    if (o.empty()) return "allocation contains an unused slot";
+  return {};
+}
+
+// Graph mode: each step lists earlier steps, each at most once; stream mode
+// has no edges (stream order is the order).
+std::string check_edges(const Allocation& a) {
+  const size_t n = a.plan.steps.size();
+  if (!a.graph) return a.dependencies.empty() ? std::string() : "stream plan contains graph dependencies";
+  if (a.dependencies.size() != n) return "graph dependency count differs from the plan";
+  for (size_t s = 0; s < n; ++s) {
+    const std::vector<size_t>& d = a.dependencies[s];
+    if (std::any_of(d.begin(), d.end(), [s](size_t x) { return x >= s; }))
+      return "graph dependency is not topologically ordered";
+    std::vector<size_t> sorted(d);
+    std::sort(sorted.begin(), sorted.end());
+    if (std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end()) return "graph dependency is repeated";
+  }
+  return {};
+}
+
 }  // namespace
 
 Verdict check_plan(const Plan& plan) {
-  std::vector<size_t> birth;
-  std::string error = births(plan, birth);
+  std::vector<size_t> writer;
+  std::string error = find_writers(plan, writer);
   if (!error.empty()) return {false, error};
   std::string out;
-  check_reads(plan, birth, out);
+  report_early_reads(plan, writer, out);
   return {out.empty(), out};
 }
 
 Verdict check_allocation(const Allocation& a) {
   const Plan& p = a.plan;
   const size_t n = p.steps.size();
-  std::vector<size_t> birth;
-  std::string error = births(p, birth);
+  std::vector<size_t> writer;
+  std::string error = find_writers(p, writer);
+  if (error.empty() && a.buffer_sizes.size() != p.buffer_count) error = "allocation buffer sizes differ from the plan";
+  std::vector<std::vector<size_t>> occupants;
+  if (error.empty()) error = place_buffers(a, occupants);
+  if (error.empty()) error = check_edges(a);
   if (!error.empty()) return {false, error};
-  if (a.buffer_sizes.size() != p.buffer_count) return {false, "allocation buffer sizes differ from the plan"};
 
-  std::vector<char> is_public(p.buffer_count, 0), placed(p.buffer_count, 0);
-  for (size_t b : p.public_inputs) is_public[b] = 1;
-  for (size_t b : p.public_outputs) is_public[b] = 1;
-  std::vector<std::vector<size_t>> occupants(a.slot_capacity_bytes.size());
-  for (const SlotAssignment& e : a.assignments) {
-    if (e.buffer >= p.buffer_count || e.slot >= occupants.size())
-      return {false, "allocation assignment index is out of range"};
-    if (is_public[e.buffer]) return {false, "public port cannot use an internal slot"};
-    if (placed[e.buffer]) return {false, "internal buffer has multiple slot assignments"};
-    placed[e.buffer] = 1;
-    occupants[e.slot].push_back(e.buffer);
-  }
-  for (size_t b = 0; b < p.buffer_count; ++b)
-    if (!is_public[b] && !placed[b]) return {false, "internal buffer has no slot assignment"};
-  for (const auto& o : occupants)
-    if (o.empty()) return {false, "allocation contains an unused slot"};
-
-  if (a.graph) {
-    if (a.dependencies.size() != n) return {false, "graph dependency count differs from the plan"};
-    for (size_t s = 0; s < n; ++s) {
-      std::vector<size_t> d = a.dependencies[s];
-      for (size_t x : d)
-        if (x >= s) return {false, "graph dependency is not topologically ordered"};
-      std::sort(d.begin(), d.end());
-      if (std::adjacent_find(d.begin(), d.end()) != d.end()) return {false, "graph dependency is repeated"};
-    }
-  } else if (!a.dependencies.empty()) {
-    return {false, "stream plan contains graph dependencies"};
-  }
-
-  // Last access of each buffer (its producer counts as an access, so an
-  // unread buffer is live at its producing step); graph mode keeps them all.
-  std::vector<size_t> last(p.buffer_count, 0);
-  std::vector<std::vector<size_t>> touched(a.graph ? p.buffer_count : 0);
-  for (size_t s = 0; s < n; ++s) {
-    for (const auto* list : {&p.steps[s].outputs, &p.steps[s].inputs})
-      for (size_t b : *list) {
-        last[b] = std::max(last[b], s);
-        if (a.graph) touched[b].push_back(s);
-      }
-  }
+  // Steps touching each buffer, ascending (a writer counts: an unread buffer
+  // is alive at the step that writes it).
+  std::vector<std::vector<size_t>> touches(p.buffer_count);
+  for (size_t s = 0; s < n; ++s)
+    for (const auto* ports : {&p.steps[s].outputs, &p.steps[s].inputs})
+      for (size_t b : *ports)
+        if (touches[b].empty() || touches[b].back() != s) touches[b].push_back(s);
 
   std::string out;
-  check_reads(p, birth, out);
+  report_early_reads(p, writer, out);
   for (const SlotAssignment& e : a.assignments)
-    if (a.buffer_sizes[e.buffer] > a.slot_capacity_bytes[e.slot]) fail(out, "CAPACITY_" + std::to_string(e.buffer));
+    if (a.buffer_sizes[e.buffer] > a.slot_capacity_bytes[e.slot]) report(out, "CAPACITY_" + std::to_string(e.buffer));
 
-  std::vector<std::vector<size_t>> precede(a.graph ? n : 0);  // steps that must come before step s
-  if (a.graph)
-    for (size_t s = 0; s < n; ++s)
-      for (size_t b : p.steps[s].inputs)
-        if (birth[b] > 0) precede[s].push_back(birth[b] - 1);
-  // Consecutive occupants of a slot in production order: the earlier one must
-  // be dead before the later one is written.  Ordering each adjacent pair
-  // orders every earlier occupant too, since an occupant's producer is one of
-  // its accesses.
-  for (auto& o : occupants) {
-    std::sort(o.begin(), o.end(), [&](size_t x, size_t y) { return std::make_pair(birth[x], x) < std::make_pair(birth[y], y); });
-    for (size_t i = 1; i < o.size(); ++i) {
-      const size_t older = o[i - 1], newer = o[i], writer = birth[newer] - 1;
-      if (a.graph)
-        precede[writer].insert(precede[writer].end(), touched[older].begin(), touched[older].end());
-      else if (last[older] >= writer)
-        fail(out, "ADJACENT_" + std::to_string(older) + "_" + std::to_string(newer));
+  // Each slot's lives in the order they begin.  A life must not begin before
+  // the previous one in its slot has ended: in stream order that is a
+  // comparison of step indices; in graph order every step that touched the
+  // previous occupant must be an ancestor of the new writer.
+  std::vector<std::vector<size_t>> must_precede(a.graph ? n : 0);
+  for (const auto& slot : occupants) {
+    std::vector<Life> lives;
+    lives.reserve(slot.size());
+    for (size_t b : slot) lives.push_back({writer[b], touches[b].back(), b});
+    std::sort(lives.begin(), lives.end());
+    for (size_t i = 1; i < lives.size(); ++i) {
+      const Life& prev = lives[i - 1];
+      const Life& next = lives[i];
+      if (a.graph) {
+        const auto& t = touches[prev.buffer];
+        must_precede[next.from].insert(must_precede[next.from].end(), t.begin(), t.end());
+      } else if (prev.to >= next.from) {
+        report(out, "ADJACENT_" + std::to_string(prev.buffer) + "_" + std::to_string(next.buffer));
+      }
     }
   }
-  if (a.graph) {
-    Ancestors anc(a.dependencies);
-    for (size_t s = 0; s < n; ++s) {
-      auto& req = precede[s];
-      if (req.empty()) continue;
-      std::sort(req.begin(), req.end());
-      req.erase(std::unique(req.begin(), req.end()), req.end());
-      if (req.back() >= s) {
-        fail(out, "GRAPH_ORDER_" + std::to_string(s));
-        continue;
-      }
-      anc.mark(s, req.front());
-      for (size_t x : req)
-        if (!anc.is_ancestor(x, s)) {
-          fail(out, "GRAPH_ORDER_" + std::to_string(s));
-          break;
-        }
+  if (!a.graph) return {out.empty(), out};
+
+  // Graph order: a step also needs a path from the writer of everything it
+  // reads.  One ancestor walk per step, cut off below its earliest need.
+  Ancestors anc(a.dependencies);
+  for (size_t s = 0; s < n; ++s) {
+    std::vector<size_t>& need = must_precede[s];
+    for (size_t b : p.steps[s].inputs)
+      if (writer[b] != kCaller) need.push_back(writer[b]);
+    if (need.empty()) continue;
+    const auto [lo, hi] = std::minmax_element(need.begin(), need.end());
+    bool ordered = *hi < s;
+    if (ordered) {
+      anc.mark(s, *lo);
+      ordered = std::all_of(need.begin(), need.end(), [&](size_t x) { return anc.is_ancestor(x, s); });
     }
+    if (!ordered) report(out, "GRAPH_ORDER_" + std::to_string(s));
   }
   return {out.empty(), out};
 }

@@ -347,3 +347,65 @@ def test_reference_pass_checker_was_compared():
         pytest.skip("the reference's PASS checker is not built here (oracle/_ref)")
     ok, text = REF.pass_check(chain(4))
     assert ok and text == ""
+
+
+# ---- random plans, defects included, against the reference's checker -----------------
+def _random_allocation(rng):
+    """A random plan, mapping and (in graph mode) edge list.  Roughly half are
+    built valid and then perturbed once: a buffer moved to another slot, a
+    capacity cut, an edge dropped or a structural defect (bad index, second
+    writer, unused slot, public buffer in a slot)."""
+    nsteps = rng.randint(1, 9)
+    nin = rng.randint(1, 3)
+    bufs = nin
+    steps = []
+    for s in range(nsteps):
+        reads = rng.sample(range(bufs), rng.randint(1, min(3, bufs)))
+        writes = list(range(bufs, bufs + rng.randint(1, 2)))
+        bufs += len(writes)
+        steps.append((reads, writes))
+    outputs = sorted(rng.sample(range(nin, bufs), rng.randint(1, min(2, bufs - nin))))
+    p = plan(bufs, range(nin), outputs, steps)
+    graph = rng.random() < 0.5
+    sizes = [rng.choice([0, 8, 16, 64]) for _ in range(bufs)]
+    out = rt.assign_slots(dict(p, buffer_sizes=sizes), graph)
+    a = dict(p, buffer_sizes=sizes, **out)
+    a["assignments"] = [list(x) for x in a["assignments"]]
+    kind = rng.randrange(9)
+    if kind == 0 and len(a["slot_capacity_bytes"]) > 1 and a["assignments"]:
+        e = rng.choice(a["assignments"])
+        e[1] = rng.randrange(len(a["slot_capacity_bytes"]))
+    elif kind == 1 and a["slot_capacity_bytes"]:
+        k = rng.randrange(len(a["slot_capacity_bytes"]))
+        a["slot_capacity_bytes"][k] = max(0, a["slot_capacity_bytes"][k] - 8)
+    elif kind == 2 and graph:
+        deps = [d for d in a["dependencies"] if d]
+        if deps:
+            d = rng.choice(deps)
+            d.pop(rng.randrange(len(d)))
+    elif kind == 3:
+        st = rng.choice(a["steps"])
+        st[rng.choice(["inputs", "outputs"])].append(rng.choice([bufs, bufs + 3, 0]))
+    elif kind == 4:
+        a["slot_capacity_bytes"].append(16)
+    elif kind == 5 and a["assignments"]:
+        a["assignments"].append([rng.choice(outputs), 0])
+    elif kind == 6:
+        rng.shuffle(a["steps"])
+        if graph:
+            a["dependencies"] = [[x for x in d if x < s] for s, d in enumerate(a["dependencies"])]
+    elif kind == 7:
+        a["public_outputs"] = [] if rng.random() < 0.5 else [bufs + 1]
+    return a
+
+
+@pytest.mark.skipif(REF is None, reason="the reference's PASS checker is not built here (oracle/_ref)")
+def test_random_allocations_match_the_reference_checker():
+    rng = random.Random(0xA5C)
+    verdicts = set()
+    for _ in range(3000):
+        a = _random_allocation(rng)
+        ours = rt.check_allocation(a)
+        assert REF.pass_check(a) == ours, a
+        verdicts.add(ours[0])
+    assert verdicts == {True, False}
