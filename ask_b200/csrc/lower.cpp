@@ -49,6 +49,9 @@
 #include "ask_b200_lower.h"
 #include "json.h"
 
+// plan.cpp: the cuda_lowering report of a recipe (its host-only plan's).
+std::string askb_recipe_lowering_report(const std::string& recipe_json, long pre_copy_input);
+
 extern "C" void askb_internal_set_error(const char* message);
 
 namespace askb {
@@ -1709,12 +1712,28 @@ std::string lower_report(const char* report_json) {
     return o + "]";
   };
   std::ostringstream steps;
+  std::vector<std::string> unresolved;
   bool first = true;
   for (const auto& step : plan.at("steps").as_array("steps")) {
     const std::string id = step.at("id").as_str("step id");
     const json::Value* kind = step.get("kind");
-    if (kind && kind->as_str("kind") != "owned")
-      unsupported("step " + id + " is a '" + kind->str + "' step; only owned steps lower to recipes");
+    if (kind && kind->as_str("kind") != "owned") {
+      // An external or library step keeps its place and its buffers; the
+      // caller binds a loaded kernel to it ("kernel", "grid", "block",
+      // "arguments") before preparing the program.
+      const std::string k = kind->str;
+      if (k != "external" && k != "library") invalid("step " + id + " has unknown kind '" + k + "'");
+      std::string what = "{\"kind\":" + json_str(k);
+      for (const char* key : {"function", "external_id", "library"})
+        if (const json::Value* v = step.get(key)) what += std::string(",\"") + key + "\":" + json_str(v->as_str(key));
+      what += "}";
+      steps << (first ? "" : ",") << "{\"id\":" << json_str(id) << ",\"unresolved\":" << what
+            << ",\"inputs\":" << list(ids(step.at("inputs"), "step inputs"))
+            << ",\"outputs\":" << list(ids(step.at("outputs"), "step outputs")) << "}";
+      first = false;
+      unresolved.push_back(id);
+      continue;
+    }
     const json::Value* src = sources->get(id);
     if (!src) invalid("no step source for " + id);
     Split split;
@@ -1738,8 +1757,10 @@ std::string lower_report(const char* report_json) {
       for (int64_t x : part.ins) read.push_back(buffer(x, ins, "arguments"));
       for (int64_t x : part.outs) written.push_back(buffer(x, outs, "results"));
       const std::string sid = split.parts.size() > 1 ? id + "#" + std::to_string(g) : id;
+      const long base_arg = part.ins.empty() ? 0 : long(part.ins[0]);
       steps << (first ? "" : ",") << "{\"id\":" << json_str(sid) << ",\"recipe\":" << json_str(part.l.recipe)
-            << ",\"inputs\":" << list(read) << ",\"outputs\":" << list(written) << "}";
+            << ",\"inputs\":" << list(read) << ",\"outputs\":" << list(written)
+            << ",\"cuda_lowering\":" << askb_recipe_lowering_report(part.l.recipe, base_arg) << "}";
       first = false;
     }
   }
@@ -1747,7 +1768,13 @@ std::string lower_report(const char* report_json) {
   o << "{\"buffer_sizes\":[";
   for (size_t i = 0; i < sizes.size(); ++i) o << (i ? "," : "") << sizes[i];
   o << "],\"inputs\":" << list(ids(plan.at("inputs"), "inputs")) << ",\"outputs\":" << list(ids(plan.at("outputs"), "outputs"))
-    << ",\"steps\":[" << steps.str() << "]}";
+    << ",\"steps\":[" << steps.str() << "]";
+  if (!unresolved.empty()) {
+    o << ",\"unresolved_steps\":[";
+    for (size_t i = 0; i < unresolved.size(); ++i) o << (i ? "," : "") << json_str(unresolved[i]);
+    o << "]";
+  }
+  o << "}";
   return o.str();
 }
 
@@ -1792,7 +1819,10 @@ int ask_b200_lower_step(const char* step_source, char* buf, size_t cap, size_t* 
     std::string ports = "[";
     for (size_t k = 0; k < l.input_args.size(); ++k) ports += (k ? "," : "") + std::to_string(l.input_args[k]);
     ports += "]";
-    write_text("{\"recipe\":" + l.recipe + ",\"input_arguments\":" + ports + "}", buf, cap, needed);
+    const long base_arg = l.input_args.empty() ? 0 : long(l.input_args[0]);
+    write_text("{\"recipe\":" + l.recipe + ",\"input_arguments\":" + ports +
+                   ",\"cuda_lowering\":" + askb_recipe_lowering_report(l.recipe, base_arg) + "}",
+               buf, cap, needed);
   });
 }
 

@@ -762,6 +762,47 @@ void build_softmax(ask_b200_plan& pl, const json::Value& r) {
   pl.block = int(a.cols / 8 / uint64_t(vpt));
 }
 
+// The diagnostics the reference's CUDA lowering reports for a step
+// (lib/Lowering/CUDA.cpp:408-417, "cuda_lowering"), for the kernels this plan
+// launches: the same fields with the same meaning, plus the plan's strategy.
+// indexing is "cooperative_grid_stride" when outputs are reduced by a warp
+// each (the reference's warp reduction), else "linear_grid_stride";
+// reduction_loop_count counts passes over the reduced domain (one: every
+// reduction of a step folds in the same pass); input_load_count counts input
+// ports, each read once per element.  pre_copy names the step's base input.
+std::string cuda_lowering(const ask_b200_plan& pl, long pre_copy_input) {
+  const bool reduce = pl.family == FAM_REDUCE, softmax = pl.family == FAM_SOFTMAX;
+  const bool warp = (reduce && !pl.views && pl.strategy == RS_WARP_ROW) || softmax;
+  const int block = pl.family == FAM_ELEMENTWISE ? kEwThreads : reduce ? kRedThreads : softmax ? pl.block : 256;
+  size_t empty = 0;
+  std::ostringstream outs;
+  for (size_t k = 0; k < pl.outputs.size(); ++k) {
+    if (pl.outputs[k].elements == 0) { ++empty; continue; }
+    outs << (outs.tellp() > 0 ? "," : "") << k;
+  }
+  uint64_t count = pl.outputs.empty() ? 0 : pl.outputs[0].elements;
+  if (pl.family == FAM_SCATTER && pl.inputs.size() > 2) count = pl.inputs[2].elements;
+  if (softmax) count = pl.sm.rows;
+  uint64_t per_output = warp ? (softmax ? uint64_t(pl.block) : 32) : 1;
+  if (reduce && !pl.views && pl.strategy == RS_SPLIT) per_output = uint64_t(pl.grid) * uint64_t(block);
+  const char* strat[] = {"warp_row", "column", "split"};
+  std::ostringstream o;
+  o << "{\"statistics_stage\":\"cuda_lowering\",\"kernel_count\":" << pl.launches << ",\"indexing\":\""
+    << (warp ? "cooperative_grid_stride" : "linear_grid_stride") << "\",\"warp_reduction_groups\":" << (warp ? 1 : 0)
+    << ",\"output_loop_count\":" << (pl.outputs.size() > empty ? 1 : 0) << ",\"input_load_count\":" << pl.inputs.size()
+    << ",\"reduction_loop_count\":" << (reduce || softmax ? 1 : 0) << ",\"zero_element_outputs\":" << empty
+    << ",\"temporary_buffer_count\":0,\"scratch_bytes\":" << pl.scratch << ",\"groups\":[";
+  if (pl.outputs.size() > empty)
+    o << "{\"outputs\":[" << outs.str() << "],\"element_count\":" << count << ",\"threads_per_output\":" << per_output
+      << "}";
+  o << "],\"bool_storage\":\"one-byte-zero-or-one\",\"cast_semantics\":\"rne-saturating-fptosi-nan-zero-v1\","
+    << "\"kernel\":\"" << pl.kernel << "\",\"strategy\":\""
+    << (reduce ? (pl.views ? "view" : strat[pl.strategy]) : kFamilyNames[pl.family]) << "\"";
+  if (pl.family == FAM_SCATTER) o << ",\"pre_copy\":{\"input\":" << pre_copy_input << ",\"output\":0}";
+  o << "}";
+  return o.str();
+}
+
 std::string describe(const ask_b200_plan& pl) {
   std::ostringstream o;
   o << "{\"format\":\"ask-b200-recipe\",\"abi_version\":" << ASK_B200_ABI_VERSION << ",\"family\":\""
@@ -808,7 +849,7 @@ std::string describe(const ask_b200_plan& pl) {
       first = false;
     }
   o << "],\"requires_disjoint_outputs\":true,\"outputs_must_not_alias_inputs\":"
-    << (pl.family == FAM_SCATTER ? "false" : "true") << "}";
+    << (pl.family == FAM_SCATTER ? "false" : "true") << ",\"cuda_lowering\":" << cuda_lowering(pl, 0) << "}";
   return o.str();
 }
 
@@ -1002,6 +1043,16 @@ const double* zipf_table(int device, double s, uint64_t n) {
 }
 
 }  // namespace
+
+// The lowering adapter's cuda_lowering report (lower.cpp): that of the
+// recipe's host-only plan, with the scatter base named by the step's argument.
+std::string askb_recipe_lowering_report(const std::string& recipe_json, long pre_copy_input) {
+  ask_b200_plan* p = nullptr;
+  if (ask_b200_plan_create(recipe_json.c_str(), -1, &p) != ASK_B200_OK)
+    throw std::runtime_error(std::string("lowered recipe: ") + ask_b200_last_error());
+  std::unique_ptr<ask_b200_plan> owned(p);
+  return cuda_lowering(*owned, pre_copy_input);
+}
 
 extern "C" {
 

@@ -30,9 +30,17 @@ extern "C" {
 
 /*
  * One step source (a module holding one func.func of ASK ops) to
- * {"recipe": {...}, "input_arguments": [k, ...]}: recipe input port i reads the
- * function's argument input_arguments[i]; outputs follow the function's return
- * order.  Text is written as by ask_b200_plan_describe.
+ * {"recipe": {...}, "input_arguments": [k, ...], "cuda_lowering": {...}}:
+ * recipe input port i reads the function's argument input_arguments[i];
+ * outputs follow the function's return order.  "cuda_lowering" carries the
+ * diagnostics fields of the reference's CUDA lowering report
+ * (lib/Lowering/CUDA.cpp:408-417: statistics_stage, kernel_count, indexing,
+ * warp_reduction_groups, output_loop_count, input_load_count,
+ * reduction_loop_count, zero_element_outputs, temporary_buffer_count, groups,
+ * bool_storage, cast_semantics and, for scatter_add, pre_copy {input:
+ * argument of the base, output}) for the kernels this library launches, plus
+ * "kernel", "strategy" and "scratch_bytes".  Text is written as by
+ * ask_b200_plan_describe.
  */
 ASK_B200_API int ask_b200_lower_step(const char *step_source, char *buf, size_t cap, size_t *needed);
 
@@ -48,7 +56,13 @@ ASK_B200_API int ask_b200_lower_step(const char *step_source, char *buf, size_t 
  * outputs -- the reference's one batch per output shape
  * (lib/Lowering/CUDA.cpp:210-244).  A gather or scatter_add whose operands
  * are computed in the step reads them from internal buffers (appended after
- * the plan's buffers) that elementwise steps write first.
+ * the plan's buffers) that elementwise steps write first.  Each recipe step
+ * carries its "cuda_lowering" report.  External and library steps keep their
+ * place and buffers as {"id", "unresolved": {"kind", "function",
+ * "external_id" | "library"}, "inputs", "outputs"}, listed again in
+ * "unresolved_steps": the caller replaces "unresolved" with a loaded kernel
+ * ("kernel", "grid", "block", "arguments"; ask_b200_program_prepare_kernels)
+ * before preparing the program.
  * ask_b200_lower_step returns one recipe and rejects both kinds of step.
  */
 ASK_B200_API int ask_b200_lower_report(const char *report_json, char *buf, size_t cap, size_t *needed);

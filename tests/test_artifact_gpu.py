@@ -332,3 +332,34 @@ def test_graph_program_rebinds_ports(session):
         assert np.array_equal(tout.cpu().numpy(), oracle.cfg5b(x, y))
     st = session.stats()
     assert st["graph_instantiations"] >= 1 and st["graph_node_updates"] >= 1
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_partition_report_with_an_external_step(session, graph):
+    """The execution plan of the reference's partitioning document (an owned
+    step, then an external step): the owned step is lowered to a recipe, the
+    external step -- left unresolved by the lowering -- is bound to a loaded
+    kernel artifact (here y = tmp + 1), and the program runs both."""
+    from test_lowering import partitioning_doc_report
+    prog = rt.lower_report(partitioning_doc_report())
+    assert prog["unresolved_steps"] == ["k1"]
+    p = R.Program()
+    t = p.input("f32")
+    plus_one = R.elementwise(p, [p.op("add", t, p.const("f32", 1.0))], 128)
+    art, types = artifact_for(plus_one, grid=1)
+    kernel = A.load_artifact(session, art, ["f32"])
+    steps = []
+    for s in prog["steps"]:
+        if "unresolved" in s:
+            steps.append(A.artifact_step(art, kernel, s["inputs"], s["outputs"], types))
+        else:
+            steps.append(rt.PlanStep(recipe=s["recipe"], inputs=s["inputs"], outputs=s["outputs"]))
+    program = session.prepareProgram(prog["buffer_sizes"], prog["inputs"], prog["outputs"], steps, graph=graph)
+    x = np.random.default_rng(7).uniform(-4, 4, 128).astype(np.float32)
+    dx = to_dev(x)
+    dy = torch.zeros(128, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    program.submit([session.importTensor(dx, readonly=True)], [session.importTensor(dy)]).wait()
+    want = np.exp(x.astype(np.float64)) + 1.0
+    got = dy.cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(got - want) <= 4 * np.spacing(want.astype(np.float32)).astype(np.float64))

@@ -771,12 +771,20 @@ def test_random_mixed_steps_through_reports():
             assert np.array_equal(bufs[1 + k], w.reshape(-1)), (seed, k)
 
 
-def test_non_owned_steps_are_unsupported():
+def test_non_owned_steps_stay_for_the_caller():
+    """An external or library step is not lowered: it keeps its buffers and is
+    listed as unresolved, for the caller to bind a loaded kernel to it; a step
+    of unknown kind is invalid."""
     r = softmax_report("f16", 8, 16)
     r["execution_plan"]["steps"][1]["kind"] = "external"
+    prog = rt.lower_report(r)
+    assert prog["unresolved_steps"] == ["kernel1"]
+    assert prog["steps"][1] == {"id": "kernel1", "unresolved": {"kind": "external", "function": "ask_kernel_1"},
+                                "inputs": [0, 1], "outputs": [2]}
+    r["execution_plan"]["steps"][1]["kind"] = "fused"
     with pytest.raises(rt.CUDAError) as err:
         rt.lower_report(r)
-    assert err.value.status == ask_b200.E_UNSUPPORTED
+    assert err.value.status == ask_b200.E_INVALID
 
 
 # ---- on the GPU: lowered programs against the hand-written recipes ------------------------
@@ -1405,3 +1413,87 @@ def test_random_reduce_steps_on_gpu(device):
             assert np.array_equal(got.cpu().numpy(), np.asarray(w).reshape(-1)), seed
         checked += 1
     assert checked >= 30
+
+
+# ---- the reference's own documented formats ---------------------------------------------
+# The graph of docs/en/api.md:34-43, as the reference documents it: a module
+# with attributes, named arguments, no ask.* attributes on ops, one result.
+API_DOC_INCREMENT = """module attributes {ask.schema_version = 1 : i64} {
+  func.func @increment(%x: tensor<4xi32>) -> tensor<4xi32> {
+    %one = "ask.constant"() {value = 1 : i32} : () -> i32
+    %ones = "ask.splat"(%one) {shape = array<i64: 4>} : (i32) -> tensor<4xi32>
+    %y = "ask.add"(%x, %ones) {overflow = "wrap"} : (tensor<4xi32>, tensor<4xi32>) -> tensor<4xi32>
+    return %y : tensor<4xi32>
+  }
+}
+"""
+
+
+def test_api_doc_graph_lowers():
+    out = rt.lower_step(API_DOC_INCREMENT)
+    assert out["input_arguments"] == [0]
+    x = np.array([0, -1, 2 ** 31 - 1, 7], np.int32)
+    (y,) = recipe_eval.evaluate(out["recipe"], [x])
+    assert np.array_equal(y, x + np.int32(1))  # wrapping add: 2^31 - 1 + 1 = -2^31
+    ask_b200.Plan(out["recipe"], -1)
+
+
+def partitioning_doc_report():
+    """The execution plan of docs/en/partitioning.md:21-41 (an owned step, then
+    an external step), with a step source for the owned step in the form the
+    reference's partitioner prints (keyed by step id, Partition.cpp:272)."""
+    plan = {"schema_version": 1, "kind": "ask.cuda.execution_plan", "inputs": ["x"], "outputs": ["y"],
+            "buffers": [{"id": "x", "shape": [128], "element_type": "f32"},
+                        {"id": "tmp", "shape": [128], "element_type": "f32"},
+                        {"id": "y", "shape": [128], "element_type": "f32"}],
+            "steps": [{"id": "k0", "kind": "owned", "function": "kernel_0", "inputs": ["x"], "outputs": ["tmp"],
+                       "depends_on": []},
+                      {"id": "k1", "kind": "external", "function": "kernel_1", "inputs": ["tmp"], "outputs": ["y"],
+                       "depends_on": ["k0"], "external_id": "graph.external0"}],
+            "scheduling": {"policy": "sequential", "stream": "session"}}
+    k0 = ("module attributes {ask.schema_version = 1 : i64} {\n"
+          "  func.func @kernel_0(%arg0: tensor<128xf32>) -> tensor<128xf32> attributes {ask.kernel_id = \"k0\", "
+          "ask.kernel_kind = \"owned\"} {\n"
+          "    %0 = \"ask.exp\"(%arg0) : (tensor<128xf32>) -> tensor<128xf32>\n"
+          "    return %0 : tensor<128xf32>\n  }\n}\n")
+    return {"phase": "partitioned", "execution_plan": plan, "step_sources": {"k0": k0}, "external_requests": []}
+
+
+def test_partitioning_doc_plan_keeps_its_external_step():
+    prog = rt.lower_report(partitioning_doc_report())
+    assert prog["buffer_sizes"] == [512, 512, 512] and prog["inputs"] == [0] and prog["outputs"] == [2]
+    owned, ext = prog["steps"]
+    assert owned["id"] == "k0" and owned["inputs"] == [0] and owned["outputs"] == [1]
+    assert json.loads(owned["recipe"])["program"] == [["input", 0], ["exp", 0]]
+    assert ext == {"id": "k1", "unresolved": {"kind": "external", "function": "kernel_1",
+                                              "external_id": "graph.external0"}, "inputs": [1], "outputs": [2]}
+    assert prog["unresolved_steps"] == ["k1"]
+
+
+REPORT_FIELDS = {"statistics_stage", "kernel_count", "indexing", "warp_reduction_groups", "output_loop_count",
+                 "input_load_count", "reduction_loop_count", "zero_element_outputs", "temporary_buffer_count",
+                 "groups", "bool_storage", "cast_semantics"}
+
+
+def test_cuda_lowering_report():
+    """The fields of the reference's cuda_lowering diagnostics
+    (lib/Lowering/CUDA.cpp:408-417), describing this library's kernels."""
+    r1 = rt.lower_step(cfg1_source())["cuda_lowering"]
+    assert REPORT_FIELDS <= set(r1) and "pre_copy" not in r1
+    assert (r1["statistics_stage"], r1["indexing"], r1["warp_reduction_groups"], r1["output_loop_count"],
+            r1["input_load_count"], r1["reduction_loop_count"], r1["kernel_count"]) == (
+        "cuda_lowering", "linear_grid_stride", 0, 1, 3, 0, 1)
+    assert r1["groups"] == [{"outputs": [0, 1], "element_count": 4096 * 4096, "threads_per_output": 1}]
+    assert (r1["bool_storage"], r1["cast_semantics"]) == ("one-byte-zero-or-one", "rne-saturating-fptosi-nan-zero-v1")
+    r2 = rt.lower_step(cfg2_source())["cuda_lowering"]
+    assert (r2["indexing"], r2["warp_reduction_groups"], r2["reduction_loop_count"], r2["strategy"]) == (
+        "cooperative_grid_stride", 1, 1, "warp_row")
+    assert r2["groups"] == [{"outputs": [0, 1, 2, 3], "element_count": 65536, "threads_per_output": 32}]
+    r5 = rt.lower_step(cfg5_sources()[0])["cuda_lowering"]
+    assert r5["strategy"] == "split" and r5["kernel_count"] == 2 and r5["scratch_bytes"] > 0
+    rs = rt.lower_step(cfg4_sources()[1])["cuda_lowering"]
+    assert rs["pre_copy"] == {"input": 0, "output": 0}
+    assert rs["groups"][0]["element_count"] == (1 << 23) * 256
+    # every recipe step of a lowered report carries its report
+    prog = rt.lower_report(softmax_report("f16", 64, 4096))
+    assert all(REPORT_FIELDS <= set(s["cuda_lowering"]) for s in prog["steps"])
