@@ -5,9 +5,10 @@
 // verifies every buffer when a plan is prepared, so a launch has no way to add
 // one), and embedded or real-time hosts with a fixed device-memory budget, for
 // which cudaMalloc may fail or stall the launching thread while the device
-// synchronises.  For the one kernel here that needs
-// scratch memory -- the split reduction, which keeps one partial record per CTA
-// between its two kernels -- this entry point supplies that scratch from a
+// synchronises.  For the reductions that need scratch memory -- the split
+// reduction, which keeps one partial record per CTA between its two kernels,
+// and the column reduction whose extent is split into chunks, which keeps one
+// record per chunk and column -- this entry point supplies that scratch from a
 // file-scope device array instead, so the caller passes only inputs and
 // outputs and nothing is allocated.
 //
@@ -15,11 +16,15 @@
 // and stays allocated until the process exits.  Its address is looked up once
 // per device with cudaGetSymbolAddress the first time the entry point runs on
 // that device; that first call should therefore happen before any stream
-// capture.  Every call shares the array and it keeps the previous call's
-// contents: the split reduction writes every partial record it later reads, so
-// nothing needs clearing, but calls that overlap on the GPU (different streams,
-// or the same plan launched concurrently) race on the array and must be
-// serialised by the caller.
+// capture.  The address is kept by device ordinal for the life of the process,
+// which assumes one context per device (the runtime API's primary context):
+// after a switch to another driver-API context, or a primary context rebuilt by
+// cudaDeviceReset, the kept address would belong to the old context.
+// Every call shares the array and it keeps the previous call's contents: both
+// reductions write every record they later read, so nothing needs clearing,
+// but calls that overlap on the GPU (different streams, or the same plan
+// launched concurrently) race on the array and must be serialised by the
+// caller.
 #include <cuda_runtime.h>
 
 #include <mutex>

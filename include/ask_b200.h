@@ -111,14 +111,19 @@ ASK_B200_API int ask_b200_plan_launch(const ask_b200_plan *plan, const uint64_t 
  * wholly planned ahead by a pool (nothing may be added at launch time), and
  * hosts with a fixed device-memory budget, where cudaMalloc may fail or stall
  * the launching thread while the device synchronises.  A split
- * reduction's scratch (one partial record per CTA) then comes from a
+ * reduction's scratch (one partial record per CTA), or the chunk records of a
+ * column reduction whose extent is split into chunks, then comes from a
  * file-scope device array of ASK_B200_NOALLOC_SCRATCH_BYTES (1 MiB) that every
  * GPU loading this library holds until the process exits; plans needing more
- * scratch (ask_b200_plan_scratch_bytes beyond the partial records of
- * outer * grid * reductions * 16 bytes) are rejected with ASK_B200_E_INVALID.
+ * scratch than that (ask_b200_plan_scratch_bytes) are rejected with
+ * ASK_B200_E_INVALID.
  * Only reduce plans are accepted (others: ASK_B200_E_UNSUPPORTED).  The first
- * call on a device looks up the array's address (cudaGetSymbolAddress); make
- * that first call before any stream capture.  All calls share the array, which
+ * call on a device looks up the array's address (cudaGetSymbolAddress) and
+ * keeps it for the life of the process, keyed by device ordinal: the entry
+ * point assumes one context per device (the runtime API's primary context) for
+ * the whole process, so a caller that switches to another driver-API context,
+ * or rebuilds the primary context after cudaDeviceReset, must not use it
+ * afterwards.  Make that first call before any stream capture.  All calls share the array, which
  * keeps the last call's contents (the kernels overwrite every record they
  * read), so calls that overlap on the GPU race and must be serialised by the
  * caller.  Ports and stream are as for ask_b200_plan_launch.

@@ -3,8 +3,9 @@
 Callers that cannot allocate device memory when they launch -- a runtime whose
 device memory is entirely planned ahead by a pool, or a host with a fixed
 device-memory budget -- launch reduce plans through this entry point, which
-takes the split reduction's scratch from a 1 MiB array built into the library
-instead of a buffer the caller allocates.  Its results must equal those of the
+takes the scratch of a split reduction, or of a column reduction whose extent
+is split into chunks, from a 1 MiB array built into the library instead of a
+buffer the caller allocates.  Its results must equal those of the
 ordinary entry point (ask_b200_plan_launch with caller-provided scratch); the
 split reduction is deterministic, so the comparison is bit-exact, which is
 within every tolerance the other reduction tests use.  Two calls in a row check
@@ -81,6 +82,31 @@ def test_noalloc_matches_ordinary_launch_twice(recipe_fn, n):
             assert _same_bits(g, r)
 
 
+def test_noalloc_column_chunks_match_ordinary_launch_twice():
+    """A column reduction with few columns over a long extent splits the
+    extent into chunks whose partial records live in scratch: through the
+    fixed array they must combine to the same bits as with caller scratch."""
+    torch.cuda.set_device(0)
+    outer, extent, inner = 1, 32768, 8
+    p = R.Program()
+    v = p.input("f32")
+    plan = ask_b200.Plan(R.reduce(p, v, ["sum", "max", "min", "argmax", "argmin"], outer, extent, inner), 0)
+    d = plan.describe()
+    assert d["kernel"] == "reduce_column_chunks_generic" and d["launch"]["grid"][1] > 1
+    assert 0 < plan.scratch_bytes <= ask_b200_noalloc_limit()
+    x = torch.from_numpy(np.random.default_rng(5).standard_normal(outer * extent * inner).astype(np.float32)).cuda()
+    x.view(extent, inner)[20000, 1] = float("nan")
+    x.view(extent, inner)[:, 2] = 3.0
+    ref = _outputs(plan)
+    _launch_ordinary(plan, [x], ref)
+    for _ in range(2):
+        got = _outputs(plan)
+        _launch_noalloc(plan, [x], got)
+        torch.cuda.synchronize()
+        for g, r in zip(got, ref):
+            assert _same_bits(g, r)
+
+
 def _prog_f32():
     p = R.Program()
     _prog_f32.value = p.input("f32")
@@ -95,8 +121,8 @@ def test_noalloc_rejects_plans_beyond_the_fixed_array():
     plan = ask_b200.Plan(rec, 0)
     needed = 64 * plan.describe()["launch"]["grid"][0] * 6 * 16
     assert needed > ask_b200_noalloc_limit()
-    x = torch.empty(16, dtype=torch.float32, device="cuda")  # never read: the check precedes any launch
-    outs = [torch.empty(64, dtype=torch.float32, device="cuda") for _ in range(6)]
+    x = torch.zeros(64 << 24, dtype=torch.float32, device="cuda")
+    outs = _outputs(plan)  # typed and sized as the port map says
     arr, n = _ports([x] + outs)
     status = ask_b200._lib.ask_b200_plan_launch_noalloc(plan._h, arr, n, None)
     assert status == ask_b200.E_INVALID
