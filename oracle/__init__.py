@@ -276,18 +276,20 @@ def reduce(recipe: dict, inputs: list, sum_mode: int = 0, threads: int = 1) -> l
     return outs
 
 
-def gather(table: np.ndarray, index: np.ndarray, outer: int, dim: int, inner: int, threads: int = 1):
+def gather(table: np.ndarray, index: np.ndarray, outer: int, dim: int, inner: int, threads: int = 1, out=None):
     n = index.size
-    out = np.empty(outer * n * inner, dtype=table.dtype)
+    if out is None:
+        out = np.empty(outer * n * inner, dtype=table.dtype)
     lib().orc_gather(_p(table), _p(index), 1 if index.dtype == np.int32 else 0, _p(out), outer, dim, inner, n,
                      table.dtype.itemsize, threads)
     return out
 
 
 def scatter_add(dtype: str, base: np.ndarray, index: np.ndarray, upd: np.ndarray, outer: int, dim: int,
-                inner: int):
+                inner: int, out=None):
     """Reference-order scatter_add in the element type (lib/Lowering/Host.cpp:677-772)."""
-    out = np.empty_like(base)
+    if out is None:
+        out = np.empty_like(base)
     lib().orc_scatter_add(dtype_code(dtype), _p(base), _p(index), 1 if index.dtype == np.int32 else 0, _p(upd),
                           _p(out), None, None, outer, dim, inner, index.size, 0)
     return out
@@ -302,14 +304,14 @@ def scatter_add_f64(base: np.ndarray, index: np.ndarray, upd: np.ndarray, outer:
     return out64, abs64
 
 
-def cfg1(a, b, c, threads: int = 1):
-    y0, y1 = np.empty_like(a), np.empty_like(a)
+def cfg1(a, b, c, threads: int = 1, out=None):
+    y0, y1 = out if out is not None else (np.empty_like(a), np.empty_like(a))
     lib().orc_cfg1(_p(a), _p(b), _p(c), _p(y0), _p(y1), a.size, threads)
     return y0, y1
 
 
-def cfg5b(x, y, threads: int = 1):
-    z = np.empty_like(x)
+def cfg5b(x, y, threads: int = 1, out=None):
+    z = np.empty_like(x) if out is None else out
     lib().orc_cfg5b(_p(x), _p(y), _p(z), x.size, threads)
     return z
 
@@ -321,10 +323,11 @@ def cfg5a(x, index_base: int = 0, threads: int = 1):
     return float(s64[0]), float(sref[0]), float(mn[0]), int(am[0])
 
 
-def softmax(dtype: str, x: np.ndarray, rows: int, cols: int, with_output: bool = True, threads: int = 1):
+def softmax(dtype: str, x: np.ndarray, rows: int, cols: int, with_output: bool = True, threads: int = 1,
+            out=None):
     m = np.empty(rows, np.float32)
     s = np.empty(rows, np.float32)
-    y = np.empty(rows * cols, np.uint16) if with_output else None
+    y = (np.empty(rows * cols, np.uint16) if out is None else out) if with_output else None
     lib().orc_softmax(dtype_code(dtype), _p(x), rows, cols, _p(m), _p(s), _p(y) if y is not None else None,
                       threads)
     return m, s, y
