@@ -181,7 +181,17 @@ std::string views_constant(const ViewSet& vs) {
     arr(v.extent);
     o << ", ";
     arr(v.stride);
-    o << ", " << i64(v.offset) << ", " << u64(v.pad) << "}";
+    o << ", " << i64(v.offset) << ", " << u64(v.pad) << ", " << i64(v.inner_rank) << ", ";
+    arr(v.inner_shape);
+    o << ", ";
+    arr(v.ilo);
+    o << ", ";
+    arr(v.istep);
+    o << ", ";
+    arr(v.iextent);
+    o << ", ";
+    arr(v.istride);
+    o << ", " << i64(v.ioffset) << ", " << u64(v.ipad) << "}";
   }
   o << "}};\n";
   return o.str();

@@ -72,6 +72,13 @@ enum IndexMap : uint8_t {
 // element is valid when every c_d - lo[d] >= 0 is a multiple of step[d] and
 // i_d < extent[d], and is then read at offset + sum(i_d * stride[d]);
 // otherwise the port yields `pad` (a value word of the port's type).
+//
+// A reshape that no strided window expresses (of a transposed, sliced or
+// padded value: the reference reads a reshape at the same row-major position,
+// ScalarEmitter.h:622) adds a second stage: when inner_rank > 0 the window
+// above yields a row-major position in a value of shape inner_shape (the
+// reshape's operand), which is split into coordinates there and read through
+// the inner window (ilo, istep, iextent, istride, ioffset; pad ipad).
 constexpr int kMaxRank = 6;
 struct PortView {
   int64_t lo[kMaxRank];
@@ -80,6 +87,14 @@ struct PortView {
   int64_t stride[kMaxRank];
   int64_t offset;
   uint64_t pad;
+  int64_t inner_rank;
+  int64_t inner_shape[kMaxRank];
+  int64_t ilo[kMaxRank];
+  int64_t istep[kMaxRank];
+  int64_t iextent[kMaxRank];
+  int64_t istride[kMaxRank];
+  int64_t ioffset;
+  uint64_t ipad;
 };
 
 constexpr int kMaxInsn = 48;

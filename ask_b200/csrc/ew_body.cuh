@@ -112,7 +112,24 @@ __device__ __forceinline__ uint64_t view_read(const PortView& v, int rank, const
     ok = ok && q0 >= 0 && (st == 1 || q * st == q0) && q < v.extent[d];
     off += q * v.stride[d];
   }
-  return ok ? word_from_storage(type, p, uint64_t(off)) : v.pad;
+  if (!ok) return v.pad;
+  if (v.inner_rank > 0) {
+    // off is a row-major position in the reshape's operand: its coordinates
+    // there (one division per axis) go through the inner window
+    int64_t pos = off;
+    off = v.ioffset;
+    for (int d = int(v.inner_rank) - 1; d >= 0; --d) {
+      const int64_t e = v.inner_shape[d];
+      const int64_t cd = pos % e;
+      pos /= e;
+      const int64_t q0 = cd - v.ilo[d], st = v.istep[d];
+      const int64_t q = st == 1 ? q0 : q0 / st;
+      ok = ok && q0 >= 0 && (st == 1 || q * st == q0) && q < v.iextent[d];
+      off += q * v.istride[d];
+    }
+    if (!ok) return v.ipad;
+  }
+  return word_from_storage(type, p, uint64_t(off));
 }
 
 // One element per thread iteration (grid-stride): the element's coordinates

@@ -485,6 +485,10 @@ struct ArgView {
   int64_t offset = 0;
   std::string pad = "0";  // JSON constant for elements outside the window
   std::vector<int64_t> shape;  // the viewed value's shape (its coordinate ranges)
+  // A reshape that no strided window expresses: the window above yields a
+  // row-major position in a value of shape inner->shape (the reshape's
+  // operand), whose coordinates are read through *inner.
+  std::shared_ptr<const ArgView> inner;
   // Whether axis d reads pad at some coordinate: an offset or strided window,
   // or one that ends before the axis does (a high pad).
   bool windowed(size_t d) const { return lo[d] != 0 || step[d] != 1 || extent[d] < shape[d]; }
@@ -933,6 +937,7 @@ class Lowering {
       out->extent = t.shape;
       out->stride = row_major(t.shape);
       out->offset = 0;
+      out->inner.reset();
       return true;
     }
     const Op* p = producer(v);
@@ -1027,15 +1032,25 @@ class Lowering {
     }
     if (n == "reshape") {
       if (!view_of(p->operands.at(0), &in)) return false;
-      for (size_t d = 0; d < in.lo.size(); ++d)
-        if (in.windowed(d)) return false;
+      bool plain = true;
+      for (size_t d = 0; d < in.lo.size(); ++d) plain = plain && !in.windowed(d);
       std::vector<int64_t> stride;
-      if (!reshape_strides(type_of(p->operands.at(0)).shape, in.stride, t.shape, &stride)) return false;
       *out = in;
       out->lo.assign(t.shape.size(), 0);
       out->step.assign(t.shape.size(), 1);
       out->extent = t.shape;
-      out->stride = stride;
+      if (plain && reshape_strides(type_of(p->operands.at(0)).shape, in.stride, t.shape, &stride)) {
+        out->stride = stride;  // the reshape is one more strided window
+        return true;
+      }
+      // Read at the same row-major position (ScalarEmitter.h:622): the window
+      // of the result yields that position in the operand, whose view becomes
+      // the inner stage.  One such stage per port.
+      if (in.inner) return false;
+      out->inner = std::make_shared<const ArgView>(in);
+      out->stride = row_major(t.shape);
+      out->offset = 0;
+      out->pad = "0";
       return true;
     }
     return false;
@@ -1081,7 +1096,7 @@ class Lowering {
     return oi == od.size() && ni == nd.size();
   }
   static bool is_identity(const ArgView& w, const Type& arg, const std::vector<int64_t>& shape) {
-    if (arg.numel() != product(shape, 0, shape.size()) || w.offset != 0) return false;
+    if (w.inner || arg.numel() != product(shape, 0, shape.size()) || w.offset != 0) return false;
     return w.stride == row_major(shape) && w.extent == shape &&
            std::all_of(w.lo.begin(), w.lo.end(), [](int64_t x) { return x == 0; }) &&
            std::all_of(w.step.begin(), w.step.end(), [](int64_t x) { return x == 1; });
@@ -1092,9 +1107,13 @@ class Lowering {
       for (size_t i = 0; i < v.size(); ++i) o += (i ? "," : "") + std::to_string(v[i]);
       return o + "]";
     };
-    return "{\"elements\":" + std::to_string(f_.arg_types[w.arg].numel()) + ",\"offset\":" + std::to_string(w.offset) +
-           ",\"lo\":" + list(w.lo) + ",\"step\":" + list(w.step) + ",\"extent\":" + list(w.extent) +
-           ",\"stride\":" + list(w.stride) + ",\"pad\":" + w.pad + "}";
+    auto window = [&](const ArgView& v) {
+      return "\"offset\":" + std::to_string(v.offset) + ",\"lo\":" + list(v.lo) + ",\"step\":" + list(v.step) +
+             ",\"extent\":" + list(v.extent) + ",\"stride\":" + list(v.stride) + ",\"pad\":" + v.pad;
+    };
+    std::string inner;
+    if (w.inner) inner = ",\"inner\":{\"shape\":" + list(w.inner->shape) + "," + window(*w.inner) + "}";
+    return "{\"elements\":" + std::to_string(f_.arg_types[w.arg].numel()) + "," + window(w) + inner + "}";
   }
   int use_view(const ArgView& w) { return use_port(w.arg, "view", view_json(w), &w); }
 
@@ -1126,7 +1145,7 @@ class Lowering {
   // Size-1 axes take no part.
   bool fast_map(const ArgView& w, std::string* map) {
     const size_t r = out_shape_.size();
-    if (is_reduce_ || w.offset != 0) return false;
+    if (is_reduce_ || w.offset != 0 || w.inner) return false;
     for (size_t d = 0; d < r; ++d)
       if (w.windowed(d)) return false;
     auto nested = [&](size_t a, size_t b) {  // row-major strides over axes [a, b)
@@ -1475,7 +1494,7 @@ class Lowering {
       if (pt.map != "view") return false;
       const ArgView& w = pt.w;
       const std::vector<int64_t>& as = f_.arg_types[pt.arg].shape;
-      if (w.offset != 0 || w.stride.size() != r) return false;
+      if (w.offset != 0 || w.stride.size() != r || w.inner) return false;
       for (size_t d = 0; d < r; ++d)
         if (w.windowed(d) || w.extent[d] != out_shape_[d]) return false;
       const std::vector<int64_t> rm = row_major(as);

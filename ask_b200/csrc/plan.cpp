@@ -467,31 +467,58 @@ void parse_ports(const json::Value& r, const char* key, bool with_map, std::vect
 // An IM_VIEW port's view (PortView) from {"elements", "offset", "lo", "step",
 // "extent", "stride", "pad"}; every element it can read must lie inside the
 // port's `elements`.
-PortView parse_view(const json::Value& v, int rank, int type, uint64_t* elements) {
-  PortView pv{};
-  *elements = checked_count(v.at("elements"), "view elements");
-  pv.offset = v.at("offset").as_int("view offset");
+// One window of a view: {"offset", "lo", "step", "extent", "stride", "pad"}
+// over `rank` axes, whose reads must lie in [0, elements).
+void parse_window(const json::Value& v, int rank, int type, uint64_t elements, int64_t* lo_, int64_t* step_,
+                  int64_t* extent_, int64_t* stride_, int64_t* offset_, uint64_t* pad_) {
+  *offset_ = v.at("offset").as_int("view offset");
   const char* keys[] = {"lo", "step", "extent", "stride"};
-  int64_t* dst[] = {pv.lo, pv.step, pv.extent, pv.stride};
+  int64_t* dst[] = {lo_, step_, extent_, stride_};
   for (int k = 0; k < 4; ++k) {
     const auto& a = v.at(keys[k]).as_array(keys[k]);
     if (int(a.size()) != rank) fail(ASK_B200_E_INVALID, std::string("view ") + keys[k] + " must have one entry per axis");
     for (int d = 0; d < rank; ++d) dst[k][d] = a[size_t(d)].as_int(keys[k]);
   }
   bool empty = false;
-  int64_t lo = pv.offset, hi = pv.offset;
+  int64_t lo = *offset_, hi = *offset_;
   for (int d = 0; d < rank; ++d) {
-    if (pv.step[d] < 1) fail(ASK_B200_E_INVALID, "view steps must be positive");
-    if (pv.extent[d] < 0) fail(ASK_B200_E_INVALID, "view extents must be non-negative");
-    if (pv.extent[d] == 0) empty = true;
-    const int64_t span = (pv.extent[d] ? pv.extent[d] - 1 : 0) * pv.stride[d];
+    if (step_[d] < 1) fail(ASK_B200_E_INVALID, "view steps must be positive");
+    if (extent_[d] < 0) fail(ASK_B200_E_INVALID, "view extents must be non-negative");
+    if (extent_[d] == 0) empty = true;
+    const int64_t span = (extent_[d] ? extent_[d] - 1 : 0) * stride_[d];
     lo += span < 0 ? span : 0;
     hi += span > 0 ? span : 0;
   }
-  if (!empty && (lo < 0 || uint64_t(hi) >= *elements))
+  if (!empty && (lo < 0 || uint64_t(hi) >= elements))
     fail(ASK_B200_E_INVALID, "a view reads outside its port's elements");
   const json::Value* pad = v.get("pad");
-  pv.pad = pad ? constant_word(*pad, type) : 0;
+  *pad_ = pad ? constant_word(*pad, type) : 0;
+}
+
+// An IM_VIEW port's view (PortView) from {"elements", "offset", "lo", "step",
+// "extent", "stride", "pad"[, "inner": {"shape", "offset", "lo", "step",
+// "extent", "stride", "pad"}]}; every element it can read must lie inside the
+// port's `elements` (with "inner", the outer window's positions inside the
+// inner shape, and the inner window's reads inside the port).
+PortView parse_view(const json::Value& v, int rank, int type, uint64_t* elements) {
+  PortView pv{};
+  *elements = checked_count(v.at("elements"), "view elements");
+  const json::Value* inner = v.get("inner");
+  uint64_t positions = *elements;
+  if (inner) {
+    const auto& sh = inner->at("shape").as_array("inner shape");
+    if (sh.empty() || sh.size() > size_t(kMaxRank)) fail(ASK_B200_E_INVALID, "inner view rank must be 1..6");
+    pv.inner_rank = int64_t(sh.size());
+    positions = 1;
+    for (size_t d = 0; d < sh.size(); ++d) {
+      pv.inner_shape[d] = sh[d].as_int("inner shape");
+      if (pv.inner_shape[d] < 1) fail(ASK_B200_E_INVALID, "inner view extents must be positive");
+      positions *= uint64_t(pv.inner_shape[d]);
+    }
+    parse_window(*inner, int(pv.inner_rank), type, *elements, pv.ilo, pv.istep, pv.iextent, pv.istride, &pv.ioffset,
+                 &pv.ipad);
+  }
+  parse_window(v, rank, type, positions, pv.lo, pv.step, pv.extent, pv.stride, &pv.offset, &pv.pad);
   return pv;
 }
 

@@ -9,15 +9,18 @@
  * execution plan that binds steps to buffers.  The supported subset is the hot
  * path: elementwise ops over the step's iteration shape, whose arguments may
  * be read through broadcast_in_dim, transpose, slice, pad, reshape and
- * concatenate (as strided, windowed views of the argument) and iota;
+ * concatenate (as strided, windowed views of the argument) and iota -- a
+ * reshape of a transposed, sliced or padded value, which no strided window
+ * expresses, is read at the same row-major position through a second,
+ * inner window (one such reshape per operand);
  * reductions (sum, prod, max, min, any, all, argmax, argmin) over any set
  * of axes (a scattered set is gathered last by a transpose), their operands
  * built the same way; gather and
  * scatter_add.  Steps outside it fail
- * with ASK_B200_E_UNSUPPORTED and a message naming the op (matmul and
- * external steps, a reshape that would need a copy, a reshape of a padded
- * value); index maps of computed elementwise values move onto their
- * operands, pads and concatenates of them become coordinate selects.
+ * with ASK_B200_E_UNSUPPORTED and a message naming the op (matmul steps, two
+ * such reshapes stacked on one operand); index maps of computed elementwise
+ * values move onto their operands, pads and concatenates of them become
+ * coordinate selects.
  */
 #ifndef ASK_B200_LOWER_H
 #define ASK_B200_LOWER_H

@@ -32,17 +32,29 @@ def _input(port, arr, shape, inner, reduce_dims=None):
     if m != "view":
         raise NotImplementedError(m)
     v = port["view"]
-    coords = np.indices(shape, dtype=np.int64)
-    ok = np.ones(shape, dtype=bool)
-    off = np.full(shape, v["offset"], dtype=np.int64)
-    for d in range(len(shape)):
+    ok, off = _window(v, np.indices(shape, dtype=np.int64))
+    out = np.full(shape, v["pad"], dtype=flat.dtype)
+    if "inner" in v:  # off is a row-major position in the inner shape, read through the inner window
+        w = v["inner"]
+        pos = np.where(ok, off, 0)
+        iok, ioff = _window(w, np.stack(np.unravel_index(pos, w["shape"])))
+        out[ok & ~iok] = w["pad"]
+        ok &= iok
+        off = ioff
+    out[ok] = flat[off[ok]]
+    return out
+
+
+def _window(v, coords):
+    """(valid, offset) of a view window at coordinates [rank, ...]."""
+    ok = np.ones(coords.shape[1:], dtype=bool)
+    off = np.full(coords.shape[1:], v["offset"], dtype=np.int64)
+    for d in range(coords.shape[0]):
         s = coords[d] - v["lo"][d]
         q = np.floor_divide(s, v["step"][d])
         ok &= (s >= 0) & (q * v["step"][d] == s) & (q < v["extent"][d])
         off += q * v["stride"][d]
-    out = np.full(shape, v["pad"], dtype=flat.dtype)
-    out[ok] = flat[off[ok]]
-    return out
+    return ok, off
 
 
 def _reduce(recipe, values):
