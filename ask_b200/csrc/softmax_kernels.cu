@@ -14,13 +14,24 @@
 //
 // Semantics per element are those of the three steps: max folds with
 // max.NaN.f32 (llvm.maximum: the canonical NaN when the row holds a NaN,
-// -0 < +0); exp(x + m*(-1)) with CUDA's expf; the division is the
-// correctly rounded f32 quotient (one reciprocal per row and Markstein's
-// correction, with the IEEE division for any unit outside its conditions, as
-// in the softmax normalise kernel); f16/bf16 rounding to nearest even.  The sum
-// is accumulated per thread in f32 and across the CTA in f64 in a fixed order,
-// so s is deterministic; its rounding may differ from the three-kernel plan's
-// in the last place.
+// -0 < +0); t = x + m*(-1) rounded to f32; exp(t); e / s; f16/bf16 rounding to
+// nearest even.  The sum is accumulated per thread in f32 and across the CTA
+// in f64 in a fixed order, so s is deterministic.
+//
+// The arithmetic runs on pairs of f32 values (add/mul/fma.rn.f32x2, two
+// elements an instruction on sm_100) wherever a thread's elements all have
+// -69 <= t <= 0 (a finite row: every e is then a normal f32):
+//   exp(t) = 2^hi * 2^lo, hi = RN(t * L) with L = RN(log2 e); the residual
+//   t*L - hi is exact by one fused multiply-add (the FMA two-product of
+//   Ogita, Rump and Oishi, 2005), to which t * (log2 e - L) is added, so
+//   |lo| <= 2^-17 and 2^lo = 1 + lo*ln2 within 2^-35; 2^hi is ex2.approx.f32
+//   (relative error about 2^-22): e is within about 3 f32 ulps of exp(t);
+//   y = RN16(e * RN(1/s)), within 2 f32 ulps of e / s before the 16-bit
+//   rounding, so within one 16-bit ulp of the three-step plan's RN16(e / s).
+// Any other thread (a non-finite row, or t below -69) computes each element
+// with CUDA's expf and the IEEE division, as the three steps do.  m is
+// bit-identical to the three-step plan's; s may differ in its last places and
+// y by at most one unit in the last place.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -89,20 +100,67 @@ __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
   return r;
 }
 
+// Pairs of f32 values in one 64-bit register (element 0 in the low half).
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float a) {
+  float r;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
+// exp(t) of a pair with -69 <= t <= 0 (see the file comment).
+constexpr float kLog2e = 0x1.715476p+0f;      // RN(log2 e)
+constexpr float kLog2eTail = 0x1.4ae0cp-26f;  // RN(log2 e - kLog2e)
+constexpr float kLn2 = 0x1.62e43p-1f;         // RN(ln 2)
+__device__ __forceinline__ uint64_t exp_pair(uint64_t t) {
+  const uint64_t L = pack2(kLog2e, kLog2e), nL = pack2(-kLog2e, -kLog2e);
+  const uint64_t tail = pack2(kLog2eTail, kLog2eTail), ln2 = pack2(kLn2, kLn2);
+  const uint64_t hi = mul2(t, L);
+  uint64_t lo = fma2(t, L, mul2(t, nL));  // t*L - hi, exact
+  lo = mul2(fma2(t, tail, lo), ln2);
+  float h0, h1;
+  unpack2(hi, h0, h1);
+  const uint64_t p = pack2(ex2_approx(h0), ex2_approx(h1));
+  return fma2(p, lo, p);
+}
+
 constexpr int kMaxWarps = 16;
 #ifndef ASKB_SOFTMAX_THREADS
 #define ASKB_SOFTMAX_THREADS 128
 #endif
 constexpr int kPreferThreads = ASKB_SOFTMAX_THREADS;  // CTA size the row split aims for
 
-// VPT == 4 (4096-element rows, 128-thread CTAs) is compiled for two 512-thread
-// CTAs' worth of registers per SM, 64 a thread: the f16 variant then fits 8
-// CTAs per SM instead of 4 without spilling (same-box A/B on cfg3: 0.111 ms
-// against 0.123 ms); wider rows keep the full budget (VPT == 8 would spill).
-template <int T, int VPT>
-__global__ void __launch_bounds__(kMaxWarps * 32, VPT == 4 ? 2 : 1) softmax_rows_kernel(const uint4* __restrict__ x, float* __restrict__ m_out,
-                                                                      float* __restrict__ s_out, uint4* __restrict__ y,
-                                                                      uint64_t rows, uint32_t vecs) {
+// Rows split into 128-thread CTAs with up to 4 vectors a thread (4096-element
+// rows) are compiled for 8 CTAs per SM, 64 registers a thread, without
+// spilling (same-box A/B on cfg3 with the scalar arithmetic: 0.111 ms against
+// 0.123 ms at 4 CTAs per SM); other splits keep the full register budget
+// (VPT == 8 would spill at 64).
+template <int T, int VPT, bool kNarrow>
+__global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 1)
+    softmax_rows_kernel(const uint4* __restrict__ x, float* __restrict__ m_out, float* __restrict__ s_out,
+                        uint4* __restrict__ y, uint64_t rows, uint32_t vecs) {
   __shared__ float red_max[2][kMaxWarps];
   __shared__ double red_sum[2][kMaxWarps];
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -113,18 +171,17 @@ __global__ void __launch_bounds__(kMaxWarps * 32, VPT == 4 ? 2 : 1) softmax_rows
     for (int q = 0; q < VPT; ++q) v[q] = ld_stream_v4(x + row * vecs + q * blockDim.x + threadIdx.x);
   }
   for (int parity = 0; row < rows; row += gridDim.x, parity ^= 1) {
-    float e[VPT * 8];
+    uint64_t e[VPT * 4];  // the thread's elements as f32 pairs: x, then t, then exp(t)
     // m = max over the row (NaN-propagating); the thread's smallest value
-    // bounds its exp results from below for the division's check.  Both fold
-    // on the packed 16-bit values, two elements an instruction.
+    // decides whether all its elements take the pair path.  Both fold on the
+    // packed 16-bit values, two elements an instruction.
     uint32_t pmax = v[0].x, pmin = v[0].x;
 #pragma unroll
     for (int q = 0; q < VPT; ++q) {
       const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        e[q * 8 + 2 * j] = widen_lo<T>(w[j]);
-        e[q * 8 + 2 * j + 1] = widen_hi<T>(w[j]);
+        e[q * 4 + j] = pack2(widen_lo<T>(w[j]), widen_hi<T>(w[j]));
         pmax = max2_nan<T>(pmax, w[j]);
         pmin = min2<T>(pmin, w[j]);
       }
@@ -144,12 +201,33 @@ __global__ void __launch_bounds__(kMaxWarps * 32, VPT == 4 ? 2 : 1) softmax_rows
     float m = red_max[parity][0];
     for (uint32_t k = 1; k < nwarps; ++k) m = max_nan(m, red_max[parity][k]);
     const float nm = __fmul_rn(m, -1.0f);
-    // e = exp(x + m*(-1)), s = sum of e
-    float part = 0.0f;
+    // e = exp(x + m*(-1)), s = sum of e.  t >= -69 for the smallest element
+    // (and so for all, t <= 0 for all) holds only when m and the thread's
+    // values are finite: NaN and infinities take the scalar path.
+    const bool pairs = __fadd_rn(mn, nm) >= -69.0f;
+    float part;
+    if (pairs) {
+      const uint64_t nm2 = pack2(nm, nm);
+      uint64_t acc = pack2(0.0f, 0.0f);
 #pragma unroll
-    for (int k = 0; k < VPT * 8; ++k) {
-      e[k] = expf(__fadd_rn(e[k], nm));
-      part = __fadd_rn(part, e[k]);
+      for (int k = 0; k < VPT * 4; ++k) {
+        e[k] = exp_pair(add2(e[k], nm2));
+        acc = add2(acc, e[k]);
+      }
+      float a0, a1;
+      unpack2(acc, a0, a1);
+      part = __fadd_rn(a0, a1);
+    } else {
+      part = 0.0f;
+#pragma unroll
+      for (int k = 0; k < VPT * 4; ++k) {
+        float lo, hi;
+        unpack2(e[k], lo, hi);
+        lo = expf(__fadd_rn(lo, nm));
+        hi = expf(__fadd_rn(hi, nm));
+        part = __fadd_rn(__fadd_rn(part, lo), hi);
+        e[k] = pack2(lo, hi);
+      }
     }
     double ps = double(part);
 #pragma unroll
@@ -163,33 +241,28 @@ __global__ void __launch_bounds__(kMaxWarps * 32, VPT == 4 ? 2 : 1) softmax_rows
       m_out[row] = m;
       s_out[row] = s;
     }
-    // y = cast(e / s): the correctly rounded quotient from one reciprocal
-    // (Markstein's two corrections).  Its conditions hold for the whole thread
-    // when s and 1/s are normal and every e >= exp(-69) > 2^-100: then
-    // 2^-100 / s <= e / s <= 1 (e <= 1 because m is the row's maximum and
-    // s >= 1), so every quotient is normal.  Otherwise the IEEE division runs.
+    // y = cast(e / s).  On the pair path y = RN16(e * RN(1/s)): with
+    // 1 <= s <= 2^100 and e >= 2^-100 (normal), every product is a normal f32
+    // within 2 ulps of e / s.  Otherwise the IEEE division.
     const float r = __frcp_rn(s);
-    const bool ok = s >= 1.0f && s <= 0x1p100f && __fadd_rn(mn, nm) >= -69.0f;
+    const bool by_reciprocal = pairs && s >= 1.0f && s <= 0x1p100f;
+    const uint64_t r2 = pack2(r, r);
 #pragma unroll
     for (int qv = 0; qv < VPT; ++qv) {
-      float q[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float ek = e[qv * 8 + k];
-        float t = __fmul_rn(ek, r);
-        t = __fmaf_rn(__fmaf_rn(-t, s, ek), r, t);
-        t = __fmaf_rn(__fmaf_rn(-t, s, ek), r, t);
-        q[k] = t;
-      }
       uint32_t o[4];
-      if (ok) {
+      if (by_reciprocal) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = narrow_two<T>(q[2 * j], q[2 * j + 1]);
+        for (int j = 0; j < 4; ++j) {
+          float lo, hi;
+          unpack2(mul2(e[qv * 4 + j], r2), lo, hi);
+          o[j] = narrow_two<T>(lo, hi);
+        }
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float lo = __fdiv_rn(e[qv * 8 + 2 * j], s), hi = __fdiv_rn(e[qv * 8 + 2 * j + 1], s);
-          o[j] = narrow_one<T>(lo) | (narrow_one<T>(hi) << 16);
+          float lo, hi;
+          unpack2(e[qv * 4 + j], lo, hi);
+          o[j] = narrow_one<T>(__fdiv_rn(lo, s)) | (narrow_one<T>(__fdiv_rn(hi, s)) << 16);
         }
       }
       st_stream_v4(y + row * vecs + qv * blockDim.x + threadIdx.x, make_uint4(o[0], o[1], o[2], o[3]));
@@ -197,17 +270,26 @@ __global__ void __launch_bounds__(kMaxWarps * 32, VPT == 4 ? 2 : 1) softmax_rows
   }
 }
 
-template <int T, int VPT>
-cudaError_t launch_rows(const SoftmaxArgs& a, int sms, cudaStream_t st) {
+template <int T, int VPT, bool kNarrow>
+cudaError_t launch_split(const SoftmaxArgs& a, unsigned threads, int sms, cudaStream_t st) {
   const uint32_t vecs = uint32_t(a.cols / 8);
-  const unsigned threads = vecs / VPT;
   int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, softmax_rows_kernel<T, VPT>, int(threads), 0);
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, softmax_rows_kernel<T, VPT, kNarrow>,
+                                                                int(threads), 0);
   if (e != cudaSuccess) return e;
   const uint64_t grid = std::min<uint64_t>(a.rows, uint64_t(sms) * uint64_t(per_sm > 0 ? per_sm : 1));
-  softmax_rows_kernel<T, VPT><<<unsigned(grid), threads, 0, st>>>(static_cast<const uint4*>(a.x), a.m, a.s,
-                                                                  static_cast<uint4*>(a.y), a.rows, vecs);
+  softmax_rows_kernel<T, VPT, kNarrow><<<unsigned(grid), threads, 0, st>>>(
+      static_cast<const uint4*>(a.x), a.m, a.s, static_cast<uint4*>(a.y), a.rows, vecs);
   return cudaGetLastError();
+}
+
+template <int T, int VPT>
+cudaError_t launch_rows(const SoftmaxArgs& a, int sms, cudaStream_t st) {
+  const unsigned threads = unsigned(a.cols / 8) / VPT;
+  if constexpr (VPT <= 4) {
+    if (threads == 128) return launch_split<T, VPT, true>(a, threads, sms, st);
+  }
+  return launch_split<T, VPT, false>(a, threads, sms, st);
 }
 
 template <int T>
