@@ -585,14 +585,16 @@ def pcie_bandwidth(torch, barrier, dist, nbytes=1 << 30):
 def bind_numa_local(torch, local):
     """Run this rank on the CPUs of its GPU's NUMA node, so that the pinned
     host buffers of the end-to-end run are allocated in that node's memory.
-    Returns the node, or None where the topology is not visible."""
+    Returns {"node": n, "cpus": k} or {"node": None, "why": reason}."""
     try:
         p = torch.cuda.get_device_properties(local)
         dev = f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        if not os.path.exists(dev):
+            return {"node": None, "why": f"{dev} not visible"}
         with open(os.path.join(dev, "numa_node")) as f:
             node = int(f.read().strip())
         if node < 0:
-            return None
+            return {"node": None, "why": "the GPU reports no NUMA node"}
         with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
             cpus = set()
             for part in f.read().strip().split(","):
@@ -600,11 +602,11 @@ def bind_numa_local(torch, local):
                 cpus.update(range(int(lo), int(hi or lo) + 1))
         cpus &= os.sched_getaffinity(0)
         if not cpus:
-            return None
+            return {"node": node, "why": "none of the node's CPUs is available to this process"}
         os.sched_setaffinity(0, cpus)
-        return node
-    except Exception:
-        return None
+        return {"node": node, "cpus": len(cpus)}
+    except Exception as e:  # the topology is informational: never fail the bench on it
+        return {"node": None, "why": f"{type(e).__name__}: {e}"}
 
 
 def run_e2e(w, args, torch, barrier, dist):
@@ -677,18 +679,31 @@ def run_e2e(w, args, torch, barrier, dist):
         v = torch.tensor([bw["h2d_gbs"], bw["d2h_gbs"]], dtype=torch.float64, device="cuda")
         dist.all_reduce(v, op=dist.ReduceOp.MIN)
         bw = {"h2d_gbs": round(float(v[0].item()), 2), "d2h_gbs": round(float(v[1].item()), 2)}
-    h2d_rate = h2d_rank / (ms * 1e-3) / 1e9
-    frac = h2d_rate / bw["h2d_gbs"] if bw["h2d_gbs"] else None
+    # the time each direction needs at the measured copy rate, against the step
+    t_h2d = h2d_rank / (bw["h2d_gbs"] * 1e9) if bw["h2d_gbs"] else 0.0
+    t_d2h = d2h_rank / (bw["d2h_gbs"] * 1e9) if bw["d2h_gbs"] else 0.0
+    step_s = ms * 1e-3
+    frac = max(t_h2d, t_d2h) / step_s
+    serial = (t_h2d + t_d2h) / step_s
+    kernels = 100.0 * w.device_ms / ms if getattr(w, "device_ms", None) else None
+    if frac > 0.85:
+        limiter = f"the host<->device link: the busier direction ({'H2D' if t_h2d >= t_d2h else 'D2H'}) alone needs " \
+                  f"{100 * frac:.0f}% of the step at the measured copy rate"
+    elif serial > 0.85:
+        limiter = f"copies in the two directions one after the other (one stream): together {100 * serial:.0f}% " \
+                  "of the step at the measured copy rates"
+    else:
+        limiter = f"neither link direction (busier {100 * frac:.0f}%, both {100 * serial:.0f}% of the step)"
+    if kernels is not None:
+        limiter += f"; the kernels take {kernels:.1f}% of the step"
     return {"value": round(w.global_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
             "path": "pinned host -> device copies, Plan.launch, device -> pinned host" +
                     (f", {len(groups)} independent plans on their own streams" if groups else ", one stream"),
-            "pcie": dict(bw, e2e_h2d_gbs_per_gpu=round(h2d_rate, 2), numa_node=getattr(w, "numa_node", None),
+            "pcie": dict(bw, e2e_h2d_gbs_per_gpu=round(h2d_rank / step_s / 1e9, 2),
+                         e2e_d2h_gbs_per_gpu=round(d2h_rank / step_s / 1e9, 2), numa=getattr(w, "numa_node", None),
                          copy_probe="1 GiB pinned copies, all ranks at once, min over ranks"),
-            "pcie_frac": round(frac, 4) if frac else None,
-            "limiter": "host->device copy bandwidth (pcie_frac = the step's H2D rate per GPU / a plain pinned "
-                       "H2D copy's); the kernels take " +
-                       f"{100.0 * w.device_ms / ms:.1f}% of the step" if getattr(w, "device_ms", None) else None}
+            "pcie_frac": round(frac, 4), "serial_copy_frac": round(serial, 4), "limiter": limiter}
 
 
 def host_memory_available() -> int:
