@@ -26,6 +26,7 @@ E_UNSUPPORTED = -2
 E_CUDA = -3
 E_NCCL = -4
 E_DEVICE = -5
+E_TIMEOUT = -6
 
 # Generator kinds of ask_b200_generate.
 GEN_UNIFORM_F32, GEN_NORMAL_F32, GEN_NORMAL_F16, GEN_NORMAL_BF16, GEN_I32, GEN_ZIPF_I64, GEN_ZIPF_I32 = range(7)
@@ -44,6 +45,7 @@ _SIGNATURES = {
     "ask_b200_plan_kernel_launches": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_int)]),
     "ask_b200_plan_launch": (ctypes.c_int, [_p, ctypes.POINTER(_u64), ctypes.c_size_t, _u64, _p]),
     "ask_b200_plan_launch_noalloc": (ctypes.c_int, [_p, ctypes.POINTER(_u64), ctypes.c_size_t, _p]),
+    "ask_b200_comm_status": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "ask_b200_comm_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
     "ask_b200_comm_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             ctypes.POINTER(_p)]),
@@ -195,6 +197,15 @@ class Comm:
         _check(_lib.ask_b200_comm_create(unique_id, nranks, rank, device, ctypes.byref(handle)))
         self._h = handle
         self.nranks, self.rank, self.device = nranks, rank, device
+
+    def status(self) -> tuple:
+        """(status, peer_exchange): status is OK or E_TIMEOUT (a bounded wait for
+        the other ranks ran out; the communicator must then be closed);
+        peer_exchange tells whether records cross GPUs by peer memory (else
+        by the NCCL all-gather).  Synchronous."""
+        st, pe = ctypes.c_int(), ctypes.c_int()
+        _check(_lib.ask_b200_comm_status(self._h, ctypes.byref(st), ctypes.byref(pe)))
+        return st.value, bool(pe.value)
 
     def close(self) -> None:
         if getattr(self, "_h", None):

@@ -105,6 +105,21 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
                        void* scratch, RedPartial* partials_out, cudaStream_t stream);
 // Combine `n` records per reduction laid out [n][n_red] into the outputs.
 cudaError_t red_combine_records(const RedArgs& args, const RedPartial* records, int n, cudaStream_t stream);
+// Cross-GPU exchange of a sharded 0-D reduction's records over peer memory
+// (one CTA): this rank's record `mine` (n_red records) is stored into slot
+// `rank` of every rank's inbox (inboxes[r], device pointers valid on this
+// device: the peers' inboxes are IPC mappings), each flag is raised with a
+// release store, the rank waits (bounded by timeout_ns) for every rank's flag,
+// and the records are folded in rank order into the outputs.  On a timeout the
+// outputs are left as they were and the inbox's status word is set to 1.
+constexpr int kExchangeMaxRanks = 64;
+constexpr size_t kInboxRecordsBytes = size_t(2) * kExchangeMaxRanks * kMaxReductions * sizeof(RedPartial);
+constexpr size_t kInboxFlagsOffset = kInboxRecordsBytes;                       // uint64 per rank
+constexpr size_t kInboxSeqOffset = kInboxFlagsOffset + kExchangeMaxRanks * 8;  // uint64 epoch
+constexpr size_t kInboxStatusOffset = kInboxSeqOffset + 8;                     // uint32, 0 = ok
+constexpr size_t kInboxBytes = kInboxStatusOffset + 8;
+cudaError_t red_exchange_combine(const RedArgs& args, const RedPartial* mine, void* const* inboxes, int nranks,
+                                 int rank, uint64_t timeout_ns, cudaStream_t stream);
 size_t red_split_scratch_bytes(int grid, int n_red);
 // RS_COLUMN with few outputs: grid.y = chunks of the extent, one partial
 // record per (output, chunk) in scratch, then a combine in chunk order.

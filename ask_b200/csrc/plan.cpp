@@ -418,6 +418,15 @@ uint64_t mul_checked(uint64_t a, uint64_t b) {
 struct ask_b200_comm {
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0, device = 0;
+  // Peer-memory exchange (when every rank's inbox could be mapped): this
+  // rank's inbox, the peers' IPC mappings, and a device array of all inbox
+  // addresses in rank order as this device sees them.
+  bool p2p = false;
+  std::string p2p_note;  // why the exchange falls back to the NCCL all-gather
+  void* inbox = nullptr;
+  std::vector<void*> opened;
+  void** inboxes_dev = nullptr;
+  uint64_t timeout_ns = 1000000000ull;
 };
 
 namespace {
@@ -1071,6 +1080,120 @@ const double* zipf_table(int device, double s, uint64_t n) {
 
 }  // namespace
 
+// Peer-memory exchange for sharded reductions.  Every rank allocates a small
+// inbox, the ranks trade its IPC handle with one NCCL all-gather, and each maps
+// the others'.  Any failure (no peer access, IPC refused, the variable
+// ASK_B200_NO_PEER_EXCHANGE set) leaves the NCCL all-gather path in place; all
+// ranks take the same decision because the outcome is all-gathered too.
+// ASK_B200_EXCHANGE_TIMEOUT_MS bounds each wait for the peers' flags (default
+// 1000).
+void release_peer_exchange(ask_b200_comm& c) {
+  if (c.p2p) {
+    // This rank's exchange kernels must be done before its buffers go.  After
+    // a completed exchange every peer has already stored into this inbox
+    // (this rank saw their flags), so nothing stores into it later; after a
+    // timed-out one a late peer still may, so the buffers stay allocated and
+    // mapped until the process exits.
+    (void)cudaDeviceSynchronize();
+    uint32_t word = 1;
+    if (cudaMemcpy(&word, static_cast<char*>(c.inbox) + kInboxStatusOffset, sizeof(word), cudaMemcpyDeviceToHost) !=
+            cudaSuccess ||
+        word != 0) {
+      (void)cudaGetLastError();
+      c.opened.clear();
+      c.inboxes_dev = nullptr;
+      c.inbox = nullptr;
+      c.p2p = false;
+      return;
+    }
+  }
+  for (void* p : c.opened)
+    if (p) (void)cudaIpcCloseMemHandle(p);
+  c.opened.clear();
+  if (c.inboxes_dev) (void)cudaFree(c.inboxes_dev);
+  if (c.inbox) (void)cudaFree(c.inbox);
+  c.inboxes_dev = nullptr;
+  c.inbox = nullptr;
+  c.p2p = false;
+}
+
+void setup_peer_exchange(ask_b200_comm& c) {
+  if (const char* t = std::getenv("ASK_B200_EXCHANGE_TIMEOUT_MS")) {
+    const long ms = std::strtol(t, nullptr, 10);
+    if (ms > 0 && ms <= 60000) c.timeout_ns = uint64_t(ms) * 1000000ull;
+  }
+  // each rank's IPC handle and whether it can take part
+  struct Card {
+    cudaIpcMemHandle_t handle;
+    int ok;
+    int pad[15];
+  };
+  static_assert(sizeof(Card) == 128, "card layout");
+  Card mine{};
+  mine.ok = std::getenv("ASK_B200_NO_PEER_EXCHANGE") ? 0 : 1;
+  if (c.nranks > kExchangeMaxRanks) mine.ok = 0;
+  if (mine.ok) {
+    if (cudaMalloc(&c.inbox, kInboxBytes) != cudaSuccess || cudaMemset(c.inbox, 0, kInboxBytes) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine.handle, c.inbox) != cudaSuccess) {
+      (void)cudaGetLastError();
+      mine.ok = 0;
+      c.p2p_note = "inbox allocation or IPC handle failed";
+    }
+  }
+  Card* cards = nullptr;
+  check_cuda(cudaMalloc(&cards, sizeof(Card) * size_t(c.nranks)), "exchange card buffer");
+  check_cuda(cudaMemcpy(cards + c.rank, &mine, sizeof(Card), cudaMemcpyHostToDevice), "exchange card");
+  std::vector<Card> all(size_t(c.nranks));
+  const ncclResult_t nr = nccl().allGather(cards + c.rank, cards, sizeof(Card), ncclUint8, c.comm, nullptr);
+  cudaError_t ce = nr == ncclSuccess ? cudaStreamSynchronize(nullptr) : cudaErrorUnknown;
+  if (ce == cudaSuccess) ce = cudaMemcpy(all.data(), cards, sizeof(Card) * all.size(), cudaMemcpyDeviceToHost);
+  (void)cudaFree(cards);
+  if (nr != ncclSuccess) fail(ASK_B200_E_NCCL, "exchange card all-gather failed");
+  check_cuda(ce, "exchange card all-gather");
+  bool ok = true;
+  for (const Card& k : all) ok = ok && k.ok;
+  std::vector<void*> addr(size_t(c.nranks), nullptr);
+  if (ok) {
+    addr[size_t(c.rank)] = c.inbox;
+    for (int r = 0; r < c.nranks && ok; ++r) {
+      if (r == c.rank) continue;
+      void* p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, all[size_t(r)].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess || !p) {
+        (void)cudaGetLastError();
+        ok = false;
+        c.p2p_note = "cudaIpcOpenMemHandle of rank " + std::to_string(r) + "'s inbox failed";
+        break;
+      }
+      c.opened.push_back(p);
+      addr[size_t(r)] = p;
+    }
+  } else if (c.p2p_note.empty()) {
+    c.p2p_note = mine.ok ? "another rank cannot take part" : "disabled on this rank";
+  }
+  // every rank must agree: all-gather the mapping outcome as well
+  int* flags = nullptr;
+  check_cuda(cudaMalloc(&flags, sizeof(int) * size_t(c.nranks)), "exchange flag buffer");
+  const int mine_ok = ok ? 1 : 0;
+  check_cuda(cudaMemcpy(flags + c.rank, &mine_ok, sizeof(int), cudaMemcpyHostToDevice), "exchange flag");
+  const ncclResult_t nr2 = nccl().allGather(flags + c.rank, flags, sizeof(int), ncclUint8, c.comm, nullptr);
+  std::vector<int> oks(size_t(c.nranks), 0);
+  cudaError_t ce2 = nr2 == ncclSuccess ? cudaStreamSynchronize(nullptr) : cudaErrorUnknown;
+  if (ce2 == cudaSuccess) ce2 = cudaMemcpy(oks.data(), flags, sizeof(int) * oks.size(), cudaMemcpyDeviceToHost);
+  (void)cudaFree(flags);
+  if (nr2 != ncclSuccess) fail(ASK_B200_E_NCCL, "exchange outcome all-gather failed");
+  check_cuda(ce2, "exchange outcome all-gather");
+  for (int v : oks) ok = ok && v;
+  if (ok) {
+    check_cuda(cudaMalloc(reinterpret_cast<void**>(&c.inboxes_dev), sizeof(void*) * size_t(c.nranks)), "inbox table");
+    check_cuda(cudaMemcpy(c.inboxes_dev, addr.data(), sizeof(void*) * addr.size(), cudaMemcpyHostToDevice),
+               "inbox table");
+    c.p2p = true;
+  } else {
+    if (c.p2p_note.empty()) c.p2p_note = "another rank could not map an inbox";
+    release_peer_exchange(c);
+  }
+}
+
 // The lowering adapter's cuda_lowering report (lower.cpp): that of the
 // recipe's host-only plan, with the scatter base named by the step's argument.
 std::string askb_recipe_lowering_report(const std::string& recipe_json, long pre_copy_input) {
@@ -1200,6 +1323,7 @@ int ask_b200_comm_create(const unsigned char id[128], int nranks, int rank, int 
     std::unique_ptr<ask_b200_comm> c(new ask_b200_comm());
     c->nranks = nranks; c->rank = rank; c->device = device;
     check_nccl(nccl().commInitRank(&c->comm, nranks, uid, rank), "ncclCommInitRank");
+    setup_peer_exchange(*c);
     *out = c.release();
   });
 }
@@ -1207,8 +1331,22 @@ int ask_b200_comm_create(const unsigned char id[128], int nranks, int rank, int 
 int ask_b200_comm_destroy(ask_b200_comm* comm) {
   return guarded([&] {
     if (!comm) return;
+    release_peer_exchange(*comm);
     if (comm->comm) check_nccl(nccl().commDestroy(comm->comm), "ncclCommDestroy");
     delete comm;
+  });
+}
+
+int ask_b200_comm_status(ask_b200_comm* comm, int* status, int* peer_exchange) {
+  return guarded([&] {
+    if (!comm || !status) fail(ASK_B200_E_INVALID, "NULL argument");
+    *status = 0;
+    if (peer_exchange) *peer_exchange = comm->p2p ? 1 : 0;
+    if (!comm->p2p) return;
+    uint32_t word = 0;
+    check_cuda(cudaMemcpy(&word, static_cast<char*>(comm->inbox) + kInboxStatusOffset, sizeof(word),
+                          cudaMemcpyDeviceToHost), "read exchange status");
+    *status = word ? ASK_B200_E_TIMEOUT : 0;
   });
 }
 
@@ -1228,10 +1366,15 @@ int ask_b200_plan_launch_sharded(const ask_b200_plan* plan, ask_b200_comm* comm,
     RedPartial* mine = reinterpret_cast<RedPartial*>(base + plan->record_offset);
     RedPartial* all = mine + plan->red.n_red;
     launch_plan(*plan, ports, scratch, st, mine);
-    const size_t rec_bytes = size_t(plan->red.n_red) * sizeof(RedPartial);
-    check_nccl(nccl().allGather(mine, all, rec_bytes, ncclUint8, comm->comm, st), "ncclAllGather");
     RedArgs a = plan->red;
     for (size_t k = 0; k < plan->outputs.size(); ++k) a.out[k] = reinterpret_cast<void*>(ports[plan->inputs.size() + k]);
+    if (comm->p2p) {
+      check_cuda(red_exchange_combine(a, mine, comm->inboxes_dev, comm->nranks, comm->rank, comm->timeout_ns, st),
+                 "exchange launch");
+      return;
+    }
+    const size_t rec_bytes = size_t(plan->red.n_red) * sizeof(RedPartial);
+    check_nccl(nccl().allGather(mine, all, rec_bytes, ncclUint8, comm->comm, st), "ncclAllGather");
     check_cuda(red_combine_records(a, all, comm->nranks, st), "combine launch");
   });
 }

@@ -439,6 +439,92 @@ __global__ void __launch_bounds__(kRedThreads)
   }
 }
 
+// ---- cross-GPU record exchange over peer memory ------------------------------------------
+// Inbox layout (kernels.h): records [2 parities][ranks][kMaxReductions], then
+// one flag per rank, the epoch counter and the status word.  Every launch takes
+// the next epoch e; rank r stores its records into slot (e & 1, r) of every
+// inbox and raises flag r to e.  A rank can be at most one epoch ahead of
+// another (it waits for everyone's flag before it finishes), so the parity
+// keeps a fast rank's next records out of the slots a slow rank still reads.
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void __launch_bounds__(kRedThreads)
+    red_exchange_kernel(const __grid_constant__ RedArgs a, const RedPartial* __restrict__ mine,
+                        void* const* __restrict__ inboxes, int nranks, int rank, uint64_t timeout_ns) {
+  pdl_enter();
+  __shared__ int s_ok;
+  __shared__ uint64_t s_epoch;
+  char* own = static_cast<char*>(inboxes[rank]);
+  uint64_t* flags = reinterpret_cast<uint64_t*>(own + kInboxFlagsOffset);
+  uint64_t* seq = reinterpret_cast<uint64_t*>(own + kInboxSeqOffset);
+  if (threadIdx.x == 0) {
+    const uint64_t epoch = *seq + 1;
+    *seq = epoch;
+    s_epoch = epoch;
+    const size_t slot = (size_t(epoch & 1) * kExchangeMaxRanks + size_t(rank)) * kMaxReductions;
+    // this rank's records into every inbox (plain stores; peers' over NVLink),
+    // then one release store per flag orders them before the flag
+    for (int r = 0; r < nranks; ++r) {
+      RedPartial* dst = reinterpret_cast<RedPartial*>(inboxes[r]) + slot;
+      for (int k = 0; k < a.n_red; ++k) dst[k] = mine[k];
+    }
+    __threadfence_system();
+    for (int r = 0; r < nranks; ++r)
+      st_release_sys(reinterpret_cast<uint64_t*>(static_cast<char*>(inboxes[r]) + kInboxFlagsOffset) + rank, epoch);
+    // bounded wait for every rank's flag
+    const uint64_t t0 = global_ns();
+    int ok = 1;
+    for (int r = 0; r < nranks && ok; ++r) {
+      while (ld_acquire_sys(flags + r) < epoch) {
+        if (global_ns() - t0 > timeout_ns) {
+          ok = 0;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    if (!ok) *reinterpret_cast<uint32_t*>(own + kInboxStatusOffset) = 1u;
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  // fold the ranks' records in rank order (relaxed system-scope loads: the
+  // slots were written by other GPUs after this SM may have cached older ones)
+  const RedPartial* recs = reinterpret_cast<const RedPartial*>(own) + size_t(s_epoch & 1) * kExchangeMaxRanks * kMaxReductions;
+  Accs s;
+  accs_init(a, s);
+  for (int j = threadIdx.x; j < nranks; j += kRedThreads) {
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(recs + size_t(j) * kMaxReductions);
+    Accs x;
+#pragma unroll
+    for (int k = 0; k < kMaxReductions; ++k)
+      if (k < a.n_red) {
+        x.v[k] = ld_relaxed_sys(src + 2 * k);
+        x.i[k] = int64_t(ld_relaxed_sys(src + 2 * k + 1));
+      }
+    accs_merge(a, s, x);
+  }
+  accs_block_reduce(a, s);
+  if (threadIdx.x == 0) write_outputs(a, s, 0);
+}
+
 // ---- specialisation table ------------------------------------------------------------
 using SetRowStats = RedSet<RED_SUM, RED_MAX, RED_MIN, RED_ARGMAX>;
 using SetGlobal = RedSet<RED_SUM, RED_MIN, RED_ARGMIN>;
@@ -560,6 +646,14 @@ int red_view_occupancy() {
   int blocks = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, red_view_generic, kRedThreads, 0) != cudaSuccess) return 1;
   return blocks > 0 ? blocks : 1;
+}
+
+cudaError_t red_exchange_combine(const RedArgs& a, const RedPartial* mine, void* const* inboxes, int nranks, int rank,
+                                 uint64_t timeout_ns, cudaStream_t st) {
+  if (a.outer != 1 || nranks < 1 || nranks > kExchangeMaxRanks || rank < 0 || rank >= nranks)
+    return cudaErrorInvalidValue;
+  (void)launch_pdl(&red_exchange_kernel, dim3(1), dim3(kRedThreads), st, a, mine, inboxes, nranks, rank, timeout_ns);
+  return cudaGetLastError();
 }
 
 cudaError_t red_combine_records(const RedArgs& a, const RedPartial* records, int n, cudaStream_t st) {

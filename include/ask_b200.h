@@ -50,6 +50,7 @@ extern "C" {
 #define ASK_B200_E_CUDA (-3)        /* CUDA runtime error (message has the CUDA string) */
 #define ASK_B200_E_NCCL (-4)        /* NCCL unavailable or a collective failed */
 #define ASK_B200_E_DEVICE (-5)      /* no usable sm_100 device, or wrong current device */
+#define ASK_B200_E_TIMEOUT (-6)     /* a bounded wait for other ranks ran out (ask_b200_comm_status) */
 
 typedef struct ask_b200_plan ask_b200_plan;
 typedef struct ask_b200_comm ask_b200_comm;
@@ -147,6 +148,22 @@ ASK_B200_API int ask_b200_comm_create(const unsigned char id[128], int nranks, i
 ASK_B200_API int ask_b200_comm_destroy(ask_b200_comm *comm);
 ASK_B200_API int ask_b200_plan_launch_sharded(const ask_b200_plan *plan, ask_b200_comm *comm, const uint64_t *ports,
                                  size_t n_ports, uint64_t scratch, void *stream);
+/*
+ * The records cross GPUs by peer memory when every rank could map the others'
+ * small exchange buffer (CUDA IPC over NVLink; decided once, at
+ * ask_b200_comm_create, identically on every rank): one kernel stores this
+ * rank's records into every rank's buffer, raises a flag per rank and waits
+ * for every rank's flag -- a wait bounded by ASK_B200_EXCHANGE_TIMEOUT_MS
+ * (default 1000 ms) -- then folds the records in rank order.  Otherwise the
+ * NCCL all-gather runs.  Every rank must make the same sequence of sharded
+ * launches.  ask_b200_comm_status reports whether the peer exchange is in use
+ * and, synchronously, whether any wait ran out (ASK_B200_E_TIMEOUT: the
+ * outputs of that launch were left unwritten and the communicator must be
+ * destroyed; its exchange buffer then stays allocated until the process exits,
+ * since a late peer may still store into it).  ask_b200_comm_destroy waits for
+ * this device's work first.  No counterpart in the reference.
+ */
+ASK_B200_API int ask_b200_comm_status(ask_b200_comm *comm, int *status, int *peer_exchange);
 
 /*
  * Seeded synthetic inputs (Philox4x32-10), generated on the device: element i

@@ -1,7 +1,10 @@
-"""Sharded cfg5 on several GPUs (one process per GPU): the all-gather combine of
-ask_b200_plan_launch_sharded must give every rank the single-GPU answer, and
-the i32 shards (no collective) must equal the corresponding slice.  Skipped
-when fewer than two GPUs are visible."""
+"""Sharded cfg5 on several GPUs (one process per GPU): the record exchange of
+ask_b200_plan_launch_sharded -- over peer memory, or by the NCCL all-gather
+when the peer exchange is switched off -- must give every rank the single-GPU
+answer, and the i32 shards (no collective) must equal the corresponding slice.
+A rank that skips a launch makes the others' bounded wait run out: they report
+ASK_B200_E_TIMEOUT instead of hanging.  Skipped when fewer than two GPUs are
+visible.  NVLS is off in every child (NCCL_NVLS_ENABLE=0)."""
 import os
 import socket
 
@@ -22,8 +25,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, queue):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+def _rank(rank, world, port, queue, peer=True):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    if not peer:
+        os.environ["ASK_B200_NO_PEER_EXCHANGE"] = "1"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     comm = None
@@ -45,9 +50,11 @@ def _rank(rank, world, port, queue):
         outs = [torch.empty(1, device="cuda"), torch.empty(1, device="cuda"),
                 torch.empty(1, dtype=torch.int64, device="cuda")]
         scratch = torch.empty(plan.scratch_bytes, dtype=torch.uint8, device="cuda")
-        for _ in range(3):  # repeated launches reuse scratch and records
+        for _ in range(5):  # repeated launches reuse scratch, records and the inboxes' two parities
             plan.launch_sharded(comm, [x], outs, scratch, st)
         torch.cuda.synchronize()
+        status, used_peer = comm.status()
+        assert status == ask_b200.OK and used_peer == peer, (status, used_peer)
         # the i32 chain on this rank's slice
         nb = (1 << 24) + 7
         bb, be = R.shard_range(nb, world, rank)
@@ -60,13 +67,15 @@ def _rank(rank, world, port, queue):
         torch.cuda.synchronize()
         queue.put((rank, (float(outs[0].item()), float(outs[1].item()), int(outs[2].item())),
                    (bb, z.cpu().numpy())))
+        dist.barrier()  # every rank's launches are done before any communicator goes
     finally:
         if comm is not None:
             comm.close()
         dist.destroy_process_group()
 
 
-def test_sharded_cfg5_matches_single_gpu(device):
+@pytest.mark.parametrize("peer", [True, False], ids=["peer_exchange", "nccl_all_gather"])
+def test_sharded_cfg5_matches_single_gpu(device, peer):
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs at least two GPUs")
@@ -76,7 +85,7 @@ def test_sharded_cfg5_matches_single_gpu(device):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, queue, peer)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
@@ -110,3 +119,67 @@ def test_sharded_cfg5_matches_single_gpu(device):
     for r in range(world):
         bb, zz = got[r][1]
         assert np.array_equal(zz, z[bb:bb + zz.size])
+
+
+def _timeout_rank(rank, world, port, queue):
+    """Rank 1 skips the second launch: rank 0 waits for its flag, gives up
+    after ASK_B200_EXCHANGE_TIMEOUT_MS and reports it.  Both ranks stay alive
+    (and keep their buffers mapped) until rank 0's kernel has returned."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      ASK_B200_EXCHANGE_TIMEOUT_MS="200")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    comm = None
+    try:
+        import ask_b200
+        from ask_b200 import recipes as R
+        uid = [ask_b200.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = ask_b200.Comm(uid[0], world, rank, rank)
+        st = torch.cuda.current_stream()
+        n = 1 << 20
+        x = torch.rand(n, device="cuda")
+        plan = ask_b200.Plan(R.cfg5a_step(n, index_base=rank * n), rank)
+        outs = [torch.full((1,), -1.0, device="cuda"), torch.full((1,), -1.0, device="cuda"),
+                torch.full((1,), -1, dtype=torch.int64, device="cuda")]
+        scratch = torch.empty(plan.scratch_bytes, dtype=torch.uint8, device="cuda")
+        plan.launch_sharded(comm, [x], outs, scratch, st)  # both ranks: completes
+        torch.cuda.synchronize()
+        first = comm.status()
+        dist.barrier()
+        if rank == 0:
+            outs[0].fill_(-7.0)
+            plan.launch_sharded(comm, [x], outs, scratch, st)  # nobody answers
+            torch.cuda.synchronize()
+        dist.barrier()  # rank 0's kernel has returned before anyone's buffers could go
+        queue.put((rank, first, comm.status(), float(outs[0].item())))
+        dist.barrier()
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_wait_is_bounded(device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    import ask_b200
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_timeout_rank, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        r, first, after, sum0 = queue.get(timeout=300)
+        got[r] = (first, after, sum0)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    if not got[0][0][1]:
+        pytest.skip("the peer exchange is not available between these GPUs (NCCL all-gather path)")
+    assert got[0][0] == (ask_b200.OK, True) and got[1][0] == (ask_b200.OK, True)
+    assert got[0][1] == (ask_b200.E_TIMEOUT, True)   # rank 0's wait ran out
+    assert got[0][2] == -7.0                          # ... and left its outputs as they were
+    assert got[1][1] == (ask_b200.OK, True)
