@@ -30,6 +30,7 @@ using ew::ew_functor_loop;
 using ew::ew_spec_loop;
 using ew::ew_view_loop;
 using ew::FnCfg1;
+using ew::FnCfg5b;
 using ew::FnSoftmaxNorm;
 
 template <class P, int V, int U>
@@ -95,7 +96,7 @@ struct EwSpecKernels {
 void* ew_kernel_ptr(int spec) {
   switch (spec) {
     case EW_CFG1: return reinterpret_cast<void*>(&ew_functor_kernel<FnCfg1>);
-    case EW_CFG5B: return EwSpecKernels<ProgCfg5b>::vec();
+    case EW_CFG5B: return reinterpret_cast<void*>(&ew_functor_kernel<FnCfg5b>);
     case EW_SOFTMAX_NORM_F16: return reinterpret_cast<void*>(&ew_functor_kernel<FnSoftmaxNorm<kF16>>);
     case EW_SOFTMAX_NORM_BF16: return reinterpret_cast<void*>(&ew_functor_kernel<FnSoftmaxNorm<kBF16>>);
     default: return reinterpret_cast<void*>(&ew_generic_kernel<4>);
@@ -142,6 +143,12 @@ cudaError_t ew_launch(int spec, const Program& prog, const EwArgs& args, int ali
   const dim3 g(grid), b(kEwThreads);
   if (spec == EW_CFG1 && functor_ok<FnCfg1>(args, aligned)) {
     (void)launch_pdl(&ew_functor_kernel<FnCfg1>, g, b, stream, args, args.count / FnCfg1::V);
+    return cudaGetLastError();
+  }
+  if (spec == EW_CFG5B && functor_ok<FnCfg5b>(args, aligned) &&
+      ((reinterpret_cast<uintptr_t>(args.in[0]) | reinterpret_cast<uintptr_t>(args.in[1]) |
+        reinterpret_cast<uintptr_t>(args.out[0])) & 31u) == 0) {
+    (void)launch_pdl(&ew_functor_kernel<FnCfg5b>, g, b, stream, args, args.count / FnCfg5b::V);
     return cudaGetLastError();
   }
   if (spec == EW_SOFTMAX_NORM_F16 && functor_ok<FnSoftmaxNorm<kF16>>(args, aligned)) {

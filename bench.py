@@ -553,11 +553,13 @@ def exchange_timing(w, args, torch, barrier, dist):
         return float(v.item())
     local = timed(lambda: pa.launch([x], outs, scratch, st))
     sharded = timed(lambda: pa.launch_sharded(comm, [x], outs, scratch, st))
+    st_code, peer = comm.status()
     return {"reduce_local_ms": round(local, 4), "reduce_sharded_ms": round(sharded, 4),
             "exchange_us": round(1000.0 * (sharded - local), 1),
-            "how": "sharded reduce (split + all-gather of 16-byte partial records + combine) minus the same plan "
-                   "combined locally, back-to-back launches, CUDA events, max over ranks; in a bench step it runs "
-                   "on a side stream beside the i32 chain"}
+            "transport": "peer stores over NVLink" if peer else "NCCL all-gather", "status": st_code,
+            "how": "sharded reduce (split kernel, records exchanged between the ranks, combine) minus the same plan "
+                   "combined locally, back-to-back launches, CUDA events, max over ranks: the exchange plus each "
+                   "launch's wait for the slowest rank; in a bench step it runs on a side stream beside the i32 chain"}
 
 
 def pcie_bandwidth(torch, barrier, dist, nbytes=1 << 30):
