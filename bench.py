@@ -692,8 +692,10 @@ def run_e2e(w, args, torch, barrier, dist):
         limiter = f"the host<->device link: the busier direction ({'H2D' if t_h2d >= t_d2h else 'D2H'}) alone needs " \
                   f"{100 * frac:.0f}% of the step at the measured copy rate"
     elif serial > 0.85:
-        limiter = f"copies in the two directions one after the other (one stream): together {100 * serial:.0f}% " \
-                  "of the step at the measured copy rates"
+        limiter = (f"the host<->device copies: at the rates measured with every rank copying at once, H2D and D2H "
+                   f"together need {100 * serial:.0f}% of the step ("
+                   + ("one stream orders them" if not groups else
+                      "the plans' streams overlap them, but both directions draw on the same host memory") + ")")
     else:
         limiter = f"neither link direction (busier {100 * frac:.0f}%, both {100 * serial:.0f}% of the step)"
     if kernels is not None:
