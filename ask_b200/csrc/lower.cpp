@@ -1595,9 +1595,30 @@ struct Split {
 //     them from internal buffers that elementwise recipes write first (the
 //     reference evaluates such operands per element inside its kernel,
 //     lib/Lowering/ScalarEmitter.h:775-815).
+// ask.mark pass-throughs (erased by the reference's prepare phase): every use
+// of a mark's result, and every return of it, reads the marked value itself.
+Func without_marks(Func f) {
+  std::map<std::string, std::string> to;
+  for (const Op& op : f.ops)
+    if (strip(op.name) == "mark" && op.operands.size() == 1) to[op.result] = op.operands[0];
+  auto resolve = [&](std::string v) {
+    for (auto it = to.find(v); it != to.end(); it = to.find(v)) v = it->second;
+    return v;
+  };
+  std::vector<Op> kept;
+  for (Op& op : f.ops) {
+    if (to.count(op.result)) continue;
+    for (std::string& x : op.operands) x = resolve(x);
+    kept.push_back(op);
+  }
+  f.ops = kept;
+  for (std::string& r : f.returns) r = resolve(r);
+  return f;
+}
+
 Split lower_source_split(const std::string& text) {
   Reader r(text);
-  const Func f = r.read_function();
+  const Func f = without_marks(r.read_function());
   std::map<std::string, const Op*> def;
   std::map<std::string, size_t> arg;
   for (const Op& op : f.ops) def[op.result] = &op;
@@ -1644,6 +1665,7 @@ Split lower_source_split(const std::string& text) {
     groups[g].push_back(k);
   }
   Split out;
+  std::map<std::string, int64_t> internal_of_value;  // a computed operand's internal buffer, written once
   auto plain = [](const Lowered& l, const std::vector<size_t>& results) {
     Part p{l, {}, {}};
     for (size_t a : l.input_args) p.ins.push_back(int64_t(a));
@@ -1664,25 +1686,37 @@ Split lower_source_split(const std::string& text) {
     size_t op_index = 0;
     while (part.ops[op_index].result != op.result) ++op_index;
     std::vector<int64_t> internal_of_arg;  // per extra argument of `part`, its internal buffer
+    std::map<std::string, std::string> arg_of_value;  // within this part: one extra argument per value
     for (size_t j = 0; j < op.operands.size(); ++j) {
-      const std::string& v = op.operands[j];
+      const std::string v = op.operands[j];
       if (arg.count(v)) continue;
       auto pd = def.find(v);
       if (pd == def.end()) invalid("value " + v + " is not defined");
       const Type t = pd->second->type;
-      Func pre = f;
-      pre.returns = {v};
-      const Lowered lp = Lowering(pre).run();
-      const int64_t k = int64_t(out.internal_bytes.size());
-      out.internal_bytes.push_back(t.numel() * element_bytes(t.dtype));
-      Part pp{lp, {}, {-1 - k}};
-      for (size_t a : lp.input_args) pp.ins.push_back(int64_t(a));
-      out.parts.push_back(pp);
-      const std::string name = "%ask_b200.internal" + std::to_string(k);
-      part.args.push_back(name);
-      part.arg_types.push_back(t);
-      internal_of_arg.push_back(k);
-      part.ops[op_index].operands[j] = name;
+      auto known = internal_of_value.find(v);
+      int64_t k;
+      if (known != internal_of_value.end()) {
+        k = known->second;
+      } else {
+        Func pre = f;
+        pre.returns = {v};
+        const Lowered lp = Lowering(pre).run();
+        k = int64_t(out.internal_bytes.size());
+        out.internal_bytes.push_back(t.numel() * element_bytes(t.dtype));
+        Part pp{lp, {}, {-1 - k}};
+        for (size_t a : lp.input_args) pp.ins.push_back(int64_t(a));
+        out.parts.push_back(pp);
+        internal_of_value[v] = k;
+      }
+      auto named = arg_of_value.find(v);
+      if (named == arg_of_value.end()) {
+        const std::string name = "%ask_b200.internal" + std::to_string(k);
+        part.args.push_back(name);
+        part.arg_types.push_back(t);
+        internal_of_arg.push_back(k);
+        named = arg_of_value.emplace(v, name).first;
+      }
+      part.ops[op_index].operands[j] = named->second;
     }
     const Lowered l = Lowering(part).run();
     Part p{l, {}, {}};

@@ -773,6 +773,43 @@ def test_gather_and_scatter_of_computed_operands():
     assert np.array_equal(bufs[4].reshape(rows, dim), want_out)
 
 
+def test_marked_and_shared_scatter_operands():
+    """A scatter_add whose operands are an ask.mark of an argument (erased, as
+    the reference's prepare phase erases marks) and one computed value used
+    twice (base and updates of the same shape) lowers to one elementwise step
+    into one internal buffer and the scatter_add step; a marked gather result
+    stays a gather step."""
+    rows, dim = 16, 8
+    s = Step("ask_kernel_0", "kernel0")
+    x, idx = s.arg([rows, dim], "i32"), s.arg([rows], "i64")
+    mi = s.op("mark", [idx], [rows], "i64", 'mark_id = "m0", role = "input", port_id = "idx"')
+    c = s.op("mul", [x, s.splat(s.const(3, "i32"), [rows, dim])], [rows, dim], "i32")
+    out = s.op("scatter_add", [c, mi, c], [rows, dim], "i32", "axis = 0 : i64")
+    out = s.op("mark", [out], [rows, dim], "i32", 'mark_id = "m1", role = "output", port_id = "out"')
+    buffers = [{"id": "x", "shape": [rows, dim], "element_type": "i32"},
+               {"id": "idx", "shape": [rows], "element_type": "i64"},
+               {"id": "out", "shape": [rows, dim], "element_type": "i32"}]
+    prog = rt.lower_report(report([s.text([out])], buffers, ["x", "idx"], ["out"], [(["x", "idx"], ["out"])]))
+    assert [st["id"] for st in prog["steps"]] == ["kernel0#0", "kernel0#1"]
+    assert prog["buffer_sizes"] == [4 * rows * dim, 8 * rows, 4 * rows * dim, 4 * rows * dim]  # one internal buffer
+    assert [st["outputs"] for st in prog["steps"]] == [[3], [2]]
+    assert prog["steps"][1]["inputs"] == [3, 1, 3]  # the mark's argument read directly
+    rng = np.random.default_rng(3)
+    xv = rng.integers(-9, 9, (rows, dim)).astype(np.int32)
+    iv = rng.integers(-2, rows + 2, rows).astype(np.int64)
+    bufs = run_program_on_cpu(prog, [xv, iv], {0: np.int32, 1: np.int64, 2: np.int32, 3: np.int32})
+    want = 3 * xv
+    ok = (iv >= 0) & (iv < rows)
+    np.add.at(want, iv[ok], (3 * xv)[ok])
+    assert np.array_equal(bufs[2].reshape(rows, dim), want)
+    g = Step("ask_kernel_0", "kernel0")
+    t, i = g.arg([rows, dim], "i32"), g.arg([4], "i64")
+    gm = g.op("mark", [g.op("gather", [t, i], [4, dim], "i32", "axis = 0 : i64")], [4, dim], "i32",
+              'mark_id = "m2", role = "output", port_id = "g"')
+    step = rt.lower_step(g.text([gm]))
+    assert step["recipe"]["family"] == "gather" and step["input_arguments"] == [0, 1]
+
+
 def random_mixed_step(seed):
     """A rank-3 i32 argument with results: a sum and a max over random axis
     sets (scattered ones included), an elementwise value and a strided slice
