@@ -156,7 +156,11 @@ ASK_B200_API int ask_b200_plan_launch_sharded(const ask_b200_plan *plan, ask_b20
  * for every rank's flag -- a wait bounded by ASK_B200_EXCHANGE_TIMEOUT_MS
  * (default 1000 ms) -- then folds the records in rank order.  Otherwise the
  * NCCL all-gather runs.  Every rank must make the same sequence of sharded
- * launches.  ask_b200_comm_status reports whether the peer exchange is in use
+ * launches, in one stream order per communicator (as for NCCL collectives):
+ * two sharded launches of one communicator running at once on different
+ * streams would take their epochs in different orders on different ranks.
+ * The epoch lives on the device, so a captured CUDA graph of sharded
+ * launches can be replayed.  ask_b200_comm_status reports whether the peer exchange is in use
  * and, synchronously, whether any wait ran out (ASK_B200_E_TIMEOUT: the
  * outputs of that launch were left unwritten and the communicator must be
  * destroyed; its exchange buffer then stays allocated until the process exits,

@@ -183,3 +183,75 @@ def test_peer_exchange_wait_is_bounded(device):
     assert got[0][1] == (ask_b200.E_TIMEOUT, True)   # rank 0's wait ran out
     assert got[0][2] == -7.0                          # ... and left its outputs as they were
     assert got[1][1] == (ask_b200.OK, True)
+
+
+def _graph_rank(rank, world, port, queue):
+    """Sharded launches captured once in a CUDA graph and replayed: the
+    exchange's epoch advances on the device, so every replay matches the
+    eagerly launched result."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    comm = None
+    try:
+        import ask_b200
+        from ask_b200 import recipes as R
+        uid = [ask_b200.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = ask_b200.Comm(uid[0], world, rank, rank)
+        n = (1 << 22) + 3 * rank
+        b = sum((1 << 22) + 3 * r for r in range(rank))
+        x = torch.empty(n, dtype=torch.float32, device="cuda")
+        ask_b200.generate(0, SEED, 0, b, n, 0.0, 1.0, x, torch.cuda.current_stream())
+        plan = ask_b200.Plan(R.cfg5a_step(n, index_base=b), rank)
+        scratch = torch.empty(plan.scratch_bytes, dtype=torch.uint8, device="cuda")
+        eager = [torch.empty(1, device="cuda"), torch.empty(1, device="cuda"), torch.empty(1, dtype=torch.int64, device="cuda")]
+        plan.launch_sharded(comm, [x], eager, scratch, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        outs = [torch.empty(1, device="cuda"), torch.empty(1, device="cuda"), torch.empty(1, dtype=torch.int64, device="cuda")]
+        side = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        dist.barrier()
+        with torch.cuda.graph(g, stream=side):
+            plan.launch_sharded(comm, [x], outs, scratch, side)
+        results = []
+        for _ in range(3):
+            for t in outs:
+                t.fill_(-1)
+            dist.barrier()
+            g.replay()
+            torch.cuda.synchronize()
+            results.append([float(outs[0].item()), float(outs[1].item()), int(outs[2].item())])
+        dist.barrier()
+        del g
+        queue.put((rank, [float(eager[0].item()), float(eager[1].item()), int(eager[2].item())], results,
+                   comm.status()))
+        dist.barrier()
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_sharded_launch_replays_in_a_cuda_graph(device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    import ask_b200
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_graph_rank, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        r, eager, replays, status = queue.get(timeout=300)
+        got[r] = (eager, replays, status)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):
+        eager, replays, status = got[r]
+        assert status[0] == ask_b200.OK
+        assert all(rep == eager for rep in replays), (eager, replays)
+    assert got[0][0] == got[1][0]
