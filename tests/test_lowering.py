@@ -1588,3 +1588,64 @@ def test_cuda_lowering_report():
     # every recipe step of a lowered report carries its report
     prog = rt.lower_report(softmax_report("f16", 64, 4096))
     assert all(REPORT_FIELDS <= set(s["cuda_lowering"]) for s in prog["steps"])
+
+
+def pipeline_report():
+    """A partition report shaped like the one the reference's partitioner
+    makes of its frontend pipeline fixture (owned y = x + 1, an external
+    kernel, owned + 3; tests/ir/pipeline.mlir): each step source is a module
+    that also carries the graph's module-level declarations (the partitioner
+    clones every non-function op into each step module, Partition.cpp:268-270)
+    and the ask.mark ports around the external step."""
+    decls = ('  "ask.semantics"() {\n    sym_name = "double_i32_v1",\n'
+             '    function_type = (tensor<?xi32>) -> tensor<?xi32>,\n'
+             '    shape_rule = "same_as", shape_operand = 0 : i64, effects = "none"\n  } : () -> ()\n'
+             '  "ask.implementation"() {\n    sym_name = "ext_double", compiler = "cuda", entry = "double_it",\n'
+             '    source = "extern \\22C\\22 __global__ void double_it(int* t, int* u) {\\0A}\\0A",\n'
+             '    signature = {t = "*i32", u = "*i32"}, source_bindings = {t = "input:0", u = "output:0"},\n'
+             '    constants = {N = 10 : i64}, options = {num_warps = 4 : i64},\n'
+             '    target = {backend = "cuda", arch = 100 : i64, warp_size = 32 : i64},\n'
+             '    grid = array<i64: 1, 1, 1>\n  } : () -> ()\n')
+
+    def step(fn, kid, k, mark):
+        body = (f'    %0 = "ask.constant"() {{value = {k} : i32}} : () -> i32\n'
+                '    %1 = "ask.splat"(%0) {shape = array<i64: 10>} : (i32) -> tensor<10xi32>\n')
+        arg = "%arg0"
+        if mark == "in":  # the external step's output port, marked where it enters
+            body += ('    %2 = "ask.mark"(%arg0) {mark_id = "m_F_out", value_id = "v_u", port_id = "F.out", '
+                     'role = "output"} : (tensor<10xi32>) -> tensor<10xi32>\n')
+            arg = "%2"
+        body += (f'    %3 = "ask.add"({arg}, %1) {{ask.id = "{kid}", overflow = "wrap"}} : '
+                 '(tensor<10xi32>, tensor<10xi32>) -> tensor<10xi32>\n')
+        res = "%3"
+        if mark == "out":
+            body += ('    %4 = "ask.mark"(%3) {mark_id = "m_F_in", value_id = "v_t", port_id = "F.in", role = "input"} '
+                     ': (tensor<10xi32>) -> tensor<10xi32>\n')
+            res = "%4"
+        return ("module attributes {ask.schema_version = 1 : i64} {\n" + decls +
+                f'  func.func @{fn}(%arg0: tensor<10xi32>) -> tensor<10xi32> attributes {{ask.kernel_id = "{kid}", '
+                'ask.kernel_kind = "owned"} {\n' + body + f"    return {res} : tensor<10xi32>\n  }}\n}}\n")
+    plan = {"schema_version": 1, "kind": "ask.cuda.execution_plan", "inputs": ["v_x"], "outputs": ["v_y"],
+            "buffers": [{"id": b, "shape": [10], "element_type": "i32"} for b in ("v_x", "v_t", "v_u", "v_y")],
+            "steps": [{"id": "P", "kind": "owned", "function": "kernel_0", "inputs": ["v_x"], "outputs": ["v_t"],
+                       "depends_on": []},
+                      {"id": "F", "kind": "external", "function": "kernel_1", "inputs": ["v_t"], "outputs": ["v_u"],
+                       "depends_on": ["P"], "external_id": "F"},
+                      {"id": "Q", "kind": "owned", "function": "kernel_2", "inputs": ["v_u"], "outputs": ["v_y"],
+                       "depends_on": ["F"]}],
+            "scheduling": {"policy": "sequential", "stream": "session"}}
+    return {"phase": "partitioned", "execution_plan": plan,
+            "step_sources": {"P": step("kernel_0", "P", 1, "out"), "Q": step("kernel_2", "Q", 3, "in")}}
+
+
+def test_pipeline_report_with_declarations_and_an_external_step():
+    prog = rt.lower_report(pipeline_report())
+    assert [s["id"] for s in prog["steps"]] == ["P", "F", "Q"] and prog["unresolved_steps"] == ["F"]
+    assert prog["steps"][1]["unresolved"] == {"kind": "external", "function": "kernel_1", "external_id": "F"}
+    x = np.array([0, 1, -1, 7, 2 ** 31 - 1, -(2 ** 31), 5, 6, 8, 9], np.int32)
+    (t,) = recipe_eval.evaluate(json.loads(prog["steps"][0]["recipe"]), [x])
+    u = (t.astype(np.int64) * 2).astype(np.int32)  # the external kernel, doubled with wrap
+    (y,) = recipe_eval.evaluate(json.loads(prog["steps"][2]["recipe"]), [u])
+    want = ((x.astype(np.int64) + 1) * 2 + 3).astype(np.int64)
+    want = ((want + 2 ** 31) % 2 ** 32 - 2 ** 31).astype(np.int32)
+    assert np.array_equal(y, want)
