@@ -255,3 +255,33 @@ def test_sharded_launch_replays_in_a_cuda_graph(device):
         assert status[0] == ask_b200.OK
         assert all(rep == eager for rep in replays), (eager, replays)
     assert got[0][0] == got[1][0]
+
+
+def test_single_rank_sharded_launch_matches_plain_launch(device):
+    """A communicator of one rank takes the peer-exchange path (its own inbox
+    only): repeated sharded launches equal the plan's plain launch bit for bit
+    and report no timeout.  Runs on one GPU."""
+    import ask_b200
+    from ask_b200 import recipes as R
+    torch.cuda.set_device(0)
+    comm = ask_b200.Comm(ask_b200.comm_unique_id(), 1, 0, 0)
+    try:
+        n = (1 << 24) + 5
+        x = torch.empty(n, dtype=torch.float32, device="cuda")
+        ask_b200.generate(0, SEED, 0, 0, n, 0.0, 1.0, x, torch.cuda.current_stream())
+        x[12345] = 0.0
+        plan = ask_b200.Plan(R.cfg5a_step(n), 0)
+        scratch = torch.empty(plan.scratch_bytes, dtype=torch.uint8, device="cuda")
+        mk = lambda: [torch.empty(1, device="cuda"), torch.empty(1, device="cuda"),
+                      torch.empty(1, dtype=torch.int64, device="cuda")]
+        plain = mk()
+        plan.launch([x], plain, scratch, torch.cuda.current_stream())
+        for _ in range(3):
+            got = mk()
+            plan.launch_sharded(comm, [x], got, scratch, torch.cuda.current_stream())
+            torch.cuda.synchronize()
+            assert [g.item() for g in got] == [p.item() for p in plain]
+        assert int(plain[2].item()) == 12345 and float(plain[1].item()) == 0.0
+        assert comm.status() == (ask_b200.OK, True)
+    finally:
+        comm.close()
