@@ -1323,7 +1323,13 @@ int ask_b200_comm_create(const unsigned char id[128], int nranks, int rank, int 
     std::unique_ptr<ask_b200_comm> c(new ask_b200_comm());
     c->nranks = nranks; c->rank = rank; c->device = device;
     check_nccl(nccl().commInitRank(&c->comm, nranks, uid, rank), "ncclCommInitRank");
-    setup_peer_exchange(*c);
+    try {
+      setup_peer_exchange(*c);
+    } catch (...) {
+      release_peer_exchange(*c);
+      (void)nccl().commDestroy(c->comm);
+      throw;
+    }
     *out = c.release();
   });
 }
