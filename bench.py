@@ -835,7 +835,12 @@ def main():
     if world == 1 and not args.no_per_config and args.workload == "cfg5" and not args.small:
         per_config = {}
         for name in PER_CONFIG:
-            per_config[name] = run_one(name, min(args.cpu_budget, 5.0))
+            try:
+                per_config[name] = run_one(name, min(args.cpu_budget, 5.0))
+            except Exception as e:  # one config failing must not take the headline line with it
+                torch.cuda.synchronize()
+                torch.cuda.empty_cache()
+                per_config[name] = {"error": f"{type(e).__name__}: {e}"[:500]}
 
     line = {"metric": METRIC, "value": head["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": head["ms_per_step"], "higher_is_better": True,
@@ -849,7 +854,7 @@ def main():
             line[key] = head[key]
     if per_config is not None:
         line["per_config"] = per_config
-        line["gpu_launches"] += sum(p["gpu_launches"] for p in per_config.values())
+        line["gpu_launches"] += sum(p.get("gpu_launches", 0) for p in per_config.values())
     if rank == 0:
         print(json.dumps(line), flush=True)
     if comm is not None:
