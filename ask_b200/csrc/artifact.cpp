@@ -283,12 +283,19 @@ Generated generate(const ask_b200_plan& pl, const std::string& entry, const uint
         // The library's hand-written loops for its specialised programs
         // (ew_kernels.cu: ew_launch), when every unit is whole and aligned.
         const char* functor = pl.spec == EW_CFG1 ? "askb::ew::FnCfg1"
+                              : pl.spec == EW_CFG5B ? "askb::ew::FnCfg5b"
                               : pl.spec == EW_SOFTMAX_NORM_F16 ? "askb::ew::FnSoftmaxNorm<askb::kF16>"
                               : pl.spec == EW_SOFTMAX_NORM_BF16 ? "askb::ew::FnSoftmaxNorm<askb::kBF16>" : nullptr;
         if (functor) {
-          body << "  using F = " << functor << ";\n  if (aligned && " << u64(pl.count) << " % F::V == 0 && (!F::kRowMapped || "
-               << u64(d.d) << " % F::V == 0))\n    askb::ew::ew_functor_loop<F>(args, " << u64(pl.count)
-               << " / F::V);\n  else\n  ";
+          // the cfg5b functor moves 32-byte units
+          std::string wide;
+          if (pl.spec == EW_CFG5B) {
+            for (size_t k = 0; k < ni; ++k) wide += " && askb::art::aligned32(" + ins(k) + ")";
+            for (size_t k = 0; k < no; ++k) wide += " && askb::art::aligned32(" + outs(k) + ")";
+          }
+          body << "  using F = " << functor << ";\n  if (aligned" << wide << " && " << u64(pl.count)
+               << " % F::V == 0 && (!F::kRowMapped || " << u64(d.d) << " % F::V == 0))\n    askb::ew::ew_functor_loop<F>(args, "
+               << u64(pl.count) << " / F::V);\n  else\n  ";
         }
         body << "  askb::ew::ew_spec_loop<Program, 4, 2>(args, aligned ? 1 : 0);\n";
         g.body = functor ? "elementwise_functor" : "elementwise";

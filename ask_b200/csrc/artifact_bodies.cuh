@@ -32,6 +32,7 @@ constexpr int kThreads = 256;  // block size of every artifact kernel
 constexpr int kFunctorMinBlocks = 5;
 
 __device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+__device__ __forceinline__ bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 // ---- reductions ----------------------------------------------------------------------
 // RL: the step's reductions, each folding program result src(k) of type type(k)

@@ -46,7 +46,7 @@ def cases():
     return {
         "cfg1": (R.cfg1_step(4099), "elementwise_functor"),
         "softmax_norm": (R.cfg3_steps("bf16", 64, 1024)[2], "elementwise_functor"),
-        "cfg5b": (R.cfg5b_step(1 << 20), "elementwise"),
+        "cfg5b": (R.cfg5b_step(1 << 20), "elementwise_functor"),
         "i64_scalar": (i64_rec, "elementwise"),
         "cfg2_rows": (R.cfg2_step(65536, 1024), "reduce_rows_warp_fast"),
         "softmax_max": (R.cfg3_steps("f16", 64, 4096)[0], "reduce_rows_cta_fast"),
