@@ -307,7 +307,7 @@ def test_cfg4_gather_full_size(device):
     t2, o2 = table.view(rows, dim).view(torch.int32), out.view(n, dim).view(torch.int32)
     for c in range(0, n, 1 << 20):  # every row, against torch's own gather as the checker
         assert torch.equal(o2[c:c + (1 << 20)], t2[idx[c:c + (1 << 20)]]), c
-    # the index distribution is the Zipf head the survey computes: row 0 ~ 12.4%
+    # the index distribution has the Zipf(1.1) head over 2^20 rows: row 0 receives about 12.4%
     frac0 = float((idx == 0).sum()) / n
     assert 0.11 < frac0 < 0.14
 
