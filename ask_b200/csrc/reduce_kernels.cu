@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(kRedThreads)
   const uint64_t o = blockIdx.x;
   AccsT<R> s;
   set_init<R, VT, 0>(s);
-  for (int j = threadIdx.x; j < n; j += kRedThreads) {
+  for (int j = threadIdx.x; j < n; j += int(blockDim.x)) {
     const RedPartial* src = part + (o * n + j) * R::N;
     AccsT<R> x;
 #pragma unroll
@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(kRedThreads)
   const uint64_t o = blockIdx.x;
   Accs s;
   accs_init(a, s);
-  for (int j = threadIdx.x; j < n; j += kRedThreads) {
+  for (int j = threadIdx.x; j < n; j += int(blockDim.x)) {
     const RedPartial* src = part + (o * n + j) * a.n_red;
     Accs x;
 #pragma unroll
@@ -438,6 +438,12 @@ __global__ void __launch_bounds__(kRedThreads)
     }
   }
 }
+
+// The record combines and the exchange run one warp per output: small enough
+// (registers, threads) to be resident beside a persistent streaming grid that
+// fills the SMs (a sharded step runs them beside the i32 chain), so they need
+// not wait for that grid to drain.
+constexpr int kCombineThreads = 32;
 
 // ---- cross-GPU record exchange over peer memory ------------------------------------------
 // Inbox layout (kernels.h): records [2 parities][ranks][kMaxReductions], then
@@ -510,7 +516,7 @@ __global__ void __launch_bounds__(kRedThreads)
   const RedPartial* recs = reinterpret_cast<const RedPartial*>(own) + size_t(s_epoch & 1) * kExchangeMaxRanks * kMaxReductions;
   Accs s;
   accs_init(a, s);
-  for (int j = threadIdx.x; j < nranks; j += kRedThreads) {
+  for (int j = threadIdx.x; j < nranks; j += int(blockDim.x)) {
     const uint64_t* src = reinterpret_cast<const uint64_t*>(recs + size_t(j) * kMaxReductions);
     Accs x;
 #pragma unroll
@@ -602,7 +608,7 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
     (void)launch_pdl(&red_split_kernel<S, R, U>, dim3(grid), dim3(kRedThreads), st, a, aligned, part);
     err = cudaGetLastError();
     if (err != cudaSuccess) return;
-    (void)launch_pdl(&red_combine_set_kernel<R, kF32>, dim3(unsigned(a.outer)), dim3(kRedThreads), st, a, part, grid, rec_out);
+    (void)launch_pdl(&red_combine_set_kernel<R, kF32>, dim3(unsigned(a.outer)), dim3(kCombineThreads), st, a, part, grid, rec_out);
     err = cudaGetLastError();
   });
   if (found) return err;
@@ -614,7 +620,7 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
   (void)launch_pdl(&red_split_generic<4>, dim3(grid), dim3(kRedThreads), st, prog, a, aligned, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(kRedThreads), st, a, part, grid, rec_out);
+  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(kCombineThreads), st, a, part, grid, rec_out);
   return cudaGetLastError();
 }
 
@@ -652,12 +658,12 @@ cudaError_t red_exchange_combine(const RedArgs& a, const RedPartial* mine, void*
                                  uint64_t timeout_ns, cudaStream_t st) {
   if (a.outer != 1 || nranks < 1 || nranks > kExchangeMaxRanks || rank < 0 || rank >= nranks)
     return cudaErrorInvalidValue;
-  (void)launch_pdl(&red_exchange_kernel, dim3(1), dim3(kRedThreads), st, a, mine, inboxes, nranks, rank, timeout_ns);
+  (void)launch_pdl(&red_exchange_kernel, dim3(1), dim3(kCombineThreads), st, a, mine, inboxes, nranks, rank, timeout_ns);
   return cudaGetLastError();
 }
 
 cudaError_t red_combine_records(const RedArgs& a, const RedPartial* records, int n, cudaStream_t st) {
-  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(kRedThreads), st, a, records, n, nullptr);
+  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(kCombineThreads), st, a, records, n, nullptr);
   return cudaGetLastError();
 }
 
