@@ -439,10 +439,11 @@ __global__ void __launch_bounds__(kRedThreads)
   }
 }
 
-// The record combines and the exchange run one warp per output: small enough
-// (registers, threads) to be resident beside a persistent streaming grid that
-// fills the SMs (a sharded step runs them beside the i32 chain), so they need
-// not wait for that grid to drain.
+// A sharded reduction's record combine and its exchange run one warp per
+// output: small enough (registers, threads) to be resident beside a persistent
+// streaming grid that fills the SMs (a sharded step runs them beside the i32
+// chain), so they need not wait for that grid to drain.  A combine that writes
+// the outputs of a single-GPU launch keeps the full CTA (nothing runs beside it).
 constexpr int kCombineThreads = 32;
 
 // ---- cross-GPU record exchange over peer memory ------------------------------------------
@@ -608,7 +609,8 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
     (void)launch_pdl(&red_split_kernel<S, R, U>, dim3(grid), dim3(kRedThreads), st, a, aligned, part);
     err = cudaGetLastError();
     if (err != cudaSuccess) return;
-    (void)launch_pdl(&red_combine_set_kernel<R, kF32>, dim3(unsigned(a.outer)), dim3(kCombineThreads), st, a, part, grid, rec_out);
+    (void)launch_pdl(&red_combine_set_kernel<R, kF32>, dim3(unsigned(a.outer)),
+                     dim3(rec_out ? kCombineThreads : kRedThreads), st, a, part, grid, rec_out);
     err = cudaGetLastError();
   });
   if (found) return err;
@@ -620,7 +622,8 @@ cudaError_t red_launch(int spec, int strategy, const Program& prog, const RedArg
   (void)launch_pdl(&red_split_generic<4>, dim3(grid), dim3(kRedThreads), st, prog, a, aligned, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(kCombineThreads), st, a, part, grid, rec_out);
+  (void)launch_pdl(&red_combine_kernel, dim3(unsigned(a.outer)), dim3(rec_out ? kCombineThreads : kRedThreads), st, a,
+                   part, grid, rec_out);
   return cudaGetLastError();
 }
 
