@@ -5,6 +5,7 @@
 
 #include "ask_numerics.cuh"
 #include "kernels.h"
+#include "pair_f32.cuh"
 #include "vec_io.cuh"
 
 namespace askb {
@@ -252,42 +253,28 @@ struct FnCfg1 {
 // ProgSoftmaxNorm<T>: y = cast(exp(cast(x, f32) + m*(-1)) / s, T), 8 elements per
 // unit; m and s are indexed by the row (unit*8 / inner).
 //
-// The division is the correctly rounded f32 quotient, computed from the row's
-// correctly rounded reciprocal y = RN(1/s) by Markstein's correction: with
-// q0 = RN(e*y) and two steps r = fma(-q, s, e) (exact when q is within an ulp
-// of e/s and no value is subnormal), q' = fma(r, y, q), the last q equals
-// RN(e/s) (P. Markstein, "Computation of elementary functions on the IBM
-// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990).  The
-// theorem's conditions -- s and y normal, a normal quotient -- are checked;
-// a unit that fails them (a zero, subnormal, infinite or NaN operand or
-// result, which softmax rows reach only at their extremes) is recomputed with
-// the IEEE division.  One reciprocal per row replaces one per element, and
-// the division no longer occupies the special-function unit per element.
+// A unit whose eight t = x + m*(-1) all lie in [-69, 0] (every unit of a
+// finite softmax row, where m is the row's maximum) with 2^-100 <= s <= 2^24
+// runs on f32 pairs: e = exp_pair(t) (pair_f32.cuh; a normal f32 within about
+// 3 ulps of exp(t), e >= 2^-99.6) and q = RN(e * RN(1/s)), a normal f32
+// (>= 2^-123.6) within 2 ulps of e / s, so RN16(q) is within one 16-bit ulp
+// of RN16(e / s).
+//
+// Any other unit computes exp with CUDA's expf and the correctly rounded f32
+// quotient, from the row's correctly rounded reciprocal y = RN(1/s) by
+// Markstein's correction: with q0 = RN(e*y) and two steps r = fma(-q, s, e)
+// (exact when q is within an ulp of e/s and no value is subnormal),
+// q' = fma(r, y, q), the last q equals RN(e/s) (P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990).  The theorem's conditions -- s and y normal, a normal
+// quotient -- are checked; a unit that fails them (a zero, subnormal,
+// infinite or NaN operand or result) is recomputed with the IEEE division.
 template <int T>
 struct FnSoftmaxNorm {
   static constexpr int V = 8;
   static constexpr bool kRowMapped = true;  // m, s are indexed by unit*8 / inner
   struct In { uint4 x; float nm, s, y; };
   using Out = uint4;
-  __device__ static float widen(uint32_t h) {
-    if constexpr (T == kF16) return __half2float(__ushort_as_half(uint16_t(h)));
-    else return __uint_as_float(h << 16);
-  }
-  __device__ static uint32_t narrow(float f) {
-    if constexpr (T == kF16) return __half_as_ushort(__float2half_rn(f));
-    else return bf16_bits_rne(f);
-  }
-  // Two non-NaN values rounded to nearest-even and packed (lo in bits 0..15):
-  // one cvt.rn.{f16,bf16}x2.f32.  For bf16 this equals bf16_bits_rne on every
-  // non-NaN input; NaN inputs take narrow() (the payload-preserving rule).
-  __device__ static uint32_t narrow2(float lo, float hi) {
-    uint32_t r;
-    if constexpr (T == kF16)
-      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    else
-      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-  }
   __device__ static In load(const EwArgs& e, uint64_t u) {
     const uint64_t row = udiv(u * V, e.inner);
     const float s = __ldg(static_cast<const float*>(e.in[2]) + row);
@@ -296,13 +283,24 @@ struct FnSoftmaxNorm {
   }
   __device__ static Out compute(const EwArgs&, const In& x) {
     const uint32_t w[4] = {x.x.x, x.x.y, x.x.z, x.x.w};
+    const float s = x.s, y = x.y;
+    uint32_t r[4];
+    if (s >= 0x1p-100f && s <= 0x1p24f && exp_pair_range<T>(w, x.nm)) {
+      const uint64_t nm2 = pack2(x.nm, x.nm), y2 = pack2(y, y);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float lo, hi;
+        unpack2(mul2(exp_pair(add2(pack2(widen_lo<T>(w[j]), widen_hi<T>(w[j])), nm2)), y2), lo, hi);
+        r[j] = narrow_two<T>(lo, hi);
+      }
+      return make_uint4(r[0], r[1], r[2], r[3]);
+    }
     float e[8], q[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      e[2 * j] = expf(__fadd_rn(widen(w[j] & 0xffffu), x.nm));
-      e[2 * j + 1] = expf(__fadd_rn(widen(w[j] >> 16), x.nm));
+      e[2 * j] = expf(__fadd_rn(widen_lo<T>(w[j]), x.nm));
+      e[2 * j + 1] = expf(__fadd_rn(widen_hi<T>(w[j]), x.nm));
     }
-    const float s = x.s, y = x.y;
     bool ok = s >= 0x1p-100f && s <= 0x1p100f;  // s and y = RN(1/s) normal (false for NaN)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -312,15 +310,14 @@ struct FnSoftmaxNorm {
       q[k] = t;
       ok &= (t >= 0x1p-124f && t <= 0x1p126f) || e[k] == 0.0f;
     }
-    uint32_t r[4];
     if (ok) {  // every q is finite
 #pragma unroll
-      for (int j = 0; j < 4; ++j) r[j] = narrow2(q[2 * j], q[2 * j + 1]);
+      for (int j = 0; j < 4; ++j) r[j] = narrow_two<T>(q[2 * j], q[2 * j + 1]);
     } else {
 #pragma unroll
       for (int k = 0; k < 8; ++k) q[k] = __fdiv_rn(e[k], s);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) r[j] = narrow(q[2 * j]) | (narrow(q[2 * j + 1]) << 16);
+      for (int j = 0; j < 4; ++j) r[j] = narrow_one<T>(q[2 * j]) | (narrow_one<T>(q[2 * j + 1]) << 16);
     }
     return make_uint4(r[0], r[1], r[2], r[3]);
   }

@@ -38,113 +38,12 @@
 
 #include "ask_numerics.cuh"
 #include "kernels.h"
+#include "pair_f32.cuh"
 #include "vec_io.cuh"
 
 namespace askb {
 
 namespace {
-
-template <int T>
-__device__ __forceinline__ float widen_lo(uint32_t w) {
-  if constexpr (T == kF16) return __half2float(__ushort_as_half(uint16_t(w & 0xffffu)));
-  else return __uint_as_float(w << 16);
-}
-template <int T>
-__device__ __forceinline__ float widen_hi(uint32_t w) {
-  if constexpr (T == kF16) return __half2float(__ushort_as_half(uint16_t(w >> 16)));
-  else return __uint_as_float(w & 0xffff0000u);
-}
-template <int T>
-__device__ __forceinline__ uint32_t narrow_one(float f) {
-  if constexpr (T == kF16) return __half_as_ushort(__float2half_rn(f));
-  else return bf16_bits_rne(f);
-}
-// Two finite values rounded to nearest even and packed, lo in bits 0..15.
-template <int T>
-__device__ __forceinline__ uint32_t narrow_two(float lo, float hi) {
-  uint32_t r;
-  if constexpr (T == kF16)
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  else
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-// llvm.maximum on f32 in one instruction: NaN if either operand is NaN (the
-// canonical NaN), otherwise the larger, with -0 < +0.
-__device__ __forceinline__ float max_nan(float a, float b) {
-  float r;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-
-// The same on two packed f16/bf16 values at once (NaN-propagating max), and
-// the plain packed minimum; widening to f32 is exact and monotone, so the
-// max/min of the widened values equals the widened max/min.
-template <int T>
-__device__ __forceinline__ uint32_t max2_nan(uint32_t a, uint32_t b) {
-  uint32_t r;
-  if constexpr (T == kF16)
-    asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  else
-    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-template <int T>
-__device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  if constexpr (T == kF16)
-    asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  else
-    asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-// Pairs of f32 values in one 64-bit register (element 0 in the low half).
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ float ex2_approx(float a) {
-  float r;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(a));
-  return r;
-}
-
-// exp(t) of a pair with -69 <= t <= 0 (see the file comment).
-constexpr float kLog2e = 0x1.715476p+0f;      // RN(log2 e)
-constexpr float kLog2eTail = 0x1.4ae0cp-26f;  // RN(log2 e - kLog2e)
-constexpr float kLn2 = 0x1.62e43p-1f;         // RN(ln 2)
-__device__ __forceinline__ uint64_t exp_pair(uint64_t t) {
-  const uint64_t L = pack2(kLog2e, kLog2e), nL = pack2(-kLog2e, -kLog2e);
-  const uint64_t tail = pack2(kLog2eTail, kLog2eTail), ln2 = pack2(kLn2, kLn2);
-  const uint64_t hi = mul2(t, L);
-  uint64_t lo = fma2(t, L, mul2(t, nL));  // t*L - hi, exact
-  lo = mul2(fma2(t, tail, lo), ln2);
-  float h0, h1;
-  unpack2(hi, h0, h1);
-  const uint64_t p = pack2(ex2_approx(h0), ex2_approx(h1));
-  return fma2(p, lo, p);
-}
 
 constexpr int kMaxWarps = 16;
 #ifndef ASKB_SOFTMAX_THREADS

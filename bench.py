@@ -37,7 +37,7 @@ sys.path.insert(0, ROOT)
 SEED = {"cfg1": 0xA5C1, "cfg2": 0xA5C2, "cfg3": 0xA5C3, "cfg4": 0xA5C4, "cfg5": 0xA5C5}
 METRIC = "achieved HBM GB/s per plan (% of ~8 TB/s) at 1/2/4/8 B200 vs ASK host CPU"
 # measured beside the headline cfg5 at N=1 (single-GPU configs: replicas only at N>1)
-PER_CONFIG = ["cfg1", "cfg2", "cfg3", "cfg3bf", "cfg4g", "cfg4s"]
+PER_CONFIG = ["cfg1", "cfg2", "cfg3", "cfg3bf", "cfg3u", "cfg4g", "cfg4s"]
 
 
 def peaks():
@@ -133,6 +133,10 @@ def static_config(name, world, small=False):
     if name in ("cfg3", "cfg3bf"):
         dt = "f16" if name == "cfg3" else "bf16"
         return {"workload": f"cfg3: 3-step softmax plan, {dt} [32768,4096]", "l2": "256 MB input > L2"}
+    if name in ("cfg3u", "cfg3ubf"):
+        dt = "f16" if name == "cfg3u" else "bf16"
+        return {"workload": f"cfg3: 3-step softmax plan, {dt} [32768,4096], each owned step its own plan launch "
+                            "(no runtime fusion)", "l2": "256 MB input > L2"}
     if name == "cfg4g":
         return {"workload": "cfg4 gather: table f32 [2^20,256], idx i64 Zipf(1.1) [2^23]", "l2": "8 GiB output > L2"}
     if name == "cfg4s":
@@ -282,6 +286,28 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         w.config = static_config(name, world)
         w.e2e = {"inputs": [x], "results": outs}
         w.tensors = {"x": x, "outs": outs, "rows": rows, "cols": cols}
+    elif name in ("cfg3u", "cfg3ubf"):
+        # The same plan launched step by step through ask_b200_plan_launch, as
+        # a Runtime that binds each owned step to its own kernel does: three
+        # kernels, x read by each.
+        dt = "f16" if name == "cfg3u" else "bf16"
+        rows, cols = 32768, 4096
+        n = rows * cols
+        x = gen(2 if dt == "f16" else 3, SEED["cfg3"], 0, n, 0.0, 2.0, torch.int16)
+        m = torch.empty(rows, dtype=torch.float32, device=dev)
+        s = torch.empty(rows, dtype=torch.float32, device=dev)
+        y = torch.empty_like(x)
+        w.plans = [ask_b200.Plan(r, rank_device()) for r in R.cfg3_steps(dt, rows, cols)]
+        pm, ps, py = w.plans
+        w.kernels = [(f"reduce_warp_row_softmax_max_{dt}", 2 * n + 4 * rows, pm.bind([x], [m], None, st)),
+                     (f"reduce_warp_row_softmax_sum_{dt}", 2 * n + 8 * rows, ps.bind([x, m], [s], None, st)),
+                     (f"ew_softmax_norm_{dt}", 4 * n + 8 * rows, py.bind([x, m, s], [y], None, st))]
+        w.config = dict(static_config(name, world),
+                        graded_bytes="each step's port bytes: max 2n + 4*rows, sum 2n + 8*rows, "
+                                     "normalise 4n + 8*rows")
+        w.dtype = dt
+        w.e2e = {"inputs": [x], "results": [y]}
+        w.tensors = {"x": x, "m": m, "s": s, "y": y, "rows": rows, "cols": cols}
     elif name in ("cfg3", "cfg3bf"):
         dt = "f16" if name == "cfg3" else "bf16"
         rows, cols = 32768, 4096
@@ -426,8 +452,8 @@ def check_outputs(w, torch, dist, world):
         fails += int(((s.double() - ref).abs() > tol).sum())
         fails += int((mx != x.amax(1)).sum()) + int((mn != x.amin(1)).sum()) + int((am != x.argmax(1)).sum())
         notes = {"checked": "every row: sum vs f64 (tol 2^-20*sum|x|), max/min/argmax (first index) bit-exact vs torch"}
-    elif w.name in ("cfg3", "cfg3bf"):
-        tdt = torch.float16 if w.name == "cfg3" else torch.bfloat16
+    elif w.name in ("cfg3", "cfg3bf", "cfg3u", "cfg3ubf"):
+        tdt = torch.float16 if w.name in ("cfg3", "cfg3u") else torch.bfloat16
         x = t["x"].view(tdt).view(t["rows"], t["cols"]).float()
         m, s, y = t["m"], t["s"], t["y"]
         mref = x.amax(1)
@@ -887,6 +913,8 @@ def cpu_case(name: str, threads: int, full: bool):
     import numpy as np
     import oracle
     name = ARTIFACT_WORKLOADS.get(name, name)
+    by_steps = name in ("cfg3u", "cfg3ubf")  # counted at the three steps' port bytes
+    name = {"cfg3u": "cfg3", "cfg3ubf": "cfg3bf"}.get(name, name)
     gt = max(threads, host_threads())
     avail = host_memory_available()
 
@@ -922,10 +950,12 @@ def cpu_case(name: str, threads: int, full: bool):
         rows, cols = (32768 if full else 1024), 4096
         x = oracle.generate(2 if dt == "f16" else 3, SEED["cfg3"], 0, 0, rows * cols, 0.0, 2.0, threads=gt)
         y = np.empty(rows * cols, np.uint16)
-        # the 3-step plan reads x three times: the same plan-port bytes as the GPU arm's plan_port_gbs;
-        # the GPU's roofline counts its own (fused) bytes, 4 per element
-        return ((lambda th: oracle.softmax(dt, x, rows, cols, threads=th, out=y)), 4 * rows * cols + 8 * rows,
-                f"cfg3 ({dt}) over {rows} rows, 3-step plan, counted at the fused step's bytes")
+        # the oracle runs the 3-step plan (x read three times); counted at the bytes the GPU arm's
+        # value counts: the fused step's own (4 per element) or, for cfg3u, the three steps' ports
+        nbytes = 8 * rows * cols + 20 * rows if by_steps else 4 * rows * cols + 8 * rows
+        return ((lambda th: oracle.softmax(dt, x, rows, cols, threads=th, out=y)), nbytes,
+                f"cfg3 ({dt}) over {rows} rows, 3-step plan, counted at "
+                + ("the three steps' port bytes" if by_steps else "the fused step's bytes"))
     rows, dim = 1 << 20, 256
     n = (1 << 23) if full else (1 << 18)
     idx = oracle.generate(5, SEED["cfg4"], 1, 0, n, 1.1, rows, threads=gt)

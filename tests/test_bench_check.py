@@ -119,7 +119,7 @@ def test_cfg2():
     assert bench.check_outputs(w, torch, None, 1)["failures"] == 1
 
 
-@pytest.mark.parametrize("name,tdt", [("cfg3", torch.float16), ("cfg3bf", torch.bfloat16)])
+@pytest.mark.parametrize("name,tdt", [("cfg3", torch.float16), ("cfg3bf", torch.bfloat16), ("cfg3u", torch.float16)])
 def test_cfg3(name, tdt):
     rng = np.random.default_rng(4)
     rows, cols = 16, 512

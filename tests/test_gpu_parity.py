@@ -253,6 +253,81 @@ def test_fused_softmax_full_size_matches_three_steps(device, dtype):
     assert int(d.max()) <= 1 and float((d != 0).float().mean()) < 1e-3
 
 
+def _rn16(q32: np.ndarray, dtype: str) -> np.ndarray:
+    """f32 -> f16/bf16 bits, round to nearest even (NaN -> a quiet NaN)."""
+    if dtype == "f16":
+        return q32.astype(np.float16).view(np.uint16)
+    b = q32.view(np.uint32).astype(np.uint64)
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(np.isnan(q32), np.uint16(0x7FC0), r)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_softmax_steps_with_given_m_and_s(device, dtype):
+    """The sum and normalise steps launched on their own, with m and s that are
+    not the row's own (t above 0 or below -69, s outside [2^-100, 2^24], zero,
+    negative, NaN, infinite), so that units take both the paired-exp path and
+    the scalar one.  Per element: t = RN32(x + RN32(-m)), e = exp(t);
+    s within 2^-20 of the f64 sum of RN32(e); y within one 16-bit ulp of
+    RN16(RN32(RN32(e) / s)), NaN where it is NaN, infinities exactly."""
+    rng = np.random.default_rng(11)
+    rows, cols = 48, 1024
+    xf = rng.normal(0.0, 3.0, rows * cols).astype(np.float32)
+    if dtype == "f16":
+        xh = xf.astype(np.float16).view(np.uint16)
+        nan16, inf16 = 0x7E00, 0x7C00
+    else:
+        xh = (xf.view(np.uint32) >> 16).astype(np.uint16)
+        nan16, inf16 = 0x7FC0, 0x7F80
+    xh[3 * cols + 100] = nan16
+    xh[4 * cols + 7] = inf16
+    xv = (f16_to_f32(xh) if dtype == "f16" else bf16_to_f32(xh)).reshape(rows, cols)
+    with np.errstate(invalid="ignore"):
+        rmax = xv.max(axis=1)
+    m = np.empty(rows, np.float32)
+    for r in range(rows):
+        m[r] = [rmax[r], rmax[r] - 5.0, rmax[r] + 80.0, np.nan, np.inf, -np.inf, 0.0, rmax[r] + 60.0][r % 8]
+    with np.errstate(all="ignore"):
+        t = (xv + (m * np.float32(-1.0))[:, None]).astype(np.float32)
+        e32 = np.exp(t.astype(np.float64)).astype(np.float32)
+        sref = e32.astype(np.float64).sum(axis=1)
+    x = torch.from_numpy(xh.view(np.int16)).cuda()
+    steps = [ask_b200.Plan(r, 0) for r in R.cfg3_steps(dtype, rows, cols)]
+    st = torch.cuda.current_stream()
+    s_dev = torch.empty(rows, dtype=torch.float32, device="cuda")
+    steps[1].launch([x, torch.from_numpy(m).cuda()], [s_dev], None, st)
+    torch.cuda.synchronize()
+    gs = s_dev.cpu().numpy().astype(np.float64)
+    assert np.array_equal(np.isnan(gs), np.isnan(sref))
+    fin = np.isfinite(sref)
+    assert np.array_equal(gs[~fin & ~np.isnan(sref)], sref[~fin & ~np.isnan(sref)])
+    assert np.all(np.abs(gs[fin] - sref[fin]) <= 2.0 ** -20 * np.abs(sref[fin]))
+    # s given to the normalise step: the row's own sum, then values around and outside the pair range
+    s_in = sref.astype(np.float32)
+    for r in range(rows):
+        k = (r // 8) % 6
+        s_in[r] = [s_in[r], s_in[r] * 2.0 ** 25, np.float32(1e-20), 0.0, -1.5, np.inf][k] if r % 8 < 3 else s_in[r]
+    s_in[47] = np.nan
+    y = torch.empty_like(x)
+    steps[2].launch([x, torch.from_numpy(m).cuda(), torch.from_numpy(s_in).cuda()], [y], None, st)
+    torch.cuda.synchronize()
+    with np.errstate(all="ignore"):
+        q32 = (e32.astype(np.float64) / s_in.astype(np.float64)[:, None]).astype(np.float32)
+    ry = _rn16(q32.reshape(-1), dtype)
+    gy = y.cpu().numpy().view(np.uint16)
+    conv = f16_to_f32 if dtype == "f16" else bf16_to_f32
+    gyv, ryv = conv(gy), conv(ry)
+    nan = np.isnan(ryv)
+    assert np.array_equal(np.isnan(gyv), nan)
+    inf = np.isinf(ryv)
+    assert np.array_equal(gyv[inf], ryv[inf])
+    fin = ~nan & ~inf
+    step = np.spacing(np.abs(ryv[fin]).astype(np.float16)).astype(np.float32) if dtype == "f16" else \
+        np.abs(conv(ry[fin] + 1) - ryv[fin])
+    bad = np.abs(gyv[fin] - ryv[fin]) > step + 1e-45
+    assert not bad.any(), f"{int(bad.sum())} outputs differ by more than one 16-bit ulp"
+
+
 # ---- cfg4: gather / scatter_add ---------------------------------------------------------
 @pytest.mark.parametrize("itype", ["i64", "i32"])
 @pytest.mark.parametrize("inner,dtype", [(256, "f32"), (3, "f32"), (8, "f16"), (5, "i64"), (64, "bool")])
