@@ -6,7 +6,6 @@
 #pragma once
 
 #include "programs.h"
-#include "pair_f32.cuh"
 #include "reduce_acc.cuh"
 
 namespace askb {
@@ -216,31 +215,14 @@ __device__ __forceinline__ constexpr bool needs_probe() {
 template <class R, int V>
 __device__ __forceinline__ void fast_fold_full(FastAcc& s, const float (&x)[V], uint32_t idx0) {
   if constexpr (set_has<R, RED_SUM>()) {
-    // Pairwise tree t[v] += t[v + w], w = V/2, ..., 1, then into fs.  For
-    // V >= 4 every level but the last runs on f32 pairs (add.rn.f32x2 on
-    // (t[2v], t[2v+1]) and (t[2v+w], t[2v+w+1]): the same sums, two an
-    // instruction).
-    if constexpr (V >= 4 && V % 4 == 0) {
-      uint64_t p[V / 2];
+    float t[V];
 #pragma unroll
-      for (int v = 0; v < V / 2; ++v) p[v] = pack2(x[2 * v], x[2 * v + 1]);
+    for (int v = 0; v < V; ++v) t[v] = x[v];
 #pragma unroll
-      for (int w = V / 4; w > 0; w >>= 1)
+    for (int w = V / 2; w > 0; w >>= 1)
 #pragma unroll
-        for (int v = 0; v < w; ++v) p[v] = add2(p[v], p[v + w]);
-      float lo, hi;
-      unpack2(p[0], lo, hi);
-      s.fs = __fadd_rn(s.fs, __fadd_rn(lo, hi));
-    } else {
-      float t[V];
-#pragma unroll
-      for (int v = 0; v < V; ++v) t[v] = x[v];
-#pragma unroll
-      for (int w = V / 2; w > 0; w >>= 1)
-#pragma unroll
-        for (int v = 0; v < w; ++v) t[v] = __fadd_rn(t[v], t[v + w]);
-      s.fs = __fadd_rn(s.fs, t[0]);
-    }
+      for (int v = 0; v < w; ++v) t[v] = __fadd_rn(t[v], t[v + w]);
+    s.fs = __fadd_rn(s.fs, t[0]);
   } else if constexpr (needs_probe<R>()) {
 #pragma unroll
     for (int v = 0; v < V; ++v) s.fs = __fmaf_rn(x[v], 0.0f, s.fs);  // NaN once any value is not finite
@@ -448,12 +430,8 @@ struct SrcCast {  // ProgSoftmaxMax<T>: cast(x, f32)
   static constexpr int kUnroll = 4;
 };
 
-// ProgSoftmaxSum<T>: exp(cast(x, f32) + m*(-1)), m indexed by the row.  A load
-// whose eight t = x + m*(-1) lie in [-69, 0] (every load of a finite row when
-// m is the row's maximum) takes exp on f32 pairs (exp_pair, pair_f32.cuh:
-// within about 3 f32 ulps of exp(t)); any other load CUDA's expf.
 template <int T>
-struct SrcExpShift {
+struct SrcExpShift {  // ProgSoftmaxSum<T>: exp(cast(x, f32) + m*(-1)), m indexed by the row
   static constexpr int V = 8;
   struct Row { float nm; };
   __device__ static Row row(const RedArgs& a, uint64_t o) {
@@ -461,13 +439,6 @@ struct SrcExpShift {
   }
   __device__ static void values(const Row& rw, uint4 r, float (&x)[V]) {
     const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-    if (exp_pair_range<T>(w, rw.nm)) {
-      const uint64_t nm2 = pack2(rw.nm, rw.nm);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        unpack2(exp_pair(add2(pack2(widen_lo<T>(w[j]), widen_hi<T>(w[j])), nm2)), x[2 * j], x[2 * j + 1]);
-      return;
-    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       x[2 * j] = expf(__fadd_rn(half_to_f32<T>(w[j] & 0xffffu), rw.nm));
