@@ -163,14 +163,20 @@ cudaError_t red_view_launch(const Program& prog, const RedArgs& a, const ViewSet
 int red_view_occupancy();
 
 // Family S: the three-step softmax plan fused (softmax_kernels.cu).  x and y
-// are [rows, cols] f16/bf16 (16-byte aligned), m and s are [rows] f32.
+// are [rows, cols] f16/bf16 (16-byte aligned), m and s are [rows] f32.  The
+// same row kernel also runs the plan's first two steps on their own (a
+// reduce plan matched to ProgSoftmaxMax / ProgSoftmaxSum): SM_STEP_MAX writes
+// m only, SM_STEP_SUM reads m (m_in) and writes s only.
+enum SoftmaxMode { SM_FUSED = 0, SM_STEP_MAX = 1, SM_STEP_SUM = 2 };
 struct SoftmaxArgs {
   const void* x;
   float* m;
   float* s;
   void* y;
+  const float* m_in;  // SM_STEP_SUM
   uint64_t rows, cols;
   int type;  // kF16 or kBF16
+  int mode;  // SoftmaxMode
 };
 // 16-byte vectors each thread of a row's CTA holds, or 0 when cols has no
 // fused kernel (cols must be a multiple of 256, at most 32768).

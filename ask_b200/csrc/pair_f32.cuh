@@ -13,7 +13,7 @@
 //   exp(t) = 2^hi * 2^lo, hi = RN(t * L) with L = RN(log2 e); the residual
 //   t*L - hi is exact by one fused multiply-add (the FMA two-product of
 //   Ogita, Rump and Oishi, 2005), to which t * (log2 e - L) is added, so
-//   |lo| <= 2^-17 and 2^lo = 1 + lo*ln2 within 2^-35; 2^hi is ex2.approx.f32
+//   |lo| <= 2^-17 and 2^lo = 1 + lo*ln2 within 2^-35; 2^hi is ex2.approx.ftz.f32
 //   (relative error about 2^-22).  The result is a normal f32 within about 3
 //   ulps of exp(t).
 #ifndef ASK_B200_PAIR_F32_CUH
@@ -126,9 +126,12 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
+// 2^a for -100 <= a <= 0 (exp_pair's range): a and 2^a are normal f32 values
+// or zero, so the flush-to-zero form, which skips the subnormal handling of
+// the plain one, computes the same value.
 __device__ __forceinline__ float ex2_approx(float a) {
   float r;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(a));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
   return r;
 }
 

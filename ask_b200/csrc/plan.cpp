@@ -707,6 +707,16 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
                               "softmax_sum_f16", "softmax_sum_bf16"};
   const char* strat_names[] = {"warp_row", "column", "split"};
   pl.kernel = std::string("reduce_") + strat_names[pl.strategy] + "_" + spec_names[pl.spec];
+  // The softmax plan's first two steps (the prologues matched above) run on the
+  // fused softmax's row kernel -- a CTA per row, the next row loaded before this
+  // row's reduction -- when the row length fits it and no strategy is forced.
+  const int sm_vpt = pl.strategy == RS_WARP_ROW && forced.empty() ? softmax_vectors_per_thread(extent) : 0;
+  if (sm_vpt && (pl.spec == RED_SOFTMAX_MAX_F16 || pl.spec == RED_SOFTMAX_MAX_BF16))
+    pl.sm_step = SM_STEP_MAX;
+  else if (sm_vpt && (pl.spec == RED_SOFTMAX_SUM_F16 || pl.spec == RED_SOFTMAX_SUM_BF16))
+    pl.sm_step = SM_STEP_SUM;
+  else
+    pl.sm_step = 0;
   int occ = blocks_per_sm_default(0);
   if (pl.device >= 0) check_cuda(red_occupancy(pl.spec, pl.strategy, &occ), "occupancy");
   if (pl.blocks_per_sm) occ = std::min(occ, pl.blocks_per_sm);
@@ -719,6 +729,14 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   pl.launches = n_outputs ? (pl.strategy == RS_SPLIT ? 2 : 1) : 0;
   pl.scratch = 0;
   pl.col_chunks = 1;
+  if (pl.sm_step) {
+    const bool f16 = pl.spec == RED_SOFTMAX_MAX_F16 || pl.spec == RED_SOFTMAX_SUM_F16;
+    pl.kernel = std::string(pl.sm_step == SM_STEP_MAX ? "softmax_rows_max_" : "softmax_rows_sum_") +
+                (f16 ? "f16" : "bf16");
+    pl.red_grid = pl.grid;
+    pl.block = int(extent / 8 / uint64_t(sm_vpt));
+    pl.grid = int(std::max<uint64_t>(1, std::min<uint64_t>(outer, uint64_t(pl.num_sms) * 8)));
+  }
   if (pl.strategy == RS_COLUMN && n_outputs && extent >= 64) {
     // Too few columns to fill the GPU (2048 threads per SM): split the extent
     // into chunks (grid.y) of at least 32 elements, none empty.
@@ -819,9 +837,10 @@ std::string cuda_lowering(const ask_b200_plan& pl, long pre_copy_input) {
   uint64_t count = pl.outputs.empty() ? 0 : pl.outputs[0].elements;
   if (pl.family == FAM_SCATTER && pl.inputs.size() > 2) count = pl.inputs[2].elements;
   if (softmax) count = pl.sm.rows;
-  uint64_t per_output = warp ? (softmax ? uint64_t(pl.block) : 32) : 1;
+  uint64_t per_output = warp ? (softmax || pl.sm_step ? uint64_t(pl.block) : 32) : 1;
   if (reduce && !pl.views && pl.strategy == RS_SPLIT) per_output = uint64_t(pl.grid) * uint64_t(block);
   const char* strat[] = {"warp_row", "column", "split"};
+  const char* strategy = pl.sm_step ? "row_cta" : pl.views ? "view" : strat[pl.strategy];
   std::ostringstream o;
   o << "{\"statistics_stage\":\"cuda_lowering\",\"kernel_count\":" << pl.launches << ",\"indexing\":\""
     << (warp ? "cooperative_grid_stride" : "linear_grid_stride") << "\",\"warp_reduction_groups\":" << (warp ? 1 : 0)
@@ -833,7 +852,7 @@ std::string cuda_lowering(const ask_b200_plan& pl, long pre_copy_input) {
       << "}";
   o << "],\"bool_storage\":\"one-byte-zero-or-one\",\"cast_semantics\":\"rne-saturating-fptosi-nan-zero-v1\","
     << "\"kernel\":\"" << pl.kernel << "\",\"strategy\":\""
-    << (reduce ? (pl.views ? "view" : strat[pl.strategy]) : kFamilyNames[pl.family]) << "\"";
+    << (reduce ? strategy : kFamilyNames[pl.family]) << "\"";
   if (pl.family == FAM_SCATTER) o << ",\"pre_copy\":{\"input\":" << pre_copy_input << ",\"output\":0}";
   o << "}";
   return o.str();
@@ -844,12 +863,12 @@ std::string describe(const ask_b200_plan& pl) {
   o << "{\"format\":\"ask-b200-recipe\",\"abi_version\":" << ASK_B200_ABI_VERSION << ",\"family\":\""
     << kFamilyNames[pl.family] << "\",\"kernel\":\"" << pl.kernel << "\",\"device\":" << pl.device
     << ",\"target\":{\"backend\":\"cuda\",\"arch\":100},\"launch\":{\"grid\":[" << pl.grid << "," << pl.col_chunks << ",1],\"block\":["
-    << (pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? kRedThreads :
+    << (pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? (pl.sm_step ? pl.block : kRedThreads) :
         pl.family == FAM_SOFTMAX ? pl.block : 256)
     << ",1,1],\"shared_bytes\":0},\"kernels_per_launch\":" << pl.launches << ",\"scratch_bytes\":" << pl.scratch;
   if (pl.family == FAM_REDUCE) {
     const char* strat[] = {"warp_row", "column", "split"};
-    o << ",\"strategy\":\"" << (pl.views ? "view" : strat[pl.strategy]) << "\",\"shardable\":" << (pl.shardable ? "true" : "false")
+    o << ",\"strategy\":\"" << (pl.sm_step ? "row_cta" : pl.views ? "view" : strat[pl.strategy]) << "\",\"shardable\":" << (pl.shardable ? "true" : "false")
       << ",\"outer\":" << pl.red.outer << ",\"extent\":" << pl.red.extent << ",\"inner\":" << pl.red.inner
       << ",\"index_base\":" << pl.red.index_base;
   }
@@ -868,7 +887,8 @@ std::string describe(const ask_b200_plan& pl) {
   for (size_t k = 0; k < pl.outputs.size(); ++k) port(pl.outputs[k], "output", k);
   // The reference artifact's invocation v2 and required element types
   // (lib/Lowering/CUDA.cpp:392-407): arguments are the ports in port order.
-  const int block = pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? kRedThreads
+  const int block = pl.family == FAM_ELEMENTWISE ? kEwThreads
+                    : pl.family == FAM_REDUCE ? (pl.sm_step ? pl.block : kRedThreads)
                     : pl.family == FAM_SOFTMAX ? pl.block : 256;
   o << "],\"invocation\":{\"version\":2,\"kind\":\"ask-b200-recipe\",\"grid\":[" << pl.grid
     << ",1,1],\"block\":[" << block << ",1,1],\"shared_bytes\":0,\"arguments\":[";
@@ -967,7 +987,23 @@ void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratc
                    "reduce launch");
         break;
       }
-      check_cuda(red_launch(pl.spec, pl.strategy, pl.prog, a, aligned ? 1 : 0, pl.grid,
+      if (pl.sm_step && aligned && !rec_out) {
+        SoftmaxArgs sa{};
+        sa.x = a.in[0];
+        sa.rows = a.outer;
+        sa.cols = a.extent;
+        sa.type = pl.inputs[0].dtype;
+        sa.mode = pl.sm_step;
+        if (pl.sm_step == SM_STEP_MAX) {
+          sa.m = static_cast<float*>(a.out[0]);
+        } else {
+          sa.m_in = static_cast<const float*>(a.in[1]);
+          sa.s = static_cast<float*>(a.out[0]);
+        }
+        check_cuda(softmax_rows_launch(sa, pl.num_sms, st), "reduce launch");
+        break;
+      }
+      check_cuda(red_launch(pl.spec, pl.strategy, pl.prog, a, aligned ? 1 : 0, pl.sm_step ? pl.red_grid : pl.grid,
                             reinterpret_cast<void*>(scratch), rec_out, st),
                  "reduce launch");
       break;

@@ -44,5 +44,7 @@ struct ask_b200_plan {
   int block = 256;  // threads per CTA where the family fixes it (softmax)
   int col_chunks = 1;  // RS_COLUMN: chunks of the extent over grid.y (1 = the one-pass column kernel)
   int blocks_per_sm = 0;  // recipe cap on resident CTAs per SM of a persistent grid (0 = occupancy)
+  int sm_step = 0;   // reduce matched to a softmax step run by the softmax row kernel (SoftmaxMode), else 0
+  int red_grid = 1;  // sm_step: the warp-row kernel's grid for a launch whose x is not 16-byte aligned
 };
 

@@ -277,7 +277,8 @@ __device__ __forceinline__ bool fast_all_finite(const FastAcc& s) {
     else
       return true;
   } else if constexpr (needs_probe<R>()) {
-    return isfinite(s.fs);
+    // the probe, including what fast_flush has moved into ds
+    return isfinite(s.ds + double(s.fs));
   } else {
     return true;
   }

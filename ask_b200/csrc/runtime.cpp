@@ -522,9 +522,10 @@ void fuse_softmax(State& st, Program& p) {
     const Step &a = p.steps[i], &b = p.steps[i + 1], &c = p.steps[i + 2];
     std::string dt;
     for (const char* t : {"f16", "bf16"})
-      if (a.kernel == std::string("reduce_warp_row_softmax_max_") + t &&
-          b.kernel == std::string("reduce_warp_row_softmax_sum_") + t && c.kernel == std::string("ew_softmax_norm_") + t)
-        dt = t;
+      for (const char* red : {"reduce_warp_row_softmax_", "softmax_rows_"})
+        if (a.kernel == std::string(red) + "max_" + t && b.kernel == std::string(red) + "sum_" + t &&
+            c.kernel == std::string("ew_softmax_norm_") + t)
+          dt = t;
     if (dt.empty() || a.copy || b.copy || c.copy || a.ports.size() != 2 || b.ports.size() != 3 || c.ports.size() != 4)
       continue;
     const size_t x = a.ports[0], m = a.ports[1], s = b.ports[2], y = c.ports[3];

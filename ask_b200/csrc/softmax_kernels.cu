@@ -39,6 +39,7 @@
 #include "ask_numerics.cuh"
 #include "kernels.h"
 #include "pair_f32.cuh"
+#include "pdl.cuh"
 #include "vec_io.cuh"
 
 namespace askb {
@@ -56,18 +57,26 @@ constexpr int kPreferThreads = ASKB_SOFTMAX_THREADS;  // CTA size the row split 
 // spilling (same-box A/B on cfg3 with the scalar arithmetic: 0.111 ms against
 // 0.123 ms at 4 CTAs per SM); other splits keep the full register budget
 // (VPT == 8 would spill at 64).
-template <int T, int VPT, bool kNarrow>
+//
+// kMode selects what the row kernel computes (SoftmaxMode): SM_FUSED the
+// three steps; SM_STEP_MAX the first step alone (m); SM_STEP_SUM the second
+// alone, s = sum of exp(x + m*(-1)) with m read from m_in (any value: the
+// pair path also checks t <= 0 on the thread's largest element).
+template <int T, int VPT, bool kNarrow, int kMode>
 __global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 1)
     softmax_rows_kernel(const uint4* __restrict__ x, float* __restrict__ m_out, float* __restrict__ s_out,
-                        uint4* __restrict__ y, uint64_t rows, uint32_t vecs) {
+                        uint4* __restrict__ y, const float* __restrict__ m_in, uint64_t rows, uint32_t vecs) {
   __shared__ float red_max[2][kMaxWarps];
   __shared__ double red_sum[2][kMaxWarps];
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  pdl_enter();
   uint64_t row = blockIdx.x;
   uint4 v[VPT];
+  float m_given = 0.0f;  // SM_STEP_SUM: this row's m, loaded with the row
   if (row < rows) {
 #pragma unroll
     for (int q = 0; q < VPT; ++q) v[q] = ld_stream_v4(x + row * vecs + q * blockDim.x + threadIdx.x);
+    if constexpr (kMode == SM_STEP_SUM) m_given = __ldg(m_in + row);
   }
   for (int parity = 0; row < rows; row += gridDim.x, parity ^= 1) {
     uint64_t e[VPT * 4];  // the thread's elements as f32 pairs: x, then t, then exp(t)
@@ -80,30 +89,49 @@ __global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 
       const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        e[q * 4 + j] = pack2(widen_lo<T>(w[j]), widen_hi<T>(w[j]));
+        if constexpr (kMode != SM_STEP_MAX) {
+          e[q * 4 + j] = pack2(widen_lo<T>(w[j]), widen_hi<T>(w[j]));
+          pmin = min2<T>(pmin, w[j]);
+        }
         pmax = max2_nan<T>(pmax, w[j]);
-        pmin = min2<T>(pmin, w[j]);
       }
     }
+    const float m_row = m_given;
     const uint64_t next = row + gridDim.x;
     if (next < rows) {
 #pragma unroll
       for (int q = 0; q < VPT; ++q) v[q] = ld_stream_v4(x + next * vecs + q * blockDim.x + threadIdx.x);
+      if constexpr (kMode == SM_STEP_SUM) m_given = __ldg(m_in + next);
     }
     // max.NaN.f32 of the two halves also turns a NaN into the canonical f32 NaN
     float mx = max_nan(widen_lo<T>(pmax), widen_hi<T>(pmax));
-    const float mn = fminf(widen_lo<T>(pmin), widen_hi<T>(pmin));
+    float m, nm;
+    bool pairs;
+    if constexpr (kMode == SM_STEP_SUM) {
+      // t in [-69, 0] for the thread's smallest and largest values (so for
+      // all), which fails for a NaN or infinite value or m
+      m = m_row;
+      nm = __fmul_rn(m, -1.0f);
+      const float mn = fminf(widen_lo<T>(pmin), widen_hi<T>(pmin));
+      pairs = __fadd_rn(mn, nm) >= -69.0f && __fadd_rn(mx, nm) <= 0.0f;
+    } else {
 #pragma unroll
-    for (int d = 16; d; d >>= 1) mx = max_nan(mx, __shfl_xor_sync(0xffffffffu, mx, d));
-    if (lane == 0) red_max[parity][warp] = mx;
-    __syncthreads();
-    float m = red_max[parity][0];
-    for (uint32_t k = 1; k < nwarps; ++k) m = max_nan(m, red_max[parity][k]);
-    const float nm = __fmul_rn(m, -1.0f);
-    // e = exp(x + m*(-1)), s = sum of e.  t >= -69 for the smallest element
-    // (and so for all, t <= 0 for all) holds only when m and the thread's
-    // values are finite: NaN and infinities take the scalar path.
-    const bool pairs = __fadd_rn(mn, nm) >= -69.0f;
+      for (int d = 16; d; d >>= 1) mx = max_nan(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+      if (lane == 0) red_max[parity][warp] = mx;
+      __syncthreads();
+      m = red_max[parity][0];
+      for (uint32_t k = 1; k < nwarps; ++k) m = max_nan(m, red_max[parity][k]);
+      if constexpr (kMode == SM_STEP_MAX) {
+        if (threadIdx.x == 0) m_out[row] = m;
+        continue;
+      }
+      nm = __fmul_rn(m, -1.0f);
+      // e = exp(x + m*(-1)), s = sum of e.  t >= -69 for the smallest element
+      // (and so for all, t <= 0 for all) holds only when m and the thread's
+      // values are finite: NaN and infinities take the scalar path.
+      const float mn = fminf(widen_lo<T>(pmin), widen_hi<T>(pmin));
+      pairs = __fadd_rn(mn, nm) >= -69.0f;
+    }
     float part;
     if (pairs) {
       const uint64_t nm2 = pack2(nm, nm);
@@ -137,49 +165,61 @@ __global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 
     for (uint32_t k = 0; k < nwarps; ++k) total += red_sum[parity][k];
     const float s = float(total);
     if (threadIdx.x == 0) {
-      m_out[row] = m;
+      if constexpr (kMode == SM_FUSED) m_out[row] = m;
       s_out[row] = s;
     }
-    // y = cast(e / s).  On the pair path y = RN16(e * RN(1/s)): with
-    // 1 <= s <= 2^100 and e >= 2^-100 (normal), every product is a normal f32
-    // within 2 ulps of e / s.  Otherwise the IEEE division.
-    const float r = __frcp_rn(s);
-    const bool by_reciprocal = pairs && s >= 1.0f && s <= 0x1p100f;
-    const uint64_t r2 = pack2(r, r);
+    if constexpr (kMode == SM_FUSED) {
+      // y = cast(e / s).  On the pair path y = RN16(e * RN(1/s)): with
+      // 1 <= s <= 2^100 and e >= 2^-100 (normal), every product is a normal f32
+      // within 2 ulps of e / s.  Otherwise the IEEE division.
+      const float r = __frcp_rn(s);
+      const bool by_reciprocal = pairs && s >= 1.0f && s <= 0x1p100f;
+      const uint64_t r2 = pack2(r, r);
 #pragma unroll
-    for (int qv = 0; qv < VPT; ++qv) {
-      uint32_t o[4];
-      if (by_reciprocal) {
+      for (int qv = 0; qv < VPT; ++qv) {
+        uint32_t o[4];
+        if (by_reciprocal) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float lo, hi;
-          unpack2(mul2(e[qv * 4 + j], r2), lo, hi);
-          o[j] = narrow_two<T>(lo, hi);
+          for (int j = 0; j < 4; ++j) {
+            float lo, hi;
+            unpack2(mul2(e[qv * 4 + j], r2), lo, hi);
+            o[j] = narrow_two<T>(lo, hi);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float lo, hi;
+            unpack2(e[qv * 4 + j], lo, hi);
+            o[j] = narrow_one<T>(__fdiv_rn(lo, s)) | (narrow_one<T>(__fdiv_rn(hi, s)) << 16);
+          }
         }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float lo, hi;
-          unpack2(e[qv * 4 + j], lo, hi);
-          o[j] = narrow_one<T>(__fdiv_rn(lo, s)) | (narrow_one<T>(__fdiv_rn(hi, s)) << 16);
-        }
+        st_stream_v4(y + row * vecs + qv * blockDim.x + threadIdx.x, make_uint4(o[0], o[1], o[2], o[3]));
       }
-      st_stream_v4(y + row * vecs + qv * blockDim.x + threadIdx.x, make_uint4(o[0], o[1], o[2], o[3]));
     }
   }
 }
 
-template <int T, int VPT, bool kNarrow>
-cudaError_t launch_split(const SoftmaxArgs& a, unsigned threads, int sms, cudaStream_t st) {
+template <int T, int VPT, bool kNarrow, int kMode>
+cudaError_t launch_mode(const SoftmaxArgs& a, unsigned threads, int sms, cudaStream_t st) {
   const uint32_t vecs = uint32_t(a.cols / 8);
   int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, softmax_rows_kernel<T, VPT, kNarrow>,
-                                                                int(threads), 0);
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &per_sm, softmax_rows_kernel<T, VPT, kNarrow, kMode>, int(threads), 0);
   if (e != cudaSuccess) return e;
   const uint64_t grid = std::min<uint64_t>(a.rows, uint64_t(sms) * uint64_t(per_sm > 0 ? per_sm : 1));
-  softmax_rows_kernel<T, VPT, kNarrow><<<unsigned(grid), threads, 0, st>>>(
-      static_cast<const uint4*>(a.x), a.m, a.s, static_cast<uint4*>(a.y), a.rows, vecs);
+  (void)launch_pdl(&softmax_rows_kernel<T, VPT, kNarrow, kMode>, dim3(unsigned(grid)), dim3(threads), st,
+                   static_cast<const uint4*>(a.x), a.m, a.s, static_cast<uint4*>(a.y), a.m_in, a.rows, vecs);
   return cudaGetLastError();
+}
+
+template <int T, int VPT, bool kNarrow>
+cudaError_t launch_split(const SoftmaxArgs& a, unsigned threads, int sms, cudaStream_t st) {
+  switch (a.mode) {
+    case SM_FUSED: return launch_mode<T, VPT, kNarrow, SM_FUSED>(a, threads, sms, st);
+    case SM_STEP_MAX: return launch_mode<T, VPT, kNarrow, SM_STEP_MAX>(a, threads, sms, st);
+    case SM_STEP_SUM: return launch_mode<T, VPT, kNarrow, SM_STEP_SUM>(a, threads, sms, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 template <int T, int VPT>

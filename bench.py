@@ -299,9 +299,9 @@ def make_workload(name, rank, world, torch, ask_b200, R, comm, small=False):
         y = torch.empty_like(x)
         w.plans = [ask_b200.Plan(r, rank_device()) for r in R.cfg3_steps(dt, rows, cols)]
         pm, ps, py = w.plans
-        w.kernels = [(f"reduce_warp_row_softmax_max_{dt}", 2 * n + 4 * rows, pm.bind([x], [m], None, st)),
-                     (f"reduce_warp_row_softmax_sum_{dt}", 2 * n + 8 * rows, ps.bind([x, m], [s], None, st)),
-                     (f"ew_softmax_norm_{dt}", 4 * n + 8 * rows, py.bind([x, m, s], [y], None, st))]
+        w.kernels = [(pm.describe()["kernel"], 2 * n + 4 * rows, pm.bind([x], [m], None, st)),
+                     (ps.describe()["kernel"], 2 * n + 8 * rows, ps.bind([x, m], [s], None, st)),
+                     (py.describe()["kernel"], 4 * n + 8 * rows, py.bind([x, m, s], [y], None, st))]
         w.config = dict(static_config(name, world),
                         graded_bytes="each step's port bytes: max 2n + 4*rows, sum 2n + 8*rows, "
                                      "normalise 4n + 8*rows")

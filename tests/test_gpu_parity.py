@@ -253,6 +253,63 @@ def test_fused_softmax_full_size_matches_three_steps(device, dtype):
     assert int(d.max()) <= 1 and float((d != 0).float().mean()) < 1e-3
 
 
+def _rows_with_specials(dtype, rows, cols, seed):
+    """[rows, cols] 16-bit softmax input (bits), N(0, 3), with a NaN row, an
+    infinite element, an all -inf row, an all -0 row, a huge spread and rows
+    whose maximum is -0 and +0 in either order."""
+    x = gen_dev(2 if dtype == "f16" else 3, 0xA5C3, seed, rows * cols, 0.0, 3.0, torch.int16)
+    xh = x.cpu().numpy().view(np.uint16).copy()
+    nan16, inf16, ninf16 = (0x7E00, 0x7C00, 0xFC00) if dtype == "f16" else (0x7FC0, 0x7F80, 0xFF80)
+    xh[5] = nan16
+    xh[min(1, rows - 1) * cols + 3] = inf16
+    if rows > 6:
+        xh[2 * cols:3 * cols] = ninf16
+        xh[3 * cols:4 * cols] = 0x8000
+        xh[4 * cols] = 0x7BFF if dtype == "f16" else 0x7F7F
+        xh[5 * cols:7 * cols] = 0xBC00 if dtype == "f16" else 0xBF80
+        xh[5 * cols + 3], xh[5 * cols + 9] = 0x8000, 0x0000
+        xh[6 * cols + 3], xh[6 * cols + 9] = 0x0000, 0x8000
+    return xh
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("rows,cols", [(300, 4096), (37, 1024), (5, 16384), (130, 2304), (9, 256)])
+def test_softmax_steps_on_the_row_kernel(device, dtype, rows, cols):
+    """The plan's max and sum steps run on the softmax row kernel (a CTA per
+    row): m bit-exact and s within 2^-20 of the oracle, and m bit-identical to
+    the same steps forced onto the warp-row reduction.  An x that is not
+    16-byte aligned takes the warp-row kernel at launch, with the same m."""
+    xh = _rows_with_specials(dtype, rows, cols, 9)
+    steps = R.cfg3_steps(dtype, rows, cols)[:2]
+    row_plans = [ask_b200.Plan(s, 0) for s in steps]
+    assert [p.describe()["kernel"] for p in row_plans] == [f"softmax_rows_max_{dtype}", f"softmax_rows_sum_{dtype}"]
+    warp_plans = [ask_b200.Plan(dict(s, strategy="warp_row"), 0) for s in steps]
+    buf = torch.empty(rows * cols + 8, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def run(plans, x):
+        m = torch.empty(rows, dtype=torch.float32, device="cuda")
+        s = torch.empty(rows, dtype=torch.float32, device="cuda")
+        plans[0].launch([x], [m], None, st)
+        plans[1].launch([x, m], [s], None, st)
+        torch.cuda.synchronize()
+        return m.cpu().numpy(), s.cpu().numpy()
+
+    x = torch.from_numpy(xh.view(np.int16)).cuda()
+    rm, rs, _ = oracle.softmax(dtype, xh, rows, cols, threads=THREADS)
+    m_row, s_row = run(row_plans, x)
+    m_warp, _ = run(warp_plans, x)
+    buf[1:1 + rows * cols].copy_(x)  # a 2-byte offset: not 16-byte aligned
+    m_off, s_off = run(row_plans, buf[1:1 + rows * cols])
+    for m, s in ((m_row, s_row), (m_off, s_off)):
+        assert same_with_nan(m, rm)
+        assert np.array_equal(np.isnan(s), np.isnan(rs))
+        fin = np.isfinite(rs)
+        assert np.array_equal(s[~fin & ~np.isnan(rs)], rs[~fin & ~np.isnan(rs)].astype(np.float32))
+        assert np.all(np.abs(s[fin].astype(np.float64) - rs[fin]) <= 2.0 ** -20 * np.abs(rs[fin]))
+    assert same_with_nan(m_row, m_warp)
+
+
 def _rn16(q32: np.ndarray, dtype: str) -> np.ndarray:
     """f32 -> f16/bf16 bits, round to nearest even (NaN -> a quiet NaN)."""
     if dtype == "f16":
