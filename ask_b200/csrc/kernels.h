@@ -164,16 +164,18 @@ int red_view_occupancy();
 
 // Family S: the three-step softmax plan fused (softmax_kernels.cu).  x and y
 // are [rows, cols] f16/bf16 (16-byte aligned), m and s are [rows] f32.  The
-// same row kernel also runs the plan's first two steps on their own (a
-// reduce plan matched to ProgSoftmaxMax / ProgSoftmaxSum): SM_STEP_MAX writes
-// m only, SM_STEP_SUM reads m (m_in) and writes s only.
-enum SoftmaxMode { SM_FUSED = 0, SM_STEP_MAX = 1, SM_STEP_SUM = 2 };
+// same row kernel also runs each step of the plan on its own (a reduce plan
+// matched to ProgSoftmaxMax / ProgSoftmaxSum, an elementwise plan matched to
+// ProgSoftmaxNorm): SM_STEP_MAX writes m only, SM_STEP_SUM reads m (m_in) and
+// writes s only, SM_STEP_NORM reads m and s (m_in, s_in) and writes y only.
+enum SoftmaxMode { SM_FUSED = 0, SM_STEP_MAX = 1, SM_STEP_SUM = 2, SM_STEP_NORM = 3 };
 struct SoftmaxArgs {
   const void* x;
   float* m;
   float* s;
   void* y;
-  const float* m_in;  // SM_STEP_SUM
+  const float* m_in;  // SM_STEP_SUM, SM_STEP_NORM
+  const float* s_in;  // SM_STEP_NORM
   uint64_t rows, cols;
   int type;  // kF16 or kBF16
   int mode;  // SoftmaxMode

@@ -462,6 +462,20 @@ void finish_elementwise(ask_b200_plan& pl) {
   const uint64_t cap = uint64_t(std::max(occ, 1)) * uint64_t(pl.num_sms);
   pl.grid = int(std::max<uint64_t>(1, std::min(needed, cap)));
   pl.launches = pl.count ? 1 : 0;
+  // The softmax plan's normalise step runs on the fused softmax's row kernel
+  // (m, s and RN(1/s) once per row, no per-unit row division) when its rows
+  // fit it and no grid cap is requested.
+  pl.sm_step = 0;
+  const bool norm = pl.spec == EW_SOFTMAX_NORM_F16 || pl.spec == EW_SOFTMAX_NORM_BF16;
+  const int vpt = norm && !pl.blocks_per_sm && pl.inner && pl.count % pl.inner == 0
+                      ? softmax_vectors_per_thread(pl.inner) : 0;
+  if (vpt) {
+    pl.sm_step = SM_STEP_NORM;
+    pl.kernel = pl.spec == EW_SOFTMAX_NORM_F16 ? "softmax_rows_norm_f16" : "softmax_rows_norm_bf16";
+    pl.red_grid = pl.grid;
+    pl.block = int(pl.inner / 8 / uint64_t(vpt));
+    pl.grid = int(std::max<uint64_t>(1, std::min<uint64_t>(pl.count / pl.inner, uint64_t(pl.num_sms) * 8)));
+  }
 }
 
 void parse_ports(const json::Value& r, const char* key, bool with_map, std::vector<int>& types, std::vector<int>& maps) {
@@ -710,7 +724,8 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
   // The softmax plan's first two steps (the prologues matched above) run on the
   // fused softmax's row kernel -- a CTA per row, the next row loaded before this
   // row's reduction -- when the row length fits it and no strategy is forced.
-  const int sm_vpt = pl.strategy == RS_WARP_ROW && forced.empty() ? softmax_vectors_per_thread(extent) : 0;
+  const int sm_vpt =
+      pl.strategy == RS_WARP_ROW && forced.empty() && !pl.blocks_per_sm ? softmax_vectors_per_thread(extent) : 0;
   if (sm_vpt && (pl.spec == RED_SOFTMAX_MAX_F16 || pl.spec == RED_SOFTMAX_MAX_BF16))
     pl.sm_step = SM_STEP_MAX;
   else if (sm_vpt && (pl.spec == RED_SOFTMAX_SUM_F16 || pl.spec == RED_SOFTMAX_SUM_BF16))
@@ -827,7 +842,8 @@ void build_softmax(ask_b200_plan& pl, const json::Value& r) {
 std::string cuda_lowering(const ask_b200_plan& pl, long pre_copy_input) {
   const bool reduce = pl.family == FAM_REDUCE, softmax = pl.family == FAM_SOFTMAX;
   const bool warp = (reduce && !pl.views && pl.strategy == RS_WARP_ROW) || softmax;
-  const int block = pl.family == FAM_ELEMENTWISE ? kEwThreads : reduce ? kRedThreads : softmax ? pl.block : 256;
+  const int block = pl.sm_step ? pl.block : pl.family == FAM_ELEMENTWISE ? kEwThreads : reduce ? kRedThreads
+                  : softmax ? pl.block : 256;
   size_t empty = 0;
   std::ostringstream outs;
   for (size_t k = 0; k < pl.outputs.size(); ++k) {
@@ -863,7 +879,7 @@ std::string describe(const ask_b200_plan& pl) {
   o << "{\"format\":\"ask-b200-recipe\",\"abi_version\":" << ASK_B200_ABI_VERSION << ",\"family\":\""
     << kFamilyNames[pl.family] << "\",\"kernel\":\"" << pl.kernel << "\",\"device\":" << pl.device
     << ",\"target\":{\"backend\":\"cuda\",\"arch\":100},\"launch\":{\"grid\":[" << pl.grid << "," << pl.col_chunks << ",1],\"block\":["
-    << (pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? (pl.sm_step ? pl.block : kRedThreads) :
+    << (pl.sm_step ? pl.block : pl.family == FAM_ELEMENTWISE ? kEwThreads : pl.family == FAM_REDUCE ? kRedThreads :
         pl.family == FAM_SOFTMAX ? pl.block : 256)
     << ",1,1],\"shared_bytes\":0},\"kernels_per_launch\":" << pl.launches << ",\"scratch_bytes\":" << pl.scratch;
   if (pl.family == FAM_REDUCE) {
@@ -887,8 +903,8 @@ std::string describe(const ask_b200_plan& pl) {
   for (size_t k = 0; k < pl.outputs.size(); ++k) port(pl.outputs[k], "output", k);
   // The reference artifact's invocation v2 and required element types
   // (lib/Lowering/CUDA.cpp:392-407): arguments are the ports in port order.
-  const int block = pl.family == FAM_ELEMENTWISE ? kEwThreads
-                    : pl.family == FAM_REDUCE ? (pl.sm_step ? pl.block : kRedThreads)
+  const int block = pl.sm_step ? pl.block : pl.family == FAM_ELEMENTWISE ? kEwThreads
+                    : pl.family == FAM_REDUCE ? kRedThreads
                     : pl.family == FAM_SOFTMAX ? pl.block : 256;
   o << "],\"invocation\":{\"version\":2,\"kind\":\"ask-b200-recipe\",\"grid\":[" << pl.grid
     << ",1,1],\"block\":[" << block << ",1,1],\"shared_bytes\":0,\"arguments\":[";
@@ -958,7 +974,21 @@ void launch_plan(const ask_b200_plan& pl, const uint64_t* ports, uint64_t scratc
       }
       a.count = pl.count;
       a.inner = make_u32div(pl.inner ? pl.inner : 1, pl.count);
-      check_cuda(ew_launch(pl.spec, pl.prog, a, aligned ? 1 : 0, pl.grid, st), "elementwise launch");
+      if (pl.sm_step && aligned) {
+        SoftmaxArgs sa{};
+        sa.x = a.in[0];
+        sa.m_in = static_cast<const float*>(a.in[1]);
+        sa.s_in = static_cast<const float*>(a.in[2]);
+        sa.y = a.out[0];
+        sa.rows = pl.count / pl.inner;
+        sa.cols = pl.inner;
+        sa.type = pl.inputs[0].dtype;
+        sa.mode = SM_STEP_NORM;
+        check_cuda(softmax_rows_launch(sa, pl.num_sms, st), "elementwise launch");
+        break;
+      }
+      check_cuda(ew_launch(pl.spec, pl.prog, a, aligned ? 1 : 0, pl.sm_step ? pl.red_grid : pl.grid, st),
+                 "elementwise launch");
       break;
     }
     case FAM_REDUCE: {

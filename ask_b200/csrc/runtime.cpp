@@ -523,9 +523,10 @@ void fuse_softmax(State& st, Program& p) {
     std::string dt;
     for (const char* t : {"f16", "bf16"})
       for (const char* red : {"reduce_warp_row_softmax_", "softmax_rows_"})
-        if (a.kernel == std::string(red) + "max_" + t && b.kernel == std::string(red) + "sum_" + t &&
-            c.kernel == std::string("ew_softmax_norm_") + t)
-          dt = t;
+        for (const char* ew : {"ew_softmax_norm_", "softmax_rows_norm_"})
+          if (a.kernel == std::string(red) + "max_" + t && b.kernel == std::string(red) + "sum_" + t &&
+              c.kernel == std::string(ew) + t)
+            dt = t;
     if (dt.empty() || a.copy || b.copy || c.copy || a.ports.size() != 2 || b.ports.size() != 3 || c.ports.size() != 4)
       continue;
     const size_t x = a.ports[0], m = a.ports[1], s = b.ports[2], y = c.ports[3];

@@ -61,22 +61,29 @@ constexpr int kPreferThreads = ASKB_SOFTMAX_THREADS;  // CTA size the row split 
 // kMode selects what the row kernel computes (SoftmaxMode): SM_FUSED the
 // three steps; SM_STEP_MAX the first step alone (m); SM_STEP_SUM the second
 // alone, s = sum of exp(x + m*(-1)) with m read from m_in (any value: the
-// pair path also checks t <= 0 on the thread's largest element).
+// pair path also checks t <= 0 on the thread's largest element);
+// SM_STEP_NORM the third alone, y = cast(exp(x + m*(-1)) / s) with m and s
+// read from m_in and s_in (pairs also need 2^-100 <= s <= 2^24, so that
+// every product e * RN(1/s) is a normal f32; otherwise expf and the IEEE
+// division, the normalise step's own scalar arithmetic).
 template <int T, int VPT, bool kNarrow, int kMode>
 __global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 1)
     softmax_rows_kernel(const uint4* __restrict__ x, float* __restrict__ m_out, float* __restrict__ s_out,
-                        uint4* __restrict__ y, const float* __restrict__ m_in, uint64_t rows, uint32_t vecs) {
+                        uint4* __restrict__ y, const float* __restrict__ m_in, const float* __restrict__ s_in,
+                        uint64_t rows, uint32_t vecs) {
+  constexpr bool kGivenM = kMode == SM_STEP_SUM || kMode == SM_STEP_NORM;
   __shared__ float red_max[2][kMaxWarps];
   __shared__ double red_sum[2][kMaxWarps];
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   pdl_enter();
   uint64_t row = blockIdx.x;
   uint4 v[VPT];
-  float m_given = 0.0f;  // SM_STEP_SUM: this row's m, loaded with the row
+  float m_given = 0.0f, s_given = 0.0f;  // SM_STEP_SUM / SM_STEP_NORM: this row's m (and s), loaded with the row
   if (row < rows) {
 #pragma unroll
     for (int q = 0; q < VPT; ++q) v[q] = ld_stream_v4(x + row * vecs + q * blockDim.x + threadIdx.x);
-    if constexpr (kMode == SM_STEP_SUM) m_given = __ldg(m_in + row);
+    if constexpr (kGivenM) m_given = __ldg(m_in + row);
+    if constexpr (kMode == SM_STEP_NORM) s_given = __ldg(s_in + row);
   }
   for (int parity = 0; row < rows; row += gridDim.x, parity ^= 1) {
     uint64_t e[VPT * 4];  // the thread's elements as f32 pairs: x, then t, then exp(t)
@@ -96,24 +103,26 @@ __global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 
         pmax = max2_nan<T>(pmax, w[j]);
       }
     }
-    const float m_row = m_given;
+    const float m_row = m_given, s_row = s_given;
     const uint64_t next = row + gridDim.x;
     if (next < rows) {
 #pragma unroll
       for (int q = 0; q < VPT; ++q) v[q] = ld_stream_v4(x + next * vecs + q * blockDim.x + threadIdx.x);
-      if constexpr (kMode == SM_STEP_SUM) m_given = __ldg(m_in + next);
+      if constexpr (kGivenM) m_given = __ldg(m_in + next);
+      if constexpr (kMode == SM_STEP_NORM) s_given = __ldg(s_in + next);
     }
     // max.NaN.f32 of the two halves also turns a NaN into the canonical f32 NaN
     float mx = max_nan(widen_lo<T>(pmax), widen_hi<T>(pmax));
     float m, nm;
     bool pairs;
-    if constexpr (kMode == SM_STEP_SUM) {
+    if constexpr (kGivenM) {
       // t in [-69, 0] for the thread's smallest and largest values (so for
       // all), which fails for a NaN or infinite value or m
       m = m_row;
       nm = __fmul_rn(m, -1.0f);
       const float mn = fminf(widen_lo<T>(pmin), widen_hi<T>(pmin));
       pairs = __fadd_rn(mn, nm) >= -69.0f && __fadd_rn(mx, nm) <= 0.0f;
+      if constexpr (kMode == SM_STEP_NORM) pairs = pairs && s_row >= 0x1p-100f && s_row <= 0x1p24f;
     } else {
 #pragma unroll
       for (int d = 16; d; d >>= 1) mx = max_nan(mx, __shfl_xor_sync(0xffffffffu, mx, d));
@@ -156,24 +165,30 @@ __global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 
         e[k] = pack2(lo, hi);
       }
     }
-    double ps = double(part);
+    float s;
+    if constexpr (kMode == SM_STEP_NORM) {
+      s = s_row;
+    } else {
+      double ps = double(part);
 #pragma unroll
-    for (int d = 16; d; d >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, d);
-    if (lane == 0) red_sum[parity][warp] = ps;
-    __syncthreads();
-    double total = 0.0;
-    for (uint32_t k = 0; k < nwarps; ++k) total += red_sum[parity][k];
-    const float s = float(total);
-    if (threadIdx.x == 0) {
-      if constexpr (kMode == SM_FUSED) m_out[row] = m;
-      s_out[row] = s;
+      for (int d = 16; d; d >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, d);
+      if (lane == 0) red_sum[parity][warp] = ps;
+      __syncthreads();
+      double total = 0.0;
+      for (uint32_t k = 0; k < nwarps; ++k) total += red_sum[parity][k];
+      s = float(total);
+      if (threadIdx.x == 0) {
+        if constexpr (kMode == SM_FUSED) m_out[row] = m;
+        s_out[row] = s;
+      }
     }
-    if constexpr (kMode == SM_FUSED) {
-      // y = cast(e / s).  On the pair path y = RN16(e * RN(1/s)): with
-      // 1 <= s <= 2^100 and e >= 2^-100 (normal), every product is a normal f32
+    if constexpr (kMode == SM_FUSED || kMode == SM_STEP_NORM) {
+      // y = cast(e / s).  On the pair path y = RN16(e * RN(1/s)): with e >=
+      // 2^-100 and 1 <= s <= 2^100 (the fused kernel: s counts exp(0) = 1)
+      // or 2^-100 <= s <= 2^24 (checked), every product is a normal f32
       // within 2 ulps of e / s.  Otherwise the IEEE division.
       const float r = __frcp_rn(s);
-      const bool by_reciprocal = pairs && s >= 1.0f && s <= 0x1p100f;
+      const bool by_reciprocal = kMode == SM_STEP_NORM ? pairs : pairs && s >= 1.0f && s <= 0x1p100f;
       const uint64_t r2 = pack2(r, r);
 #pragma unroll
       for (int qv = 0; qv < VPT; ++qv) {
@@ -208,7 +223,8 @@ cudaError_t launch_mode(const SoftmaxArgs& a, unsigned threads, int sms, cudaStr
   if (e != cudaSuccess) return e;
   const uint64_t grid = std::min<uint64_t>(a.rows, uint64_t(sms) * uint64_t(per_sm > 0 ? per_sm : 1));
   (void)launch_pdl(&softmax_rows_kernel<T, VPT, kNarrow, kMode>, dim3(unsigned(grid)), dim3(threads), st,
-                   static_cast<const uint4*>(a.x), a.m, a.s, static_cast<uint4*>(a.y), a.m_in, a.rows, vecs);
+                   static_cast<const uint4*>(a.x), a.m, a.s, static_cast<uint4*>(a.y), a.m_in, a.s_in, a.rows,
+                   vecs);
   return cudaGetLastError();
 }
 
@@ -218,6 +234,7 @@ cudaError_t launch_split(const SoftmaxArgs& a, unsigned threads, int sms, cudaSt
     case SM_FUSED: return launch_mode<T, VPT, kNarrow, SM_FUSED>(a, threads, sms, st);
     case SM_STEP_MAX: return launch_mode<T, VPT, kNarrow, SM_STEP_MAX>(a, threads, sms, st);
     case SM_STEP_SUM: return launch_mode<T, VPT, kNarrow, SM_STEP_SUM>(a, threads, sms, st);
+    case SM_STEP_NORM: return launch_mode<T, VPT, kNarrow, SM_STEP_NORM>(a, threads, sms, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -81,15 +81,18 @@ def test_config_recipes_select_specialised_kernels(name, recipe, kernel):
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 def test_softmax_partition_steps(dtype):
     kernels = [host_plan(s).describe()["kernel"] for s in R.cfg3_steps(dtype)]
-    assert kernels == [f"softmax_rows_max_{dtype}", f"softmax_rows_sum_{dtype}", f"ew_softmax_norm_{dtype}"]
+    assert kernels == [f"softmax_rows_max_{dtype}", f"softmax_rows_sum_{dtype}", f"softmax_rows_norm_{dtype}"]
+    capped = dict(R.cfg3_steps(dtype)[2], blocks_per_sm=4)  # a grid cap keeps the elementwise functor
+    assert host_plan(capped).describe()["kernel"] == f"ew_softmax_norm_{dtype}"
     d = host_plan(R.cfg3_steps(dtype)[1]).describe()
     assert d["strategy"] == "row_cta" and d["launch"]["block"] == [128, 1, 1]
     # a forced strategy, or rows the row kernel does not take, keep the warp-row reduction
     forced = [dict(s, strategy="warp_row") for s in R.cfg3_steps(dtype)[:2]]
     assert [host_plan(s).describe()["kernel"] for s in forced] == [
         f"reduce_warp_row_softmax_max_{dtype}", f"reduce_warp_row_softmax_sum_{dtype}"]
-    odd = [host_plan(s).describe()["kernel"] for s in R.cfg3_steps(dtype, 64, 1000)[:2]]
-    assert odd == [f"reduce_warp_row_softmax_max_{dtype}", f"reduce_warp_row_softmax_sum_{dtype}"]
+    odd = [host_plan(s).describe()["kernel"] for s in R.cfg3_steps(dtype, 64, 1000)]
+    assert odd == [f"reduce_warp_row_softmax_max_{dtype}", f"reduce_warp_row_softmax_sum_{dtype}",
+                   f"ew_softmax_norm_{dtype}"]
 
 
 def test_port_map_orders_inputs_then_outputs():

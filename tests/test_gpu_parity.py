@@ -275,38 +275,40 @@ def _rows_with_specials(dtype, rows, cols, seed):
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("rows,cols", [(300, 4096), (37, 1024), (5, 16384), (130, 2304), (9, 256)])
 def test_softmax_steps_on_the_row_kernel(device, dtype, rows, cols):
-    """The plan's max and sum steps run on the softmax row kernel (a CTA per
-    row): m bit-exact and s within 2^-20 of the oracle, and m bit-identical to
-    the same steps forced onto the warp-row reduction.  An x that is not
-    16-byte aligned takes the warp-row kernel at launch, with the same m."""
+    """The plan's three steps run on the softmax row kernel (a CTA per row):
+    m bit-exact, s within 2^-20 and y within one 16-bit ulp of the oracle; m
+    bit-identical to the max step forced onto the warp-row reduction.  An x
+    that is not 16-byte aligned takes the warp-row reduction and the
+    elementwise functor at launch, with the same m; a grid cap keeps the
+    normalise on the functor."""
     xh = _rows_with_specials(dtype, rows, cols, 9)
-    steps = R.cfg3_steps(dtype, rows, cols)[:2]
+    steps = R.cfg3_steps(dtype, rows, cols)
     row_plans = [ask_b200.Plan(s, 0) for s in steps]
-    assert [p.describe()["kernel"] for p in row_plans] == [f"softmax_rows_max_{dtype}", f"softmax_rows_sum_{dtype}"]
-    warp_plans = [ask_b200.Plan(dict(s, strategy="warp_row"), 0) for s in steps]
+    assert [p.describe()["kernel"] for p in row_plans] == [f"softmax_rows_max_{dtype}", f"softmax_rows_sum_{dtype}",
+                                                           f"softmax_rows_norm_{dtype}"]
+    warp_plans = [ask_b200.Plan(dict(s, strategy="warp_row"), 0) for s in steps[:2]]
+    norm_functor = ask_b200.Plan(dict(steps[2], blocks_per_sm=8), 0)
+    assert norm_functor.describe()["kernel"] == f"ew_softmax_norm_{dtype}"
     buf = torch.empty(rows * cols + 8, dtype=torch.int16, device="cuda")
     st = torch.cuda.current_stream()
 
-    def run(plans, x):
+    def run(plans, x, norm, y_out):
         m = torch.empty(rows, dtype=torch.float32, device="cuda")
         s = torch.empty(rows, dtype=torch.float32, device="cuda")
         plans[0].launch([x], [m], None, st)
         plans[1].launch([x, m], [s], None, st)
+        norm.launch([x, m, s], [y_out], None, st)
         torch.cuda.synchronize()
-        return m.cpu().numpy(), s.cpu().numpy()
+        return m.cpu().numpy(), s.cpu().numpy(), y_out.cpu().numpy().view(np.uint16).copy()
 
     x = torch.from_numpy(xh.view(np.int16)).cuda()
-    rm, rs, _ = oracle.softmax(dtype, xh, rows, cols, threads=THREADS)
-    m_row, s_row = run(row_plans, x)
-    m_warp, _ = run(warp_plans, x)
+    m_row, s_row, y_row = run(row_plans, x, row_plans[2], torch.empty_like(x))
+    m_warp, s_warp, y_functor = run(warp_plans, x, norm_functor, torch.empty_like(x))
     buf[1:1 + rows * cols].copy_(x)  # a 2-byte offset: not 16-byte aligned
-    m_off, s_off = run(row_plans, buf[1:1 + rows * cols])
-    for m, s in ((m_row, s_row), (m_off, s_off)):
-        assert same_with_nan(m, rm)
-        assert np.array_equal(np.isnan(s), np.isnan(rs))
-        fin = np.isfinite(rs)
-        assert np.array_equal(s[~fin & ~np.isnan(rs)], rs[~fin & ~np.isnan(rs)].astype(np.float32))
-        assert np.all(np.abs(s[fin].astype(np.float64) - rs[fin]) <= 2.0 ** -20 * np.abs(rs[fin]))
+    ybuf = torch.empty(rows * cols + 8, dtype=torch.int16, device="cuda")
+    m_off, s_off, y_off = run(row_plans, buf[1:1 + rows * cols], row_plans[2], ybuf[1:1 + rows * cols])
+    for m, s, y in ((m_row, s_row, y_row), (m_off, s_off, y_off), (m_warp, s_warp, y_functor)):
+        _softmax_check(dtype, xh, rows, cols, m, s, y)
     assert same_with_nan(m_row, m_warp)
 
 

@@ -647,7 +647,7 @@ def test_report_lowers_to_a_program():
     assert prog["inputs"] == [0] and prog["outputs"] == [3]
     assert [s["inputs"] for s in prog["steps"]] == [[0], [0, 1], [0, 1, 2]]
     assert [kernel_of(json.loads(s["recipe"])) for s in prog["steps"]] == [
-        "softmax_rows_max_f16", "softmax_rows_sum_f16", "ew_softmax_norm_f16"]
+        "softmax_rows_max_f16", "softmax_rows_sum_f16", "softmax_rows_norm_f16"]
     prog = rt.lower_report(scatter_report(1 << 20, 256, 1 << 23))
     assert [s["inputs"] for s in prog["steps"]] == [[0, 1], [2, 1, 3]]
 

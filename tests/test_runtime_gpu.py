@@ -214,7 +214,7 @@ def test_softmax_program_matches_direct_steps(device, graph, fuse, dtype):
         assert session.stats()["fused_softmax_steps"] == 1
     else:
         assert [k["kernel"] for k in d["steps"]] == [f"softmax_rows_max_{dtype}",
-                                                     f"softmax_rows_sum_{dtype}", f"ew_softmax_norm_{dtype}"]
+                                                     f"softmax_rows_sum_{dtype}", f"softmax_rows_norm_{dtype}"]
     xin = session.importTensor(x, readonly=True)
     outs = [torch.empty_like(m), torch.empty_like(s), torch.empty_like(y_ref)]
     bufs = [session.importTensor(t) for t in outs]
