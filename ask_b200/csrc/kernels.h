@@ -184,6 +184,9 @@ struct SoftmaxArgs {
 // fused kernel (cols must be a multiple of 256, at most 32768).
 int softmax_vectors_per_thread(uint64_t cols);
 cudaError_t softmax_rows_launch(const SoftmaxArgs& a, int sms, cudaStream_t stream);
+// The grid softmax_rows_launch uses for `a` (SMs x resident CTAs, at most
+// one CTA per row); needs the device current.
+int softmax_rows_grid(const SoftmaxArgs& a, int sms);
 
 cudaError_t gen_launch(int kind, uint64_t seed, uint32_t stream_id, uint64_t offset, uint64_t count, double p0,
                        double p1, const double* zipf_cdf, uint64_t zipf_n, void* dst, cudaStream_t stream);

@@ -435,6 +435,14 @@ constexpr int kMaxRanks = 64;
 
 int blocks_per_sm_default(int) { return 8; }
 
+// The grid of a softmax row-kernel launch: the launcher's own (SMs x resident
+// CTAs of the instance, a CTA per row at most) when the plan has a device,
+// else 8 CTAs per SM.
+int softmax_grid(const ask_b200_plan& pl, const SoftmaxArgs& a) {
+  if (pl.device >= 0) return softmax_rows_grid(a, pl.num_sms);
+  return int(std::max<uint64_t>(1, std::min<uint64_t>(a.rows, uint64_t(pl.num_sms) * 8)));
+}
+
 void finish_elementwise(ask_b200_plan& pl) {
   // Specialisation lookup on the canonical SSA form.
   pl.spec = EW_GENERIC;
@@ -474,7 +482,12 @@ void finish_elementwise(ask_b200_plan& pl) {
     pl.kernel = pl.spec == EW_SOFTMAX_NORM_F16 ? "softmax_rows_norm_f16" : "softmax_rows_norm_bf16";
     pl.red_grid = pl.grid;
     pl.block = int(pl.inner / 8 / uint64_t(vpt));
-    pl.grid = int(std::max<uint64_t>(1, std::min<uint64_t>(pl.count / pl.inner, uint64_t(pl.num_sms) * 8)));
+    SoftmaxArgs sa{};
+    sa.rows = pl.count / pl.inner;
+    sa.cols = pl.inner;
+    sa.type = pl.inputs[0].dtype;
+    sa.mode = SM_STEP_NORM;
+    pl.grid = softmax_grid(pl, sa);
   }
 }
 
@@ -750,7 +763,12 @@ void build_reduce(ask_b200_plan& pl, const json::Value& r) {
                 (f16 ? "f16" : "bf16");
     pl.red_grid = pl.grid;
     pl.block = int(extent / 8 / uint64_t(sm_vpt));
-    pl.grid = int(std::max<uint64_t>(1, std::min<uint64_t>(outer, uint64_t(pl.num_sms) * 8)));
+    SoftmaxArgs sa{};
+    sa.rows = outer;
+    sa.cols = extent;
+    sa.type = pl.inputs[0].dtype;
+    sa.mode = pl.sm_step;
+    pl.grid = softmax_grid(pl, sa);
   }
   if (pl.strategy == RS_COLUMN && n_outputs && extent >= 64) {
     // Too few columns to fill the GPU (2048 threads per SM): split the extent
@@ -827,7 +845,7 @@ void build_softmax(ask_b200_plan& pl, const json::Value& r) {
   pl.outputs = {{kF32, a.rows, IM_FULL}, {kF32, a.rows, IM_FULL}, {a.type, n, IM_FULL}};
   pl.kernel = a.type == kF16 ? "softmax_rows_f16" : "softmax_rows_bf16";
   pl.launches = a.rows ? 1 : 0;
-  pl.grid = int(std::min<uint64_t>(a.rows ? a.rows : 1, uint64_t(pl.num_sms) * 4));
+  pl.grid = softmax_grid(pl, a);
   pl.block = int(a.cols / 8 / uint64_t(vpt));
 }
 

@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "ask_numerics.cuh"
 #include "kernels.h"
@@ -214,14 +215,35 @@ __global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 
   }
 }
 
+// Resident CTAs per SM of one instance for a CTA size (threads / 32 <=
+// kMaxWarps), queried once: the same on every B200.
 template <int T, int VPT, bool kNarrow, int kMode>
-cudaError_t launch_mode(const SoftmaxArgs& a, unsigned threads, int sms, cudaStream_t st) {
+cudaError_t resident_ctas(unsigned threads, int* per_sm) {
+  static std::atomic<int> cache[kMaxWarps + 1];
+  int n = cache[threads / 32].load(std::memory_order_relaxed);
+  if (n == 0) {
+    const cudaError_t e =
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, softmax_rows_kernel<T, VPT, kNarrow, kMode>, int(threads), 0);
+    if (e != cudaSuccess) return e;
+    n = std::max(n, 1);
+    cache[threads / 32].store(n, std::memory_order_relaxed);
+  }
+  *per_sm = n;
+  return cudaSuccess;
+}
+
+// Launch on `st`, or with grid_out set only report the grid a launch uses.
+template <int T, int VPT, bool kNarrow, int kMode>
+cudaError_t launch_mode(const SoftmaxArgs& a, unsigned threads, int sms, cudaStream_t st, int* grid_out) {
   const uint32_t vecs = uint32_t(a.cols / 8);
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      &per_sm, softmax_rows_kernel<T, VPT, kNarrow, kMode>, int(threads), 0);
+  int per_sm = 1;
+  const cudaError_t e = resident_ctas<T, VPT, kNarrow, kMode>(threads, &per_sm);
   if (e != cudaSuccess) return e;
-  const uint64_t grid = std::min<uint64_t>(a.rows, uint64_t(sms) * uint64_t(per_sm > 0 ? per_sm : 1));
+  const uint64_t grid = std::min<uint64_t>(a.rows, uint64_t(sms) * uint64_t(per_sm));
+  if (grid_out) {
+    *grid_out = int(grid);
+    return cudaSuccess;
+  }
   (void)launch_pdl(&softmax_rows_kernel<T, VPT, kNarrow, kMode>, dim3(unsigned(grid)), dim3(threads), st,
                    static_cast<const uint4*>(a.x), a.m, a.s, static_cast<uint4*>(a.y), a.m_in, a.s_in, a.rows,
                    vecs);
@@ -229,32 +251,32 @@ cudaError_t launch_mode(const SoftmaxArgs& a, unsigned threads, int sms, cudaStr
 }
 
 template <int T, int VPT, bool kNarrow>
-cudaError_t launch_split(const SoftmaxArgs& a, unsigned threads, int sms, cudaStream_t st) {
+cudaError_t launch_split(const SoftmaxArgs& a, unsigned threads, int sms, cudaStream_t st, int* grid_out) {
   switch (a.mode) {
-    case SM_FUSED: return launch_mode<T, VPT, kNarrow, SM_FUSED>(a, threads, sms, st);
-    case SM_STEP_MAX: return launch_mode<T, VPT, kNarrow, SM_STEP_MAX>(a, threads, sms, st);
-    case SM_STEP_SUM: return launch_mode<T, VPT, kNarrow, SM_STEP_SUM>(a, threads, sms, st);
-    case SM_STEP_NORM: return launch_mode<T, VPT, kNarrow, SM_STEP_NORM>(a, threads, sms, st);
+    case SM_FUSED: return launch_mode<T, VPT, kNarrow, SM_FUSED>(a, threads, sms, st, grid_out);
+    case SM_STEP_MAX: return launch_mode<T, VPT, kNarrow, SM_STEP_MAX>(a, threads, sms, st, grid_out);
+    case SM_STEP_SUM: return launch_mode<T, VPT, kNarrow, SM_STEP_SUM>(a, threads, sms, st, grid_out);
+    case SM_STEP_NORM: return launch_mode<T, VPT, kNarrow, SM_STEP_NORM>(a, threads, sms, st, grid_out);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <int T, int VPT>
-cudaError_t launch_rows(const SoftmaxArgs& a, int sms, cudaStream_t st) {
+cudaError_t launch_rows(const SoftmaxArgs& a, int sms, cudaStream_t st, int* grid_out) {
   const unsigned threads = unsigned(a.cols / 8) / VPT;
   if constexpr (VPT <= 4) {
-    if (threads == 128) return launch_split<T, VPT, true>(a, threads, sms, st);
+    if (threads == 128) return launch_split<T, VPT, true>(a, threads, sms, st, grid_out);
   }
-  return launch_split<T, VPT, false>(a, threads, sms, st);
+  return launch_split<T, VPT, false>(a, threads, sms, st, grid_out);
 }
 
 template <int T>
-cudaError_t launch_type(const SoftmaxArgs& a, int sms, cudaStream_t st) {
+cudaError_t launch_type(const SoftmaxArgs& a, int sms, cudaStream_t st, int* grid_out) {
   switch (softmax_vectors_per_thread(a.cols)) {
-    case 1: return launch_rows<T, 1>(a, sms, st);
-    case 2: return launch_rows<T, 2>(a, sms, st);
-    case 4: return launch_rows<T, 4>(a, sms, st);
-    case 8: return launch_rows<T, 8>(a, sms, st);
+    case 1: return launch_rows<T, 1>(a, sms, st, grid_out);
+    case 2: return launch_rows<T, 2>(a, sms, st, grid_out);
+    case 4: return launch_rows<T, 4>(a, sms, st, grid_out);
+    case 8: return launch_rows<T, 8>(a, sms, st, grid_out);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -277,7 +299,15 @@ int softmax_vectors_per_thread(uint64_t cols) {
 
 cudaError_t softmax_rows_launch(const SoftmaxArgs& a, int sms, cudaStream_t st) {
   if (a.rows == 0) return cudaSuccess;
-  return a.type == kF16 ? launch_type<kF16>(a, sms, st) : launch_type<kBF16>(a, sms, st);
+  return a.type == kF16 ? launch_type<kF16>(a, sms, st, nullptr) : launch_type<kBF16>(a, sms, st, nullptr);
+}
+
+int softmax_rows_grid(const SoftmaxArgs& a, int sms) {
+  int grid = 0;
+  const cudaError_t e = a.rows == 0 ? cudaErrorInvalidValue
+                        : a.type == kF16 ? launch_type<kF16>(a, sms, nullptr, &grid)
+                                         : launch_type<kBF16>(a, sms, nullptr, &grid);
+  return e == cudaSuccess && grid > 0 ? grid : 1;
 }
 
 }  // namespace askb
