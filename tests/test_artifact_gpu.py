@@ -197,21 +197,31 @@ def test_integer_and_bool_reductions(session, dtype, cols):
 @pytest.mark.parametrize("dt,rows,cols", [("f16", 64, 4096), ("bf16", 4096, 512)])
 def test_softmax_steps(session, dt, rows, cols):
     """The three softmax steps as artifacts (row max; sum of exp(cast(x) - m[row])
-    with an outer-indexed port; normalise) against the oracle."""
+    with an outer-indexed port; normalise) against the oracle, with a NaN, an
+    infinity and an all -inf row among them."""
     rng = np.random.default_rng(2)
     xf = (rng.standard_normal(rows * cols) * 3).astype(np.float32)
     x = xf.astype(np.float16).view(np.uint16) if dt == "f16" else (xf.view(np.uint32) >> 16).astype(np.uint16)
+    nan16, inf16, ninf16 = (0x7E00, 0x7C00, 0xFC00) if dt == "f16" else (0x7FC0, 0x7F80, 0xFF80)
+    x[7] = nan16
+    x[cols + 11] = inf16
+    x[2 * cols:3 * cols] = ninf16
     steps = R.cfg3_steps(dt, rows, cols)
     (m,) = run_artifact(session, steps[0], [x], ["f32"])
-    assert np.array_equal(m, oracle.reduce(steps[0], [x])[0])
+    assert same_with_nan(m, oracle.reduce(steps[0], [x])[0])
     (s,) = run_artifact(session, steps[1], [x, m], ["f32"])
     (want,) = oracle.reduce(steps[1], [x, m])
-    assert np.all(np.abs(s.astype(np.float64) - want) <= 2.0 ** -20 * np.abs(want))
+    fin = np.isfinite(want)
+    assert np.array_equal(np.isnan(s), np.isnan(want))
+    assert np.all(np.abs(s[fin].astype(np.float64) - want[fin]) <= 2.0 ** -20 * np.abs(want[fin]))
     (y,) = run_artifact(session, steps[2], [x, m, s], [dt])
     (wy,) = oracle.elementwise(steps[2], [x, m, s])
     # CUDA's expf against the host libm's exp: within one unit of the output type
     conv = f16_to_f32 if dt == "f16" else bf16_to_f32
     gyv, wyv = conv(y), conv(wy)
+    nan = np.isnan(wyv)
+    assert np.array_equal(np.isnan(gyv), nan)
+    gyv, wyv, wy = gyv[~nan], wyv[~nan], wy[~nan]
     step = np.spacing(np.abs(wyv).astype(np.float16)).astype(np.float32) if dt == "f16" else \
         np.abs(bf16_to_f32(wy + 1) - wyv)
     assert np.all(np.abs(gyv - wyv) <= step + 1e-45)
