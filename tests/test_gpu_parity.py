@@ -314,6 +314,32 @@ def test_softmax_steps_on_the_row_kernel(device, dtype, rows, cols):
     assert same_with_nan(m_row, m_warp)
 
 
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_softmax_max_and_sum_split_over_long_rows(device, dtype):
+    """Few rows of 32768: the max and sum steps take the split reduction (CTAs
+    split each row, partial records combined); rows with a NaN, an infinity,
+    all -inf and all -0 against the oracle."""
+    rows, cols = 7, 32768
+    xh = _rows_with_specials(dtype, rows, cols, 4)
+    steps = R.cfg3_steps(dtype, rows, cols)[:2]
+    plans = [ask_b200.Plan(s, 0) for s in steps]
+    assert [p.describe()["strategy"] for p in plans] == ["split", "split"]
+    x = torch.from_numpy(xh.view(np.int16)).cuda()
+    st = torch.cuda.current_stream()
+    m = torch.empty(rows, dtype=torch.float32, device="cuda")
+    s = torch.empty(rows, dtype=torch.float32, device="cuda")
+    scratch = [torch.empty(max(p.scratch_bytes, 16), dtype=torch.uint8, device="cuda") for p in plans]
+    plans[0].launch([x], [m], scratch[0], st)
+    plans[1].launch([x, m], [s], scratch[1], st)
+    torch.cuda.synchronize()
+    rm, rs, _ = oracle.softmax(dtype, xh, rows, cols, threads=THREADS)
+    gm, gs = m.cpu().numpy(), s.cpu().numpy()
+    assert same_with_nan(gm, rm)
+    assert np.array_equal(np.isnan(gs), np.isnan(rs))
+    fin = np.isfinite(rs)
+    assert np.all(np.abs(gs[fin].astype(np.float64) - rs[fin]) <= 2.0 ** -20 * np.abs(rs[fin]))
+
+
 def _rn16(q32: np.ndarray, dtype: str) -> np.ndarray:
     """f32 -> f16/bf16 bits, round to nearest even (NaN -> a quiet NaN)."""
     if dtype == "f16":
