@@ -115,6 +115,33 @@ def test_row_statistics_through_the_reference_runtime(ref, graph):
         assert np.array_equal(got[k], want[k]), k
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_softmax_steps_through_the_reference_runtime(ref, dt):
+    """The softmax plan's three steps as artifacts, each run by the reference
+    Runtime and fed the previous step's outputs; against the oracle."""
+    rows, cols = 64, 4096
+    rng = np.random.default_rng(12)
+    xf = (rng.standard_normal(rows * cols) * 3).astype(np.float32)
+    x = xf.astype(np.float16).view(np.uint16) if dt == "f16" else (xf.view(np.uint32) >> 16).astype(np.uint16)
+    x[9] = 0x7E00 if dt == "f16" else 0x7FC0  # a NaN row
+    steps = R.cfg3_steps(dt, rows, cols)
+    (m,), _ = run_reference(ref, steps[0], [x])
+    (s,), _ = run_reference(ref, steps[1], [x, m])
+    (y,), _ = run_reference(ref, steps[2], [x, m, s])
+    rm, rs, ry = oracle.softmax(dt, x, rows, cols)
+    assert same_with_nan(m, rm)
+    fin = np.isfinite(rs)
+    assert np.array_equal(np.isnan(s), np.isnan(rs))
+    assert np.all(np.abs(s[fin].astype(np.float64) - rs[fin]) <= 2.0 ** -20 * np.abs(rs[fin]))
+    conv = f16_to_f32 if dt == "f16" else bf16_to_f32
+    gyv, ryv = conv(y.view(np.uint16)), conv(ry)
+    nan = np.isnan(ryv)
+    assert np.array_equal(np.isnan(gyv), nan)
+    step = np.spacing(np.abs(ryv[~nan]).astype(np.float16)).astype(np.float32) if dt == "f16" else \
+        np.abs(bf16_to_f32(ry[~nan] + 1) - ryv[~nan])
+    assert np.all(np.abs(gyv[~nan] - ryv[~nan]) <= step + 1e-45)
+
+
 def test_gather_through_the_reference_runtime(ref):
     rng = np.random.default_rng(11)
     dim, inner, n = 500, 32, 3000
