@@ -370,7 +370,10 @@ Generated generate(const ask_b200_plan& pl, const std::string& entry, const uint
   src << "// ask_b200 kernel artifact (" << g.body << "), generated from a recipe step.\n"
       << "#include \"artifact_bodies.cuh\"\n\nnamespace {\n" << decls << "}  // namespace\n\n"
       << "extern \"C\" __global__ void __launch_bounds__(askb::art::kThreads"
-      << (g.body == "elementwise_functor" ? ", askb::art::kFunctorMinBlocks" : "") << ") " << entry << "(" << sig.str()
+      << (g.body != "elementwise_functor" ? ""
+          : pl.family == FAM_ELEMENTWISE && pl.spec == EW_CFG1 ? ", askb::art::kDeepFunctorMinBlocks"
+                                                                : ", askb::art::kFunctorMinBlocks")
+      << ") " << entry << "(" << sig.str()
       << ") {\n"
       << body.str() << "}\n";
   g.source = src.str();

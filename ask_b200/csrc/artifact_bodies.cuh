@@ -30,6 +30,9 @@ constexpr int kThreads = 256;  // block size of every artifact kernel
 // ports) from raising the whole kernel's register count and lowering its
 // occupancy.
 constexpr int kFunctorMinBlocks = 5;
+// The cfg1 functor keeps two units of loads in flight (58 registers in the
+// library): its entries are compiled for 4 resident CTAs.
+constexpr int kDeepFunctorMinBlocks = 4;
 
 __device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 __device__ __forceinline__ bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }

@@ -183,12 +183,24 @@ __device__ __forceinline__ void ew_functor_loop(const EwArgs& a, uint64_t units)
   const uint64_t stride = uint64_t(gridDim.x) * kEwThreads;
   uint64_t u = uint64_t(blockIdx.x) * kEwThreads + threadIdx.x;
   if (u >= units) return;
-  typename F::In cur = F::load(a, u), nxt;
-  for (; u < units; u += stride) {
-    const uint64_t un = u + stride;
-    if (un < units) nxt = F::load(a, un);
-    F::store(a, u, F::compute(a, cur));
-    cur = nxt;
+  if constexpr (F::kDepth == 2) {  // the units two and one strides ahead in flight
+    typename F::In cur = F::load(a, u), nxt, nxt2;
+    if (u + stride < units) nxt = F::load(a, u + stride);
+    for (; u < units; u += stride) {
+      const uint64_t u2 = u + 2 * stride;
+      if (u2 < units) nxt2 = F::load(a, u2);
+      F::store(a, u, F::compute(a, cur));
+      cur = nxt;
+      nxt = nxt2;
+    }
+  } else {
+    typename F::In cur = F::load(a, u), nxt;
+    for (; u < units; u += stride) {
+      const uint64_t un = u + stride;
+      if (un < units) nxt = F::load(a, un);
+      F::store(a, u, F::compute(a, cur));
+      cur = nxt;
+    }
   }
 }
 
@@ -199,6 +211,7 @@ __device__ __forceinline__ void ew_functor_loop(const EwArgs& a, uint64_t units)
 // units, no prefetch) and 4.07 ms for a 16-byte version of this functor.
 struct FnCfg5b {
   static constexpr int V = 8;
+  static constexpr int kDepth = 1;
   static constexpr bool kRowMapped = false;
   struct In { Vec32 x, y; };
   struct Out { Vec32 z; };
@@ -223,6 +236,9 @@ struct FnCfg5b {
 // ProgCfg1: y0 = exp(a)*b + c ; y1 = maximum(a, b) + tanh(c)*(-1), 4 elements per unit.
 struct FnCfg1 {
   static constexpr int V = 4;
+  // loads two units ahead: 57.6 against 59.7 us on cfg1 with one (same box;
+  // 58 registers, 4 CTAs an SM instead of 5, twice the bytes in flight)
+  static constexpr int kDepth = 2;
   static constexpr bool kRowMapped = false;
   struct In { uint4 a, b, c; };
   struct Out { float y0[4], y1[4]; };
@@ -272,6 +288,7 @@ struct FnCfg1 {
 template <int T>
 struct FnSoftmaxNorm {
   static constexpr int V = 8;
+  static constexpr int kDepth = 1;
   static constexpr bool kRowMapped = true;  // m, s are indexed by unit*8 / inner
   struct In { uint4 x; float nm, s, y; };
   using Out = uint4;

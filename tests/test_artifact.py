@@ -67,7 +67,10 @@ def test_generated_sources_compile_for_sm100a(name):
     assert gen["body"] == body
     assert gen["launch"] == {"grid": [592, 1, 1], "block": [256, 1, 1], "shared_bytes": 0}
     assert gen["parameter_widths"] == [0] * (len(params) - 2) + [4, 8]
-    bounds = "askb::art::kThreads, askb::art::kFunctorMinBlocks" if body == "elementwise_functor" else "askb::art::kThreads"
+    # functor entries are compiled for the functor's occupancy (the cfg1 functor keeps two units in flight)
+    bounds = "askb::art::kThreads" if body != "elementwise_functor" else \
+        "askb::art::kThreads, askb::art::kDeepFunctorMinBlocks" if name == "cfg1" else \
+        "askb::art::kThreads, askb::art::kFunctorMinBlocks"
     assert f'extern "C" __global__ void __launch_bounds__({bounds}) k_{name}(' in gen["source"]
     cubin = A.compile_source(gen["source"])
     assert cubin[:4] == b"\x7fELF"
