@@ -518,6 +518,7 @@ def measure(w, args, torch, barrier, dist, local):
     # A step of one plan is timed by the region's two events alone; a step of
     # several plans also records an event after each plan for per-plan times.
     start.record(st)
+    h0 = time.perf_counter()
     for s in range(args.steps):
         if nk > 1:
             ev[s][0].record(st)
@@ -525,6 +526,7 @@ def measure(w, args, torch, barrier, dist, local):
             fn()
             if nk > 1:
                 ev[s][k + 1].record(st)
+    h1 = time.perf_counter()
     end.record(st)
     barrier()
     clocks = sampler.stop()
@@ -550,9 +552,13 @@ def measure(w, args, torch, barrier, dist, local):
                 "kernel": kernels[dom]["kernel"],
                 "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                 else "fallback 6.65 TB/s"}
+    # host time to enqueue one step through the public API (Python -> C ABI
+    # launch, or a runtime program's graph launch); the GPU runs behind it
+    host_us = 1e6 * (h1 - h0) / args.steps
     return {"value": round(w.global_bytes / (ms_per_step * 1e-3) / 1e9, 1), "ms_per_step": round(ms_per_step, 4),
             "roofline": roofline, "kernels": kernels, "clocks": clocks,
-            "gpu_launches": w.launches_per_step() * args.steps}
+            "gpu_launches": w.launches_per_step() * args.steps,
+            "host_enqueue_us_per_step": round(host_us, 1)}
 
 
 def exchange_timing(w, args, torch, barrier, dist):
@@ -875,7 +881,7 @@ def main():
             "kernels": head["kernels"], "cpu_baseline": head.get("cpu_baseline"), "e2e": head.get("e2e"),
             "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
             "pct_of_8tbs": round(100.0 * head["value"] / world / 8000.0, 2)}
-    for key in ("check", "exchange", "plan_port_gbs"):
+    for key in ("check", "exchange", "plan_port_gbs", "host_enqueue_us_per_step"):
         if key in head:
             line[key] = head[key]
     if per_config is not None:
