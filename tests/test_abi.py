@@ -82,8 +82,10 @@ def test_config_recipes_select_specialised_kernels(name, recipe, kernel):
 def test_softmax_partition_steps(dtype):
     kernels = [host_plan(s).describe()["kernel"] for s in R.cfg3_steps(dtype)]
     assert kernels == [f"softmax_rows_max_{dtype}", f"softmax_rows_sum_{dtype}", f"softmax_rows_norm_{dtype}"]
-    capped = dict(R.cfg3_steps(dtype)[2], blocks_per_sm=4)  # a grid cap keeps the elementwise functor
-    assert host_plan(capped).describe()["kernel"] == f"ew_softmax_norm_{dtype}"
+    # a grid cap keeps the warp-row reductions and the elementwise functor
+    capped = [host_plan(dict(s, blocks_per_sm=4)).describe()["kernel"] for s in R.cfg3_steps(dtype)]
+    assert capped == [f"reduce_warp_row_softmax_max_{dtype}", f"reduce_warp_row_softmax_sum_{dtype}",
+                      f"ew_softmax_norm_{dtype}"]
     d = host_plan(R.cfg3_steps(dtype)[1]).describe()
     assert d["strategy"] == "row_cta" and d["launch"]["block"] == [128, 1, 1]
     # a forced strategy, or rows the row kernel does not take, keep the warp-row reduction
