@@ -54,10 +54,17 @@ constexpr int kMaxWarps = 16;
 constexpr int kPreferThreads = ASKB_SOFTMAX_THREADS;  // CTA size the row split aims for
 
 // Rows split into 128-thread CTAs with up to 4 vectors a thread (4096-element
-// rows) are compiled for 8 CTAs per SM, 64 registers a thread, without
-// spilling (same-box A/B on cfg3 with the scalar arithmetic: 0.111 ms against
-// 0.123 ms at 4 CTAs per SM); other splits keep the full register budget
-// (VPT == 8 would spill at 64).
+// rows) are compiled for a number of resident CTAs per SM chosen per mode by
+// measurement (same box, [32768, 4096] f16, CUDA events): the fused kernel for
+// 6 (80 registers a thread: 90.2 us against 98.3 at 8 CTAs of 64 registers,
+// 94.3 at 7 and 90.2-92.2 at 5), the normalise step for 5 (88.3 us against
+// 94.3 at 8 and 90.2 at 6), the max and sum steps for 8 (the sum step 65.6 us
+// against 66.6 at 6; the max step needs 40 registers).  Other splits keep the
+// full register budget (VPT == 8 would spill at 64).
+template <int kMode>
+constexpr int narrow_ctas_per_sm() {
+  return kMode == SM_FUSED ? 6 : kMode == SM_STEP_NORM ? 5 : 8;
+}
 //
 // kMode selects what the row kernel computes (SoftmaxMode): SM_FUSED the
 // three steps; SM_STEP_MAX the first step alone (m); SM_STEP_SUM the second
@@ -68,7 +75,7 @@ constexpr int kPreferThreads = ASKB_SOFTMAX_THREADS;  // CTA size the row split 
 // every product e * RN(1/s) is a normal f32; otherwise expf and the IEEE
 // division, the normalise step's own scalar arithmetic).
 template <int T, int VPT, bool kNarrow, int kMode>
-__global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? 8 : 1)
+__global__ void __launch_bounds__(kNarrow ? 128 : kMaxWarps * 32, kNarrow ? narrow_ctas_per_sm<kMode>() : 1)
     softmax_rows_kernel(const uint4* __restrict__ x, float* __restrict__ m_out, float* __restrict__ s_out,
                         uint4* __restrict__ y, const float* __restrict__ m_in, const float* __restrict__ s_in,
                         uint64_t rows, uint32_t vecs) {
